@@ -1,0 +1,765 @@
+// C ABI of libkernrelay.so: the reference's six entry points (kernrelay.h) and
+// the B200 extensions (kernrelay_b200.h).  No C++ exception crosses the ABI.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <condition_variable>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "common.h"
+#include "json_min.hpp"
+#include "kernrelay.h"
+#include "kernrelay_b200.h"
+#include "model.h"
+#include "ptx.cuh"
+#include "synth.cuh"
+
+#define KRB_EXPORT extern "C" __attribute__((visibility("default")))
+
+using Clock = std::chrono::steady_clock;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+double us_between(Clock::time_point a, Clock::time_point b) {
+  return std::chrono::duration<double, std::micro>(b - a).count();
+}
+
+int fail(const std::exception &e) {
+  g_last_error = e.what();
+  return 1;
+}
+
+int write_out(const std::string &res, char *out, size_t cap) {
+  if (!out || cap < res.size() + 1) throw std::runtime_error("output buffer too small");
+  std::memcpy(out, res.c_str(), res.size() + 1);
+  return 0;
+}
+
+int write_error(const std::string &what, char *out, size_t cap) {
+  g_last_error = what;
+  if (out && cap) {
+    const std::string msg = "{\"error\":\"" + krb::json::escape(what) + "\"}";
+    std::snprintf(out, cap, "%s", msg.c_str());
+  }
+  return 1;
+}
+
+cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+std::string fmt(double v) {
+  char b[64];
+  std::snprintf(b, sizeof(b), "%.3f", v);
+  return b;
+}
+
+void stats(const std::vector<double> &s, double *best, double *typ) {
+  std::vector<double> v = s;
+  std::sort(v.begin(), v.end());
+  *best = v.empty() ? 0 : v.front();
+  *typ = v.empty() ? 0 : v[v.size() / 2];
+}
+
+std::string samples_json(const std::vector<double> &s) {
+  std::string o = "[";
+  for (size_t i = 0; i < s.size(); ++i) {
+    if (i) o += ",";
+    o += fmt(s[i]);
+  }
+  return o + "]";
+}
+
+int popcount_status(uint32_t st) {
+  int n = 0;
+  for (uint32_t b = krb::kStatusRsWait; b <= krb::kStatusFlagWait; b <<= 1)
+    if (st & b) ++n;
+  return n;
+}
+
+// Result JSON of one engine, same fields as the reference's ResultJson
+// (qwen_main.cpp:1785-1803) plus B200 extras.
+std::string stage_json(krb::Engine &e, const std::string &mode, int warmup, int iters,
+                       const std::vector<double> &samples, const std::vector<double> &host,
+                       const krb::Engine::Verdict &v, uint32_t status, int flag_edges) {
+  double best, typ, hb, ht;
+  stats(samples, &best, &typ);
+  stats(host, &hb, &ht);
+  std::ostringstream os;
+  os << "{\"mode\":\"" << mode << "\",\"seq\":" << e.cfg().seq << ",\"device\":" << e.device()
+     << ",\"warmup\":" << warmup << ",\"iters\":" << iters << ",\"best_us\":" << fmt(best)
+     << ",\"typical_us\":" << fmt(typ) << ",\"samples_us\":" << samples_json(samples)
+     << ",\"argmax\":" << v.argmax << ",\"ref_argmax\":" << v.ref_argmax
+     << ",\"maxdiff\":" << v.maxdiff << ",\"abs_mean\":" << v.abs_mean
+     << ",\"flag_edges\":" << flag_edges << ",\"flag_timeouts\":" << popcount_status(status)
+     << ",\"host_best_us\":" << fmt(hb) << ",\"host_typical_us\":" << fmt(ht)
+     << ",\"status\":" << status << ",\"rank\":" << e.rank() << ",\"world\":" << e.world()
+     << ",\"has_ref\":" << (v.has_ref ? "true" : "false") << "}";
+  return os.str();
+}
+
+class Barrier {
+ public:
+  explicit Barrier(int n) : n_(n) {}
+  void wait() {
+    std::unique_lock<std::mutex> lk(m_);
+    const int gen = gen_;
+    if (++count_ == n_) {
+      count_ = 0;
+      ++gen_;
+      cv_.notify_all();
+    } else {
+      cv_.wait(lk, [&] { return gen_ != gen; });
+    }
+  }
+
+ private:
+  std::mutex m_;
+  std::condition_variable cv_;
+  int n_, count_ = 0, gen_ = 0;
+};
+
+}  // namespace
+
+// =================================================================== reference ABI
+KRB_EXPORT const char *kr_version(void) { return "KernRelay 0.3 (libkernrelay, B200 sm_100a)"; }
+
+KRB_EXPORT int kr_plan_run(const char *schedule_json, int iters, int warmup, const char *devices,
+                           const char *mode, const char *out_json) {
+  if (!schedule_json || !out_json) return 2;  // kr_api.cpp:27
+  (void)iters;
+  (void)warmup;
+  (void)devices;
+  std::string err;
+  try {
+    const std::string m = mode ? mode : "direct";
+    if (m != "direct" && m != "graph" && m != "graph_per_stream" && m != "graph_segment")
+      throw std::runtime_error("unknown plan mode " + m);
+    krb::json::Value doc = krb::json::parse_file(schedule_json);
+    (void)doc;
+    err = "plan executor not built in the B200 library (TP-MLP prefill path only)";
+  } catch (const std::exception &e) {
+    err = e.what();
+  }
+  std::ofstream f(out_json);
+  f << "{\"error\":\"" << krb::json::escape(err) << "\"}\n";
+  g_last_error = err;
+  return 3;
+}
+
+KRB_EXPORT int kr_qwen_run(const char *model_dir, const char *mode, int seq, int device,
+                           int warmup, int iters, char *out, size_t out_cap) {
+  try {
+    if (!model_dir || !*model_dir) throw std::runtime_error("model path required");
+    krb::EngineOpts o;
+    o.model_dir = model_dir;
+    o.mode = mode ? mode : "serial_graph";
+    o.seq = seq;
+    o.device = device;
+    o.tiles = 4;
+    if (const char *t = std::getenv("KR_TILES")) o.tiles = std::max(1, std::atoi(t));
+    krb::Engine e(o);
+    if (e.mode().tp) throw std::runtime_error("use kr_qwen_tp_run for tp modes");
+    e.run();
+    e.sync();
+    krb::Engine::Verdict v = e.verify();
+    if (e.mode().graph) e.capture_graph();
+    for (int i = 0; i < warmup; ++i) {
+      e.run();
+      e.sync();
+    }
+    std::vector<double> samples, host;
+    for (int i = 0; i < std::max(1, iters); ++i) {
+      e.sync();
+      const auto t0 = Clock::now();
+      e.run();
+      const auto th = Clock::now();
+      e.sync();
+      const auto t1 = Clock::now();
+      samples.push_back(us_between(t0, t1));
+      host.push_back(us_between(t0, th));
+    }
+    v = e.verify();  // after replays, re-check numerics (qwen_main.cpp:2168)
+    const uint32_t st = e.read_status();
+    if (st) throw std::runtime_error("device status " + std::to_string(st));
+    return write_out(stage_json(e, o.mode, warmup, iters, samples, host, v, st,
+                                e.mode().split ? e.cfg().L * o.tiles : 0),
+                     out, out_cap);
+  } catch (const std::exception &ex) {
+    return write_error(ex.what(), out, out_cap);
+  }
+}
+
+KRB_EXPORT int kr_qwen_pp_run(const char *model_dir, const char *mode, int seq, int dev0,
+                              int dev1, int requests, int warmup, int iters, char *out,
+                              size_t out_cap) {
+  (void)model_dir;
+  (void)mode;
+  (void)seq;
+  (void)dev0;
+  (void)dev1;
+  (void)requests;
+  (void)warmup;
+  (void)iters;
+  return write_error("pp modes are not built in the B200 library", out, out_cap);
+}
+
+namespace {
+
+std::vector<int> tp_devices(int k, int dev0, int dev1) {
+  std::vector<int> d;
+  if (const char *e = std::getenv("KR_TP_DEVICES")) {
+    std::stringstream ss(e);
+    std::string tok;
+    while (std::getline(ss, tok, ','))
+      if (!tok.empty()) d.push_back(std::atoi(tok.c_str()));
+    if (int(d.size()) < k) throw std::runtime_error("KR_TP_DEVICES lists fewer devices than k");
+    d.resize(k);
+  } else if (k == 2) {
+    if (dev1 < 0 || dev1 == dev0) throw std::runtime_error("--device2 must be a different device");
+    d = {dev0, dev1};
+  } else {
+    for (int i = 0; i < k; ++i) d.push_back(dev0 + i);
+  }
+  for (size_t i = 0; i < d.size(); ++i)
+    for (size_t j = i + 1; j < d.size(); ++j)
+      if (d[i] == d[j]) throw std::runtime_error("tp devices must be distinct");
+  return d;
+}
+
+}  // namespace
+
+KRB_EXPORT int kr_qwen_tp_run(const char *model_dir, const char *mode, int seq, int dev0,
+                              int dev1, int tiles, int warmup, int iters, char *out,
+                              size_t out_cap) {
+  try {
+    if (!model_dir || !*model_dir) throw std::runtime_error("model path required");
+    const std::string mname = mode ? mode : "tp2";
+    const krb::Mode m = krb::Mode::parse(mname);
+    if (!m.tp) throw std::runtime_error("kr_qwen_tp_run needs a tp mode");
+    if (tiles < 1 || tiles > 8) throw std::runtime_error("--tiles must be in 1..8");
+    const int k = m.world;
+    const int t_eff = m.split ? tiles : 1;
+    const std::vector<int> devs = tp_devices(k, dev0, dev1);
+    int ndev = 0;
+    KRB_CUDA(cudaGetDeviceCount(&ndev));
+    for (int d : devs)
+      if (d < 0 || d >= ndev) throw std::runtime_error("device " + std::to_string(d) + " not present");
+    // peer access between all pairs (NVLink/NVSwitch)
+    if (m.split && k > 1) {
+      for (int i : devs)
+        for (int j : devs) {
+          if (i == j) continue;
+          int can = 0;
+          KRB_CUDA(cudaDeviceCanAccessPeer(&can, i, j));
+          if (!can) throw std::runtime_error("no peer access between devices");
+          KRB_CUDA(cudaSetDevice(i));
+          cudaError_t r = cudaDeviceEnablePeerAccess(j, 0);
+          if (r == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+          else KRB_CUDA(r);
+        }
+    }
+    // build the engines in parallel (weight load dominates)
+    std::vector<std::unique_ptr<krb::Engine>> eng(k);
+    std::vector<std::string> errs(k);
+    {
+      std::vector<std::thread> th;
+      for (int r = 0; r < k; ++r)
+        th.emplace_back([&, r] {
+          try {
+            krb::EngineOpts o;
+            o.model_dir = model_dir;
+            o.mode = mname;
+            o.seq = seq;
+            o.rank = r;
+            o.world = k;
+            o.device = devs[r];
+            o.tiles = t_eff;
+            eng[r] = std::make_unique<krb::Engine>(o);
+          } catch (const std::exception &ex) {
+            errs[r] = ex.what();
+          }
+        });
+      for (auto &t : th) t.join();
+      for (int r = 0; r < k; ++r)
+        if (!errs[r].empty()) throw std::runtime_error("rank" + std::to_string(r) + ": " + errs[r]);
+    }
+    std::vector<ncclComm_t> comms(k, nullptr);
+    if (m.split) {
+      std::vector<void *> bases(k);
+      for (int r = 0; r < k; ++r) bases[r] = eng[r]->sym_base();
+      for (int r = 0; r < k; ++r) eng[r]->set_peers(bases);
+    } else if (k > 1) {
+      if (ncclCommInitAll(comms.data(), k, devs.data()) != ncclSuccess)
+        throw std::runtime_error("ncclCommInitAll failed");
+      for (int r = 0; r < k; ++r) eng[r]->set_nccl(comms[r]);
+    }
+    Barrier bar(k + 1);
+    std::mutex mu;
+    std::string err;
+    std::vector<std::string> stage(k);
+    std::vector<double> wall;
+    auto worker = [&](int r) {
+      krb::Engine &e = *eng[r];
+      bool ok = true;
+      auto guard = [&](auto fn) {
+        if (!ok) return;
+        try {
+          fn();
+        } catch (const std::exception &ex) {
+          ok = false;
+          std::lock_guard<std::mutex> lk(mu);
+          if (err.empty()) err = "rank" + std::to_string(r) + ": " + ex.what();
+        }
+      };
+      krb::Engine::Verdict v;
+      guard([&] {
+        KRB_CUDA(cudaSetDevice(e.device()));
+        e.run();
+        e.sync();
+        v = e.verify();
+        if (e.mode().graph) e.capture_graph();
+      });
+      bar.wait();
+      for (int w = 0; w < warmup; ++w) {
+        bar.wait();
+        guard([&] {
+          e.run();
+          e.sync();
+        });
+        bar.wait();
+      }
+      std::vector<double> samples;
+      for (int i = 0; i < std::max(1, iters); ++i) {
+        bar.wait();
+        const auto t0 = Clock::now();
+        guard([&] {
+          e.run();
+          e.sync();
+        });
+        samples.push_back(us_between(t0, Clock::now()));
+        bar.wait();
+      }
+      guard([&] {
+        v = e.verify();
+        const uint32_t st = e.read_status();
+        if (st) throw std::runtime_error("device status " + std::to_string(st));
+        stage[r] = stage_json(e, "tp_rank" + std::to_string(r), warmup, iters, samples, {}, v, st,
+                              e.mode().split ? e.cfg().L * t_eff : 0);
+      });
+      bar.wait();
+    };
+    std::vector<std::thread> th;
+    for (int r = 0; r < k; ++r) th.emplace_back(worker, r);
+    bar.wait();  // first run + verify done
+    for (int w = 0; w < warmup; ++w) {
+      bar.wait();
+      bar.wait();
+    }
+    for (int i = 0; i < std::max(1, iters); ++i) {
+      bar.wait();
+      const auto t0 = Clock::now();
+      bar.wait();
+      wall.push_back(us_between(t0, Clock::now()));
+    }
+    bar.wait();
+    for (auto &t : th) t.join();
+    for (int r = 0; r < k; ++r) {
+      if (comms[r]) ncclCommDestroy(comms[r]);
+    }
+    eng.clear();
+    if (!err.empty()) throw std::runtime_error(err);
+    double best, typ;
+    stats(wall, &best, &typ);
+    std::ostringstream os;
+    os << "{\"mode\":\"" << mname << "\",\"seq\":" << seq << ",\"tiles\":" << t_eff << ",\"k\":" << k
+       << ",\"devices\":[";
+    for (int r = 0; r < k; ++r) os << (r ? "," : "") << devs[r];
+    os << "],\"wall_best_us\":" << fmt(best) << ",\"wall_typical_us\":" << fmt(typ)
+       << ",\"wall_samples_us\":" << samples_json(wall) << ",\"stages\":[";
+    for (int r = 0; r < k; ++r) os << (r ? "," : "") << stage[r];
+    os << "]}";
+    return write_out(os.str(), out, out_cap);
+  } catch (const std::exception &ex) {
+    return write_error(ex.what(), out, out_cap);
+  }
+}
+
+
+// =================================================================== B200 extensions
+KRB_EXPORT const char *krb_last_error(void) { return g_last_error.c_str(); }
+
+KRB_EXPORT int krb_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+KRB_EXPORT int krb_synth_normal_host(const char *name, uint64_t seed, double std_, uint64_t offset,
+                                     uint64_t n, uint16_t *out) {
+  try {
+    if (!name || !out) throw std::runtime_error("null argument");
+    const uint64_t key = krb::synth_key(name, seed);
+    const double scale = krb::synth_scale(std_);
+    const unsigned nt = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    std::vector<std::thread> th;
+    for (unsigned t = 0; t < nt; ++t)
+      th.emplace_back([=] {
+        const uint64_t lo = n * t / nt, hi = n * (t + 1) / nt;
+        for (uint64_t i = lo; i < hi; ++i) out[i] = krb::synth_normal_bf16(key, offset + i, scale);
+      });
+    for (auto &x : th) x.join();
+    return 0;
+  } catch (const std::exception &e) {
+    return fail(e);
+  }
+}
+
+#define KRB_OP_BEGIN try {
+#define KRB_OP_END      \
+  return 0;             \
+  }                     \
+  catch (const std::exception &e) { return fail(e); }
+
+using bf = __nv_bfloat16;
+
+KRB_EXPORT int krb_gemm_bf16(const void *A, long lda, const void *B, long ldb, void *C, long ldc,
+                             const void *bias, int M, int N, int K, int bn, void *stream) {
+  KRB_OP_BEGIN
+  krb::gemm_bf16(static_cast<const bf *>(A), lda, static_cast<const bf *>(B), ldb,
+                 static_cast<bf *>(C), ldc, static_cast<const bf *>(bias), M, N, K, bn, 0, nullptr,
+                 as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_gemm_silu_bf16(const void *A, long lda, const void *Bgu, long ldb, void *act,
+                                  long ldact, int M, int n_out, int K, int bn, void *stream) {
+  KRB_OP_BEGIN
+  if (bn != 128 && bn != 256) throw std::runtime_error("gemm_silu: bn must be 128 or 256");
+  krb::gemm_silu_bf16(static_cast<const bf *>(A), lda, static_cast<const bf *>(Bgu), ldb,
+                      static_cast<bf *>(act), ldact, M, n_out, K, bn, 0, nullptr, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_rmsnorm_bf16(const void *x, const void *gamma, void *y, float *rstd, int rows,
+                                int H, float eps, void *stream) {
+  KRB_OP_BEGIN
+  krb::rmsnorm_bf16(static_cast<const bf *>(x), static_cast<const bf *>(gamma), static_cast<bf *>(y),
+                    rstd, rows, H, eps, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_add_rmsnorm_bf16(const void *a, const void *b, const void *gamma, void *y,
+                                    float *rstd, void *sum, int rows, int H, float eps,
+                                    void *stream) {
+  KRB_OP_BEGIN
+  krb::add_rmsnorm_bf16(static_cast<const bf *>(a), static_cast<const bf *>(b),
+                        static_cast<const bf *>(gamma), static_cast<bf *>(y), rstd,
+                        static_cast<bf *>(sum), rows, H, eps, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_embed_bf16(const int64_t *ids, const void *table, void *out, int S, int H, int V,
+                              uint32_t *status, void *stream) {
+  KRB_OP_BEGIN
+  krb::embed_bf16(ids, static_cast<const bf *>(table), static_cast<bf *>(out), S, H, V, status,
+                  as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_qk_norm_rope_bf16(void *qkv, int S, int HQ, int HKV, int D, const void *cos_tab,
+                                     const void *sin_tab, const void *q_norm, const void *k_norm,
+                                     float eps, void *stream) {
+  KRB_OP_BEGIN
+  krb::qk_norm_rope_bf16(static_cast<bf *>(qkv), S, HQ, HKV, D, static_cast<const bf *>(cos_tab),
+                         static_cast<const bf *>(sin_tab), static_cast<const bf *>(q_norm),
+                         static_cast<const bf *>(k_norm), eps, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HKV, int D,
+                                          float scale, void *stream) {
+  KRB_OP_BEGIN
+  krb::attention_prefill_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(out), S, HQ, HKV, D,
+                              scale, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const void *resid,
+                                     const void *gamma, void *sum_out, void *x_out, int S, int H,
+                                     int K, int tiles, float eps, int bn, uint32_t *status,
+                                     void *stream) {
+  void *scratch = nullptr;
+  try {
+    if (tiles < 1 || S % tiles) throw std::runtime_error("relay: S % tiles != 0");
+    const int dev_bn = bn > 0 ? bn : 256;
+    krb::SymLayout L = krb::SymLayout::make(S, H, tiles, 1);
+    cudaStream_t s = as_stream(stream);
+    KRB_CUDA(cudaMalloc(&scratch, L.bytes));
+    KRB_CUDA(cudaMemsetAsync(scratch, 0, L.bytes, s));
+    // epoch = 1 for this single run
+    krb::bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(scratch) + L.epoch()), s);
+    krb::RelayArgs ra{};
+    ra.S = S;
+    ra.H = H;
+    ra.K = K;
+    ra.T = tiles;
+    ra.k = 1;
+    ra.rank = 0;
+    ra.R = S / tiles;
+    ra.Rk = ra.R;
+    krb::relay_expectations(S, H, tiles, 1, 0, dev_bn, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.peer_base[0] = static_cast<uint8_t *>(scratch);
+    ra.local_base = static_cast<uint8_t *>(scratch);
+    ra.rs_off = L.rs_off;
+    ra.ag_off = L.ag_off;
+    ra.flag_off = L.flag_off;
+    ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(scratch) + L.epoch());
+    ra.layer = 0;
+    ra.L = 1;
+    ra.resid = static_cast<const bf *>(resid);
+    ra.gamma = static_cast<const bf *>(gamma);
+    ra.sum_out = static_cast<bf *>(sum_out);
+    ra.x_out = static_cast<bf *>(x_out);
+    ra.eps = eps;
+    ra.do_norm = 1;
+    ra.timeout_ns = 2000000000ull;
+    ra.status = status;
+    krb::relay_down_layer(static_cast<const bf *>(act), K, static_cast<const bf *>(w_down), K, dev_bn,
+                          ra, s);
+    KRB_CUDA(cudaStreamSynchronize(s));
+    KRB_CUDA(cudaFree(scratch));
+    return 0;
+  } catch (const std::exception &e) {
+    if (scratch) {
+      cudaDeviceSynchronize();
+      cudaFree(scratch);
+    }
+    return fail(e);
+  }
+}
+
+// ---------------------------------------------------------------- per-rank engine
+struct krb_engine {
+  std::unique_ptr<krb::Engine> e;
+  std::vector<void *> opened;  // IPC-mapped peer regions
+  ncclComm_t comm = nullptr;
+};
+
+KRB_EXPORT int krb_engine_create(const char *model_dir, const char *mode, int seq, int rank,
+                                 int world, int device, int tiles, krb_engine **out) {
+  try {
+    if (!model_dir || !mode || !out) throw std::runtime_error("null argument");
+    krb::EngineOpts o;
+    o.model_dir = model_dir;
+    o.mode = mode;
+    o.seq = seq;
+    o.rank = rank;
+    o.world = world;
+    o.device = device;
+    o.tiles = tiles;
+    auto *h = new krb_engine();
+    try {
+      h->e = std::make_unique<krb::Engine>(o);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+    return 0;
+  } catch (const std::exception &e) {
+    return fail(e);
+  }
+}
+
+KRB_EXPORT void krb_engine_destroy(krb_engine *h) {
+  if (!h) return;
+  if (h->e) cudaSetDevice(h->e->device());
+  if (h->e) cudaStreamSynchronize(h->e->stream());
+  for (void *p : h->opened)
+    if (p) cudaIpcCloseMemHandle(p);
+  if (h->comm) ncclCommDestroy(h->comm);
+  h->e.reset();
+  delete h;
+}
+
+KRB_EXPORT int krb_engine_ipc_handle(krb_engine *h, void *handle_out, size_t cap) {
+  KRB_OP_BEGIN
+  if (!h || !handle_out || cap < sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("bad argument");
+  if (!h->e->sym_base()) throw std::runtime_error("engine has no relay region (not a split mode)");
+  KRB_CUDA(cudaSetDevice(h->e->device()));
+  cudaIpcMemHandle_t ipc;
+  KRB_CUDA(cudaIpcGetMemHandle(&ipc, h->e->sym_base()));
+  std::memcpy(handle_out, &ipc, sizeof(ipc));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_open_peers(krb_engine *h, const void *handles, size_t bytes) {
+  KRB_OP_BEGIN
+  if (!h || !handles) throw std::runtime_error("bad argument");
+  const int k = h->e->world();
+  if (bytes < size_t(k) * sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("handle buffer too small");
+  KRB_CUDA(cudaSetDevice(h->e->device()));
+  std::vector<void *> bases(k, nullptr);
+  for (int r = 0; r < k; ++r) {
+    if (r == h->e->rank()) {
+      bases[r] = h->e->sym_base();
+      continue;
+    }
+    cudaIpcMemHandle_t ipc;
+    std::memcpy(&ipc, static_cast<const char *>(handles) + size_t(r) * sizeof(ipc), sizeof(ipc));
+    void *p = nullptr;
+    KRB_CUDA(cudaIpcOpenMemHandle(&p, ipc, cudaIpcMemLazyEnablePeerAccess));
+    h->opened.push_back(p);
+    bases[r] = p;
+  }
+  h->e->set_peers(bases);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_nccl_unique_id(void *out, size_t cap) {
+  KRB_OP_BEGIN
+  if (!out || cap < sizeof(ncclUniqueId)) throw std::runtime_error("buffer too small");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) throw std::runtime_error("ncclGetUniqueId failed");
+  std::memcpy(out, &id, sizeof(id));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_init_nccl(krb_engine *h, const void *id, size_t bytes) {
+  KRB_OP_BEGIN
+  if (!h || !id || bytes < sizeof(ncclUniqueId)) throw std::runtime_error("bad argument");
+  KRB_CUDA(cudaSetDevice(h->e->device()));
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = ncclCommInitRank(&h->comm, h->e->world(), uid, h->e->rank());
+  if (r != ncclSuccess) throw std::runtime_error(std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+  h->e->set_nccl(h->comm);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_capture(krb_engine *h) {
+  KRB_OP_BEGIN
+  h->e->capture_graph();
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_run(krb_engine *h) {
+  KRB_OP_BEGIN
+  h->e->run();
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_run_host(krb_engine *h, const int64_t *ids_host, float *logits_host) {
+  KRB_OP_BEGIN
+  h->e->enqueue_host(ids_host, logits_host);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_sync(krb_engine *h) {
+  KRB_OP_BEGIN
+  h->e->sync();
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_stream(krb_engine *h, void **stream_out) {
+  KRB_OP_BEGIN
+  *stream_out = reinterpret_cast<void *>(h->e->stream());
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_status(krb_engine *h, uint32_t *status_out) {
+  KRB_OP_BEGIN
+  *status_out = h->e->read_status();
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_stage_times(krb_engine *h, char *out, size_t cap) {
+  try {
+    krb::StageTimes st = h->e->instrumented_run();
+    std::ostringstream os;
+    os << "{\"stage_us\":{\"embed\":" << fmt(st.embed) << ",\"qkv\":" << fmt(st.qkv)
+       << ",\"rope\":" << fmt(st.rope) << ",\"attention\":" << fmt(st.attn) << ",\"o\":" << fmt(st.o)
+       << ",\"addnorm\":" << fmt(st.addnorm) << ",\"gateup\":" << fmt(st.gateup)
+       << ",\"down\":" << fmt(st.down) << ",\"allreduce\":" << fmt(st.allreduce)
+       << ",\"addnorm2\":" << fmt(st.addnorm2) << ",\"relay\":" << fmt(st.relay)
+       << ",\"lm_head\":" << fmt(st.lm_head) << "},\"total_us\":" << fmt(st.total) << "}";
+    return write_out(os.str(), out, cap);
+  } catch (const std::exception &e) {
+    return write_error(e.what(), out, cap);
+  }
+}
+
+KRB_EXPORT int krb_engine_verify(krb_engine *h, char *out, size_t cap) {
+  try {
+    krb::Engine::Verdict v = h->e->verify();
+    std::ostringstream os;
+    os << "{\"argmax\":" << v.argmax << ",\"ref_argmax\":" << v.ref_argmax << ",\"maxdiff\":" << v.maxdiff
+       << ",\"abs_mean\":" << v.abs_mean << ",\"has_ref\":" << (v.has_ref ? "true" : "false") << "}";
+    return write_out(os.str(), out, cap);
+  } catch (const std::exception &e) {
+    return write_error(e.what(), out, cap);
+  }
+}
+
+KRB_EXPORT int krb_engine_last_logits(krb_engine *h, float *out, int n) {
+  KRB_OP_BEGIN
+  std::vector<float> v = h->e->last_logits();
+  if (v.empty()) throw std::runtime_error("this rank produces no logits");
+  if (n < int(v.size())) throw std::runtime_error("buffer too small");
+  std::memcpy(out, v.data(), v.size() * 4);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_final_hidden(krb_engine *h, uint16_t *out, size_t n) {
+  KRB_OP_BEGIN
+  const krb::ModelCfg &c = h->e->cfg();
+  const size_t need = size_t(c.seq) * c.H;
+  if (n < need) throw std::runtime_error("buffer too small");
+  KRB_CUDA(cudaSetDevice(h->e->device()));
+  KRB_CUDA(cudaStreamSynchronize(h->e->stream()));
+  KRB_CUDA(cudaMemcpy(out, h->e->hidden_ptr(), need * 2, cudaMemcpyDeviceToHost));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_info(krb_engine *h, char *out, size_t cap) {
+  try {
+    const krb::ModelCfg &c = h->e->cfg();
+    std::ostringstream os;
+    os << "{\"H\":" << c.H << ",\"I\":" << c.I << ",\"L\":" << c.L << ",\"HQ\":" << c.HQ
+       << ",\"HKV\":" << c.HKV << ",\"D\":" << c.D << ",\"V\":" << c.V << ",\"seq\":" << c.seq
+       << ",\"world\":" << h->e->world() << ",\"rank\":" << h->e->rank()
+       << ",\"lm_rows\":" << h->e->lm_rows() << ",\"split\":" << (h->e->mode().split ? "true" : "false")
+       << ",\"device\":" << h->e->device() << "}";
+    return write_out(os.str(), out, cap);
+  } catch (const std::exception &e) {
+    return write_error(e.what(), out, cap);
+  }
+}
+
+KRB_EXPORT int krb_engine_layer_dump(krb_engine *h, int on) {
+  KRB_OP_BEGIN
+  h->e->set_layer_dump(on != 0);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_layer_hidden(krb_engine *h, int layer, uint16_t *out, size_t n) {
+  KRB_OP_BEGIN
+  std::vector<uint16_t> v = h->e->layer_hidden(layer);
+  if (n < v.size()) throw std::runtime_error("buffer too small");
+  std::memcpy(out, v.data(), v.size() * 2);
+  KRB_OP_END
+}

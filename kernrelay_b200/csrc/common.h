@@ -1,0 +1,77 @@
+// Host-side helpers shared by every translation unit of libkernrelay.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace krb {
+
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+inline void check_cuda(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    throw CudaError(std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                    cudaGetErrorString(e) + ")");
+  }
+}
+
+#define KRB_CUDA(call) ::krb::check_cuda((call), #call)
+
+int sm_count(int device);
+
+// 2D bf16 tensor map for a row-major [rows, cols] matrix with row pitch `ld`
+// elements, box [box_rows, box_cols], 128-byte swizzle when box_cols*2 == 128.
+CUtensorMap make_tmap_2d_bf16(const void *base, uint64_t rows, uint64_t cols, uint64_t ld,
+                              uint32_t box_rows, uint32_t box_cols);
+
+// ---- op launchers (all asynchronous on `stream`; shapes validated, throw on misuse)
+// C[M,N] = A[M,K] . B[N,K]^T (+bias[N]); lda/ldb/ldc in elements.
+void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
+               __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int N, int K,
+               int bn, int grid_limit, uint32_t *status, cudaStream_t stream);
+
+// act[M, n_out] = silu(gate) * up, with B rows interleaved in blocks of bn:
+// rows [b*bn, b*bn+bn/2) gate, [b*bn+bn/2, (b+1)*bn) up for outputs [b*bn/2, (b+1)*bn/2).
+void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
+                    __nv_bfloat16 *act, long ldact, int M, int n_out, int K, int bn,
+                    int grid_limit, uint32_t *status, cudaStream_t stream);
+
+// Choose the UMMA N tile that minimises wave-quantisation loss for a plain GEMM.
+int pick_bn_store(int M, int N, int sms);
+int pick_bn_silu(int M, int n_out, int sms);
+
+// ---- elementwise / normalisation kernels (norm.cu)
+void embed_bf16(const int64_t *ids, const __nv_bfloat16 *table, __nv_bfloat16 *out, int S,
+                int H, int V, uint32_t *status, cudaStream_t stream);
+void rmsnorm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *y,
+                  float *rstd, int rows, int H, float eps, cudaStream_t stream);
+// sum = a + b (bf16-rounded, written when sum != null); y = rmsnorm(sum) * gamma
+void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
+                      const __nv_bfloat16 *gamma, __nv_bfloat16 *y, float *rstd,
+                      __nv_bfloat16 *sum, int rows, int H, float eps, cudaStream_t stream);
+// In-place per-head RMSNorm over D (optional) + rotate-half RoPE on the q and k
+// heads of a fused [S, (HQ+2*HKV)*D] qkv buffer; positions 0..S-1.
+void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
+                       const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
+                       const __nv_bfloat16 *q_norm, const __nv_bfloat16 *k_norm, float eps,
+                       cudaStream_t stream);
+// Causal GQA prefill attention over the fused qkv buffer; out [S, HQ*D].
+void attention_prefill_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *out, int S, int HQ,
+                            int HKV, int D, float scale, cudaStream_t stream);
+// Same over explicit Q/K/V head bases (row pitch ld): query head h of nq reads
+// KV head h / group; out row pitch ldo.
+void attention_heads_bf16(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *v,
+                          long ld, __nv_bfloat16 *out, long ldo, int S, int nq, int group, int D,
+                          float scale, cudaStream_t stream);
+// Transpose a row-major [rows, cols] bf16 matrix into [cols, rows] (dst pitch ld_dst).
+void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, long ld_dst,
+                    int rows, int cols, cudaStream_t stream);
+
+}  // namespace krb

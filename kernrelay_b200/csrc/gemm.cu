@@ -1,0 +1,205 @@
+// tcgen05 GEMM kernels (plain store / bias / SiLU-mul epilogues) and launchers.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.h"
+#include "gemm.cuh"
+
+namespace krb {
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                TileSched ts, int M, int K, EpiArgs ea, uint32_t *status) {
+  extern __shared__ uint8_t smem_raw[];
+  const GemmSmemView<BN> s = GemmSmemView<BN>::carve(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&ta);
+    tma_prefetch_desc(&tb);
+  }
+  gemm_setup<BN>(s, 128);
+  if (warp == 0) {
+    if (lane == 0) gemm_producer<BN>(s, &ta, &tb, ts, K, status);
+  } else if (warp == 1) {
+    if (lane == 0) gemm_mma<BN>(s, ts, K, status);
+  } else {
+    gemm_epilogue<BN, MODE>(s, ts, M, ea, status);
+  }
+  gemm_teardown<BN>(s);
+}
+
+// ------------------------------------------------------------------ host side
+int sm_count(int device) {
+  static int cached[64] = {0};
+  if (device >= 0 && device < 64 && cached[device]) return cached[device];
+  int n = 0;
+  KRB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+  if (device >= 0 && device < 64) cached[device] = n;
+  return n;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    KRB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p) throw CudaError("cuTensorMapEncodeTiled missing");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMap make_tmap_2d_bf16(const void *base, uint64_t rows, uint64_t cols, uint64_t ld,
+                              uint32_t box_rows, uint32_t box_cols) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw CudaError("tensor map base not 16B aligned");
+  if ((ld * 2) % 16 != 0) throw CudaError("tensor map row pitch not a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw =
+      (box_cols * 2 == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return m;
+}
+
+static double wave_eff(long tiles, int sms) {
+  const long waves = (tiles + sms - 1) / sms;
+  return double(tiles) / double(waves * sms);
+}
+
+int pick_bn_store(int M, int N, int sms) {
+  const int cands[3] = {256, 224, 128};
+  const long mblk = (M + kBM - 1) / kBM;
+  int best = 256;
+  double best_score = -1;
+  for (int bn : cands) {
+    const long tiles = mblk * ((N + bn - 1) / bn);
+    // efficiency of waves, times column utilisation of the last N block
+    const double col_util = double(N) / double(((N + bn - 1) / bn) * bn);
+    // wider tiles read A fewer times; small bias towards them
+    const double score = wave_eff(tiles, sms) * col_util * (1.0 + 0.02 * (bn / 32));
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+int pick_bn_silu(int M, int n_out, int sms) {
+  const long mblk = (M + kBM - 1) / kBM;
+  const int cands[2] = {256, 128};
+  int best = 256;
+  double best_score = -1;
+  for (int bn : cands) {
+    const int half = bn / 2;
+    const long nblk = (n_out + half - 1) / half;
+    const double col_util = double(n_out) / double(nblk * half);
+    const double score = wave_eff(mblk * nblk, sms) * col_util * (1.0 + 0.02 * (bn / 32));
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int BN, int MODE>
+static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int n_b_rows, int K,
+                        const EpiArgs &ea, int grid_limit, uint32_t *status, cudaStream_t stream) {
+  using C = GemmCfg<BN>;
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  static bool configured[64] = {false};
+  auto kern = gemm_kernel<BN, MODE>;
+  if (!configured[dev & 63]) {
+    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(C::kSmemBytes)));
+    configured[dev & 63] = true;
+  }
+  TileSched ts;
+  ts.num_m = (M + kBM - 1) / kBM;
+  ts.num_n = (n_b_rows + BN - 1) / BN;
+  ts.band = ts.num_m;
+  const int tiles = ts.num_m * ts.num_n;
+  int grid = std::min(tiles, sm_count(dev));
+  if (grid_limit > 0) grid = std::min(grid, grid_limit);
+  kern<<<grid, kGemmThreads, C::kSmemBytes, stream>>>(ta, tb, ts, M, K, ea, status);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
+               __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int N, int K,
+               int bn, int grid_limit, uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_bf16: empty shape");
+  if (N % 8 != 0 || ldc % 8 != 0) throw CudaError("gemm_bf16: N and ldc must be multiples of 8");
+  if (reinterpret_cast<uintptr_t>(C) % 16 || (bias && reinterpret_cast<uintptr_t>(bias) % 16))
+    throw CudaError("gemm_bf16: C/bias must be 16-byte aligned");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
+  EpiArgs ea{C, ldc, bias, N};
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  switch (bn) {
+    case 256: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
+      launch_gemm<256, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
+      break;
+    }
+    case 224: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
+      launch_gemm<224, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
+      break;
+    }
+    case 128: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
+      launch_gemm<128, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
+      break;
+    }
+    default:
+      throw CudaError("gemm_bf16: unsupported bn " + std::to_string(bn));
+  }
+}
+
+void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
+                    __nv_bfloat16 *act, long ldact, int M, int n_out, int K, int bn,
+                    int grid_limit, uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || n_out <= 0 || K <= 0) throw CudaError("gemm_silu_bf16: empty shape");
+  if (n_out % 8 != 0 || ldact % 8 != 0) throw CudaError("gemm_silu_bf16: n_out % 8 != 0");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_silu(M, n_out, sm_count(dev));
+  const int half = bn / 2;
+  const int nblk = (n_out + half - 1) / half;
+  const int n_b_rows = nblk * bn;
+  EpiArgs ea{act, ldact, nullptr, n_out};
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  switch (bn) {
+    case 256: {
+      const CUtensorMap tb = make_tmap_2d_bf16(Bgu, n_b_rows, K, ldb, 256, kBK);
+      launch_gemm<256, kEpiSiluMul>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+      break;
+    }
+    case 128: {
+      const CUtensorMap tb = make_tmap_2d_bf16(Bgu, n_b_rows, K, ldb, 128, kBK);
+      launch_gemm<128, kEpiSiluMul>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+      break;
+    }
+    default:
+      throw CudaError("gemm_silu_bf16: unsupported bn " + std::to_string(bn));
+  }
+}
+
+}  // namespace krb

@@ -1,0 +1,341 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = A[M, K] . B[N, K]^T        (A, B bf16 K-major; fp32 accumulate in TMEM)
+//
+// Roles inside one 192-thread CTA (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle).
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN,
+//               K=16) into one of two TMEM accumulators and commits to mbarriers.
+//               Warp 1 also owns the TMEM allocation.
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), apply the epilogue, store to HBM, and
+//               hand the accumulator back so the next tile's MMAs overlap.
+//
+// Tiles are visited in "band" order: the output rows are cut into bands of
+// `band` 128-row blocks; all tiles of band 0 come first (row blocks fastest),
+// then band 1, ...  A plain GEMM uses one band covering all rows.  The relay
+// kernel uses one band per row tile of the tp_split schedule so that row tile t
+// completes before row tile t+1 starts.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace krb {
+
+constexpr int kBM = 128;        // UMMA M (cta_group::1)
+constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of bf16
+constexpr int kUmmaK = 16;      // K per tcgen05.mma kind::f16
+constexpr int kGemmThreads = 192;
+constexpr uint64_t kMbarLimitNs = 2000000000ull;  // 2 s: far beyond any legal wait
+
+enum EpiMode : int {
+  kEpiStore = 0,    // C = bf16(acc [+ bias])
+  kEpiSiluMul = 1,  // C[:, j] = bf16(silu(acc[:, g(j)]) * acc[:, u(j)]), interleaved blocks
+};
+
+template <int BN>
+struct GemmCfg {
+  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
+  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 224 ? 5 : 6);
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTileBytes = kStages * kStageBytes;
+  // TMEM accumulator spacing (power of two) and total allocation.
+  static constexpr uint32_t kAccStride = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t kTmemCols = 2 * kAccStride;
+  // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
+  static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
+  static constexpr uint32_t kSmemBytes = kTileBytes + kBarBytes + 1024;  // +1024 alignment slack
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms");
+};
+
+struct TileSched {
+  int num_m;   // 128-row blocks
+  int num_n;   // BN-column blocks
+  int band;    // row blocks per band (num_m % band == 0)
+  __device__ __forceinline__ int total() const { return num_m * num_n; }
+  __device__ __forceinline__ void tile(int idx, int &mb, int &nb) const {
+    const int per_band = band * num_n;
+    const int b = idx / per_band;
+    const int r = idx - b * per_band;
+    nb = r / band;
+    mb = b * band + (r - nb * band);
+  }
+};
+
+template <int BN>
+struct GemmSmemView {
+  uint8_t *tiles;
+  uint64_t *full;
+  uint64_t *empty;
+  uint64_t *tfull;
+  uint64_t *tempty;
+  uint32_t *tmem_slot;
+  volatile int *abort;
+  __device__ __forceinline__ static GemmSmemView carve(uint8_t *raw) {
+    using C = GemmCfg<BN>;
+    GemmSmemView v;
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) &
+                                                ~uintptr_t(1023));
+    v.tiles = base;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::kTileBytes);
+    v.full = bars;
+    v.empty = bars + C::kStages;
+    v.tfull = bars + 2 * C::kStages;
+    v.tempty = bars + 2 * C::kStages + 2;
+    v.tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::kStages + 4);
+    v.abort = reinterpret_cast<volatile int *>(v.tmem_slot + 1);
+    return v;
+  }
+};
+
+// One-time CTA setup: barriers by thread 0, TMEM by warp 1.  Ends with
+// __syncthreads so every role sees the TMEM base address.
+template <int BN>
+__device__ __forceinline__ void gemm_setup(const GemmSmemView<BN> &s, int epi_threads) {
+  using C = GemmCfg<BN>;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], epi_threads);
+    }
+    *s.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(s.tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+template <int BN>
+__device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN> &s) {
+  using C = GemmCfg<BN>;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if ((threadIdx.x >> 5) == 1) tmem_dealloc(*s.tmem_slot, C::kTmemCols);
+}
+
+// ---- warp 0, one thread: TMA producer
+template <int BN>
+__device__ __forceinline__ void gemm_producer(const GemmSmemView<BN> &s, const CUtensorMap *ta,
+                                              const CUtensorMap *tb, const TileSched &ts, int K,
+                                              uint32_t *status) {
+  using C = GemmCfg<BN>;
+  const int nkb = (K + kBK - 1) / kBK;
+  int stage = 0;
+  uint32_t phase = 0;
+  long issued = 0;
+  const uint64_t pol_a = l2_policy_evict_last();
+  for (int t = blockIdx.x; t < ts.total() && !*s.abort; t += gridDim.x) {
+    int mb, nb;
+    ts.tile(t, mb, nb);
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!mbar_wait(&s.empty[stage], phase ^ 1, kMbarLimitNs) || *s.abort) {
+        report_status(status, kStatusTmaWait);
+        *s.abort = 1;
+        goto drain;
+      }
+      {
+        uint8_t *a = s.tiles + stage * C::kStageBytes;
+        uint8_t *b = a + C::kABytes;
+        mbar_arrive_expect_tx(&s.full[stage], C::kStageBytes);
+        tma_load_2d_hint(a, ta, &s.full[stage], kb * kBK, mb * kBM, pol_a);
+        tma_load_2d(b, tb, &s.full[stage], kb * kBK, nb * BN);
+      }
+      ++issued;
+      if (++stage == C::kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+drain:
+  // Make sure no TMA write is still in flight into this CTA's shared memory
+  // before the CTA can exit: wait on the last phase armed for each stage.
+  {
+    const long n = issued < C::kStages ? issued : C::kStages;
+    int st = stage;
+    uint32_t ph = phase;
+    for (long i = 0; i < n; ++i) {
+      if (st == 0) {
+        st = C::kStages - 1;
+        ph ^= 1;
+      } else {
+        --st;
+      }
+      mbar_wait(&s.full[st], ph, kMbarLimitNs / 4);
+    }
+  }
+}
+
+// ---- warp 1, one thread: tcgen05.mma issuer
+template <int BN>
+__device__ __forceinline__ void gemm_mma(const GemmSmemView<BN> &s, const TileSched &ts, int K,
+                                         uint32_t *status) {
+  using C = GemmCfg<BN>;
+  constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+  const uint32_t tmem = *s.tmem_slot;
+  const int nkb = (K + kBK - 1) / kBK;
+  int stage = 0;
+  uint32_t phase = 0;
+  int it = 0;
+  for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
+    const int acc = it & 1;
+    const uint32_t acc_phase = (it >> 1) & 1;
+    if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1, kMbarLimitNs) || *s.abort) {
+      report_status(status, kStatusMmaWait);
+      *s.abort = 1;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t d = tmem + acc * C::kAccStride;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (!mbar_wait(&s.full[stage], phase, kMbarLimitNs) || *s.abort) {
+        report_status(status, kStatusMmaWait);
+        *s.abort = 1;
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a = smem_u32(s.tiles + stage * C::kStageBytes);
+      const uint32_t b = a + C::kABytes;
+#pragma unroll
+      for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+        umma_bf16(d, sdesc_kmajor_sw128(a + kk * kUmmaK * 2),
+                  sdesc_kmajor_sw128(b + kk * kUmmaK * 2), idesc, (kb | kk) != 0);
+      }
+      umma_commit(&s.empty[stage]);
+      if (++stage == C::kStages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    umma_commit(&s.tfull[acc]);
+    if (!ok) break;
+  }
+}
+
+// Epilogue helpers -----------------------------------------------------------
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Store 32 fp32 values as bf16 at dst (16-byte aligned when full).
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16 *dst, const float *v, int valid) {
+  if (valid >= 32) {
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+struct EpiArgs {
+  __nv_bfloat16 *c;           // output
+  long ldc;                   // output row pitch (elements)
+  const __nv_bfloat16 *bias;  // [N] or null (kEpiStore only)
+  int n_out;                  // valid output columns
+};
+
+// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul
+template <int BN, int MODE>
+__device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
+                                              int M, const EpiArgs &ea, uint32_t *status) {
+  using C = GemmCfg<BN>;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int quad = warp & 3;
+  const uint32_t tmem = *s.tmem_slot;
+  int it = 0;
+  for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
+    int mb, nb;
+    ts.tile(t, mb, nb);
+    const int acc = it & 1;
+    const uint32_t acc_phase = (it >> 1) & 1;
+    if (!mbar_wait(&s.tfull[acc], acc_phase, kMbarLimitNs) || *s.abort) {
+      report_status(status, kStatusEpiWait);
+      *s.abort = 1;
+      break;
+    }
+    tc_fence_after();
+    const int row = mb * kBM + quad * 32 + lane;
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
+    if constexpr (MODE == kEpiStore) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        if (col0 >= ea.n_out) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32(tbase + c * 32, r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (ea.bias) {
+          const uint4 *b4 = reinterpret_cast<const uint4 *>(ea.bias + col0);
+          const int valid = min(32, ea.n_out - col0);
+          if (valid >= 32) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w = __ldg(b4 + q);
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = unpack_bf16x2(ws[e]);
+                v[q * 8 + e * 2] += f.x;
+                v[q * 8 + e * 2 + 1] += f.y;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid) v[j] += __bfloat162float(ea.bias[col0 + j]);
+          }
+        }
+        if (row < M) store_row32_bf16(ea.c + row * ea.ldc + col0, v, min(32, ea.n_out - col0));
+      }
+    } else {
+      constexpr int HALF = BN / 2;
+      static_assert(HALF % 32 == 0, "silu epilogue needs BN/2 % 32 == 0");
+#pragma unroll 1
+      for (int c = 0; c < HALF / 32; ++c) {
+        const int col0 = nb * HALF + c * 32;
+        if (col0 >= ea.n_out) break;
+        uint32_t g[32], u[32];
+        tmem_ld_32x32(tbase + c * 32, g);
+        tmem_ld_32x32(tbase + HALF + c * 32, u);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+        if (row < M) store_row32_bf16(ea.c + row * ea.ldc + col0, v, min(32, ea.n_out - col0));
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(&s.tempty[acc]);
+  }
+}
+
+}  // namespace krb

@@ -1,0 +1,203 @@
+// Model directory (manifest.json + weights.bin + ids.bin [+ ref files]) and the
+// per-rank prefill engine.  The directory format is the reference's
+// (scripts/export_model.py:142-223, read by qwen_main.cpp:377-450); the B200
+// build additionally accepts tensors marked {"synth": {...}} in the manifest,
+// which are generated on the device instead of being read from weights.bin.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "relay.cuh"
+
+namespace krb {
+
+struct ModelCfg {
+  std::string arch;
+  int H = 0, I = 0, L = 0, HQ = 0, HKV = 0, D = 0, V = 0;
+  double eps = 1e-6;
+  bool qk_norm = false;
+  bool bias = true;
+  bool tied = true;
+  double theta = 1e6;
+  int seq = 0;
+  int max_pos = 4096;
+  uint64_t seed = 1234;
+};
+
+struct TensorSpec {
+  std::vector<int64_t> shape;
+  size_t offset = 0, bytes = 0;
+  bool synth = false;
+  std::string kind;    // "normal" | "const" | "alias_t" (transpose of another tensor)
+  double std_ = 0.02;
+  double value = 1.0;
+  uint64_t seed = 0;
+  std::string alias;
+  size_t numel() const {
+    size_t n = 1;
+    for (auto d : shape) n *= size_t(d);
+    return n;
+  }
+};
+
+struct Manifest {
+  std::string dir;
+  ModelCfg cfg;
+  std::map<std::string, TensorSpec> tensors;
+  bool has(const std::string &n) const { return tensors.count(n) != 0; }
+  const TensorSpec &at(const std::string &n) const;
+};
+
+Manifest load_manifest(const std::string &dir);
+
+// Execution mode of one engine.
+struct Mode {
+  std::string name;
+  int world = 1;        // TP degree k
+  bool tp = false;      // tp* modes (MLP sharded, reduction per layer)
+  bool split = false;   // row-tile relay (fused kernel) instead of GEMM + AllReduce
+  bool graph = false;   // capture the prefill into a CUDA graph and replay it
+  bool fused = true;    // Add+RMSNorm fused (serial = unfused add then norm)
+  static Mode parse(const std::string &name);
+};
+
+struct EngineOpts {
+  std::string model_dir;
+  std::string mode = "serial";
+  int seq = 2048;
+  int rank = 0;
+  int world = 1;
+  int device = 0;
+  int tiles = 4;
+  int lm_rows = -1;   // -1: all S rows (reference); 1: last row only
+};
+
+// Per-stage device time accumulated by an instrumented run (microseconds).
+struct StageTimes {
+  double embed = 0, qkv = 0, rope = 0, attn = 0, o = 0, addnorm = 0, gateup = 0, down = 0,
+         allreduce = 0, addnorm2 = 0, relay = 0, lm_head = 0, total = 0;
+};
+
+class Engine {
+ public:
+  explicit Engine(const EngineOpts &o);
+  ~Engine();
+  Engine(const Engine &) = delete;
+  Engine &operator=(const Engine &) = delete;
+
+  const ModelCfg &cfg() const { return m_.cfg; }
+  const Mode &mode() const { return mode_; }
+  int rank() const { return opts_.rank; }
+  int world() const { return opts_.world; }
+  int device() const { return opts_.device; }
+  cudaStream_t stream() const { return stream_; }
+
+  // symmetric relay region (tp split modes); null otherwise
+  void *sym_base() const { return sym_; }
+  size_t sym_bytes() const { return sym_layout_.bytes; }
+  void set_peers(const std::vector<void *> &bases);  // index = rank, own entry = sym_base()
+  void set_nccl(ncclComm_t comm) { nccl_ = comm; }
+
+  // one prefill on the engine stream (asynchronous)
+  void enqueue();
+  // one prefill with the host-side copies a caller pays: ids from pinned host
+  // memory to the device, last-row logits back to the host (fp32)
+  void enqueue_host(const int64_t *ids_host, float *last_logits_host);
+  void capture_graph();
+  void run();  // graph replay if captured, else enqueue()
+  void sync();
+  uint32_t read_status();
+  StageTimes instrumented_run();
+
+  // correctness: compare the last-row logits with ref_last_logits.bin / ref.json
+  struct Verdict {
+    int argmax = -1, ref_argmax = -1;
+    double maxdiff = 0, abs_mean = 0;
+    bool has_ref = false;
+  };
+  Verdict verify();
+  std::vector<float> last_logits();
+  // device pointers for tests / profiling
+  const __nv_bfloat16 *hidden_ptr() const;  // residual stream after the last layer (hf or h0)
+  int lm_rows() const { return lm_rows_; }
+  // per-op k-slice timing table (kr_qwen_profile_many)
+  std::string profile_many(const std::string &spec_path);
+  // dump the residual stream after every layer into host memory on the next run
+  void set_layer_dump(bool on);
+  std::vector<uint16_t> layer_hidden(int l);  // bf16 bits [S, H]
+
+ private:
+  void load_weights();
+  void alloc_activations();
+  void fetch(const std::string &name, __nv_bfloat16 *staging);
+  void layer(int l, StageTimes *st);
+  void prologue(StageTimes *st);
+  void epilogue(StageTimes *st);
+  void add_norm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
+                __nv_bfloat16 *y, __nv_bfloat16 *sum);
+
+  EngineOpts opts_;
+  Manifest m_;
+  Mode mode_;
+  int Iloc_ = 0, nqkv_ = 0, bn_gu_ = 256, bn_down_ = 256, gu_rows_ = 0;
+  int lm_rows_ = 0;
+  cudaStream_t stream_ = nullptr;
+  cudaGraphExec_t graph_ = nullptr;
+  ncclComm_t nccl_ = nullptr;
+
+  // weights
+  struct LayerW {
+    __nv_bfloat16 *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr,
+                  *wdown = nullptr, *ln1 = nullptr, *ln2 = nullptr, *qn = nullptr,
+                  *kn = nullptr;
+  };
+  std::vector<LayerW> lw_;
+  __nv_bfloat16 *embed_ = nullptr, *wlm_ = nullptr, *final_norm_ = nullptr, *cos_ = nullptr,
+                *sin_ = nullptr;
+  std::vector<void *> allocs_;
+  void *weight_map_ = nullptr;
+  size_t weight_map_bytes_ = 0;
+  std::string weight_map_dir_;
+
+  // activations
+  __nv_bfloat16 *h0_ = nullptr, *h1_ = nullptr, *x_ = nullptr, *qkv_ = nullptr,
+                *attn_ = nullptr, *o_ = nullptr, *act_ = nullptr, *down_ = nullptr,
+                *red_ = nullptr, *hf_ = nullptr, *xf_ = nullptr, *logits_ = nullptr;
+  int64_t *ids_ = nullptr;
+  uint32_t *status_ = nullptr;
+  float *last_f32_ = nullptr;
+  __nv_bfloat16 *dump_ = nullptr;  // [L, S, H] when layer dumps are on
+
+  // relay
+  SymLayout sym_layout_{};
+  void *sym_ = nullptr;
+  std::vector<void *> peers_;
+  uint32_t rs_expect_ = 0, ag_expect_ = 0;
+  int nseg_ = 0;
+  uint64_t flag_timeout_ns_ = 2000000000ull;
+
+  void *alloc(size_t bytes);
+};
+
+// relay launcher (relay.cu)
+void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w_down, long ldb,
+                      int bn, const RelayArgs &ra, cudaStream_t stream);
+void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
+                        uint32_t *ag_expect, int *nseg);
+
+// device-side synthesis / fill (synth.cu)
+void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_,
+                         cudaStream_t stream);
+void fill_const_device(__nv_bfloat16 *dst, size_t n, float value, cudaStream_t stream);
+void bump_epoch(uint32_t *epoch, cudaStream_t stream);
+void bf16_row_to_f32(const __nv_bfloat16 *src, float *dst, int n, cudaStream_t stream);
+
+}  // namespace krb

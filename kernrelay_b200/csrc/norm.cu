@@ -1,0 +1,250 @@
+// Memory-bound kernels of the prefill: embedding gather, RMSNorm, Add+RMSNorm,
+// per-head QK-RMSNorm + rotate-half RoPE, and a tiled transpose used at load time.
+//
+// All of them read/write bf16 with 16-byte vector accesses where the layout
+// allows, reduce in fp32 with warp shuffles and round once on output.
+#include "common.h"
+#include "ptx.cuh"
+
+namespace krb {
+
+// ------------------------------------------------------------------ embedding
+// out[s, :] = table[ids[s], :]   (aclnnEmbedding in qwen_main.cpp:646-659)
+__global__ void embed_kernel(const int64_t *__restrict__ ids, const uint4 *__restrict__ table,
+                             uint4 *__restrict__ out, int S, int hv, int V, uint32_t *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= S) return;
+  const int64_t id = ids[warp];
+  uint4 *dst = out + static_cast<long>(warp) * hv;
+  if (id < 0 || id >= V) {
+    if (lane == 0) report_status(status, kStatusBadArgs);
+    for (int i = lane; i < hv; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4 *src = table + id * hv;
+  for (int i = lane; i < hv; i += 32) dst[i] = __ldg(src + i);
+}
+
+void embed_bf16(const int64_t *ids, const __nv_bfloat16 *table, __nv_bfloat16 *out, int S, int H,
+                int V, uint32_t *status, cudaStream_t stream) {
+  if (H % 8) throw CudaError("embed: H % 8 != 0");
+  const int threads = 256;
+  const int blocks = (S * 32 + threads - 1) / threads;
+  embed_kernel<<<blocks, threads, 0, stream>>>(ids, reinterpret_cast<const uint4 *>(table),
+                                               reinterpret_cast<uint4 *>(out), S, H / 8, V,
+                                               status);
+  KRB_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ RMSNorm family
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4 &w, float *f) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float2 t = unpack_bf16x2(ws[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float *f) {
+  uint4 w;
+  w.x = pack_bf16x2(f[0], f[1]);
+  w.y = pack_bf16x2(f[2], f[3]);
+  w.z = pack_bf16x2(f[4], f[5]);
+  w.w = pack_bf16x2(f[6], f[7]);
+  return w;
+}
+
+// One warp per row; NV = max 8-element vectors per lane (H <= NV*256).
+// If b != null: s = bf16(a + b) (written to sum if non-null) and the norm is
+// taken over the bf16-rounded s, as the stored residual is what later layers see.
+template <int NV>
+__global__ void add_rmsnorm_kernel(const uint4 *__restrict__ a, const uint4 *__restrict__ b,
+                                   const uint4 *__restrict__ gamma, uint4 *__restrict__ y,
+                                   float *__restrict__ rstd, uint4 *__restrict__ sum, int rows,
+                                   int hv, float inv_h, float eps) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long base = static_cast<long>(row) * hv;
+  float x[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = lane + i * 32;
+    if (v < hv) {
+      unpack8(__ldg(a + base + v), x[i]);
+      if (b) {
+        float t[8];
+        unpack8(__ldg(b + base + v), t);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = bf16_round(x[i][e] + t[e]);
+        if (sum) sum[base + v] = pack8(x[i]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += x[i][e] * x[i][e];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss * inv_h + eps);
+  if (rstd && lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int v = lane + i * 32;
+    if (v < hv) {
+      float g[8];
+      unpack8(__ldg(gamma + v), g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[i][e] = x[i][e] * r * g[e];
+      y[base + v] = pack8(x[i]);
+    }
+  }
+}
+
+static void launch_add_rmsnorm(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
+                               const __nv_bfloat16 *gamma, __nv_bfloat16 *y, float *rstd,
+                               __nv_bfloat16 *sum, int rows, int H, float eps,
+                               cudaStream_t stream) {
+  if (H % 8) throw CudaError("rmsnorm: H % 8 != 0");
+  const int hv = H / 8;
+  const int threads = 128;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  const auto *a4 = reinterpret_cast<const uint4 *>(a);
+  const auto *b4 = reinterpret_cast<const uint4 *>(b);
+  const auto *g4 = reinterpret_cast<const uint4 *>(gamma);
+  auto *y4 = reinterpret_cast<uint4 *>(y);
+  auto *s4 = reinterpret_cast<uint4 *>(sum);
+  const float inv_h = 1.0f / float(H);
+  if (hv <= 4 * 32)
+    add_rmsnorm_kernel<4><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+  else if (hv <= 8 * 32)
+    add_rmsnorm_kernel<8><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+  else if (hv <= 16 * 32)
+    add_rmsnorm_kernel<16><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+  else if (hv <= 32 * 32)
+    add_rmsnorm_kernel<32><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+  else
+    throw CudaError("rmsnorm: H too large");
+  KRB_CUDA(cudaGetLastError());
+}
+
+void rmsnorm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *y,
+                  float *rstd, int rows, int H, float eps, cudaStream_t stream) {
+  launch_add_rmsnorm(x, nullptr, gamma, y, rstd, nullptr, rows, H, eps, stream);
+}
+
+void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
+                      __nv_bfloat16 *y, float *rstd, __nv_bfloat16 *sum, int rows, int H,
+                      float eps, cudaStream_t stream) {
+  launch_add_rmsnorm(a, b, gamma, y, rstd, sum, rows, H, eps, stream);
+}
+
+// ------------------------------------------------------------------ QK-norm + RoPE
+// One warp per (position, head) for the HQ query heads and HKV key heads of the
+// fused qkv row.  Optional per-head RMSNorm over D (Qwen3 q_norm/k_norm, applied
+// before RoPE as in HF Qwen3Attention), then rotate-half RoPE with the bf16
+// cos/sin tables of the model directory (export_model.py:70-77 layout [max_pos, D]).
+template <int D>
+__global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int HQ, int HKV,
+                                    const __nv_bfloat16 *__restrict__ cos_tab,
+                                    const __nv_bfloat16 *__restrict__ sin_tab,
+                                    const __nv_bfloat16 *__restrict__ q_norm,
+                                    const __nv_bfloat16 *__restrict__ k_norm, float eps) {
+  constexpr int HALF = D / 2;
+  constexpr int PER = HALF / 32;  // pairs per lane
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nh = HQ + HKV;
+  if (gw >= S * nh) return;
+  const int s = gw / nh;
+  const int h = gw - s * nh;
+  __nv_bfloat16 *p = qkv + (static_cast<long>(s) * (HQ + 2 * HKV) + h) * D;
+  const __nv_bfloat16 *nw = (h < HQ) ? q_norm : k_norm;
+  float lo[PER], hi[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    lo[i] = __bfloat162float(p[lane + 32 * i]);
+    hi[i] = __bfloat162float(p[HALF + lane + 32 * i]);
+  }
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += lo[i] * lo[i] + hi[i] * hi[i];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / float(D) + eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      // HF RMSNorm returns bf16 before RoPE: keep that rounding point
+      lo[i] = bf16_round(lo[i] * r * __bfloat162float(nw[lane + 32 * i]));
+      hi[i] = bf16_round(hi[i] * r * __bfloat162float(nw[HALF + lane + 32 * i]));
+    }
+  }
+  const __nv_bfloat16 *cr = cos_tab + static_cast<long>(s) * D;
+  const __nv_bfloat16 *sr = sin_tab + static_cast<long>(s) * D;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int j = lane + 32 * i;
+    const float c0 = __bfloat162float(cr[j]), s0 = __bfloat162float(sr[j]);
+    const float c1 = __bfloat162float(cr[HALF + j]), s1 = __bfloat162float(sr[HALF + j]);
+    const float a = lo[i], b = hi[i];
+    p[j] = __float2bfloat16_rn(a * c0 - b * s0);
+    p[HALF + j] = __float2bfloat16_rn(b * c1 + a * s1);
+  }
+}
+
+void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
+                       const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
+                       const __nv_bfloat16 *q_norm, const __nv_bfloat16 *k_norm, float eps,
+                       cudaStream_t stream) {
+  const long warps = static_cast<long>(S) * (HQ + HKV);
+  const int threads = 256;
+  const long blocks = (warps * 32 + threads - 1) / threads;
+  switch (D) {
+    case 64:
+      qk_norm_rope_kernel<64><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab, sin_tab,
+                                                              q_norm, k_norm, eps);
+      break;
+    case 128:
+      qk_norm_rope_kernel<128><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab, sin_tab,
+                                                               q_norm, k_norm, eps);
+      break;
+    default:
+      throw CudaError("qk_norm_rope: head_dim must be 64 or 128");
+  }
+  KRB_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ transpose
+__global__ void transpose_kernel(const __nv_bfloat16 *__restrict__ src, long ld_src,
+                                 __nv_bfloat16 *__restrict__ dst, long ld_dst, int rows,
+                                 int cols) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * ld_src + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * ld_dst + r] = tile[threadIdx.x][i];
+  }
+}
+
+void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, long ld_dst,
+                    int rows, int cols, cudaStream_t stream) {
+  dim3 block(32, 8);
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose_kernel<<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  KRB_CUDA(cudaGetLastError());
+}
+
+}  // namespace krb
