@@ -34,12 +34,12 @@ int krb_device_count(void);
 
 /* ---------------------------------------------------------------- host synthesis
  * Element values of a synthetic tensor (manifest entry {"synth": {"kind":
- * "normal", "std": s, "seed": seed}}), elements [offset, offset+n) of the
+ * "normal", "std": s, "mean": m, "seed": seed}}), elements [offset, offset+n) of the
  * tensor's flat reference layout, as raw bf16 bits.  CPU only; the device
  * loader produces bit-identical values.  (No reference counterpart: the
  * reference exports real checkpoints, scripts/export_model.py:159-169.) */
-int krb_synth_normal_host(const char *name, uint64_t seed, double std_, uint64_t offset,
-                          uint64_t n, uint16_t *out);
+int krb_synth_normal_host(const char *name, uint64_t seed, double std_, double mean,
+                          uint64_t offset, uint64_t n, uint16_t *out);
 
 /* ---------------------------------------------------------------- stand-alone ops */
 /* C[M,N] = A[M,K] . B[N,K]^T (+ bias[N]); tcgen05 GEMM.  bn = UMMA N tile
@@ -65,6 +65,11 @@ int krb_rmsnorm_bf16(const void *x, const void *gamma, void *y, float *rstd, int
 int krb_add_rmsnorm_bf16(const void *a, const void *b, const void *gamma, void *y, float *rstd,
                          void *sum, int rows, int H, float eps, void *stream);
 
+/* Residual-stream form used by the engine: sum = res + delta in fp32 (res and
+ * sum fp32 [rows, H], delta bf16 or NULL), y = RMSNorm(sum) * gamma (bf16). */
+int krb_add_rmsnorm_res_f32(const float *res, const void *delta, const void *gamma, void *y,
+                            float *sum, int rows, int H, float eps, void *stream);
+
 /* out[s,:] = table[ids[s],:]; ids outside [0,V) produce zero rows and set
  * bit 7 of *status (may be NULL).  Replaces aclnnEmbedding (qwen_main.cpp:646-659). */
 int krb_embed_bf16(const int64_t *ids, const void *table, void *out, int S, int H, int V,
@@ -84,8 +89,9 @@ int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HK
                                float scale, void *stream);
 
 /* Fused down-GEMM + row-tile relay + Add+RMSNorm on ONE device (tp degree 1):
- *   down = act[S,K] . w_down[H,K]^T, released to the consumer warps tile by
- *   tile through device counters; sum = bf16(resid + down); x = RMSNorm(sum)*gamma.
+ *   down = act[S,K] . w_down[H,K]^T (bf16 partial), released to the consumer
+ *   warps tile by tile through device counters; sum = resid + down (resid and
+ *   sum fp32 [S,H]); x = RMSNorm(sum)*gamma (bf16).
  * The relay scratch (partial rows, gathered rows, counters: about 4*S*H bytes)
  * is allocated by this call with cudaMalloc and freed before it returns, after
  * synchronising `stream`.  Replaces the tp_split tile loop of qwen_main.cpp:1274-1302
@@ -93,6 +99,21 @@ int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HK
 int krb_relay_down_single(const void *act, const void *w_down, const void *resid,
                           const void *gamma, void *sum_out, void *x_out, int S, int H, int K,
                           int tiles, float eps, int bn, uint32_t *status, void *stream);
+
+/* Failure-detection probe: runs the relay kernel as rank 0 of a two-rank job
+ * whose peer never participates (its region is a second local allocation that
+ * nobody signals).  Rank 0's bounded waits expire after timeout_ms; the kernel
+ * records the status bits (bit 3: partials missing, bit 4: all-gather missing)
+ * in *status_out and returns with the CUDA context usable.  Allocates and frees
+ * its own buffers; synchronises the device.  (The reference's equivalent is the
+ * kr_wait_* status word 2 after maxSpins, kernels/kr_wait_aiv.cpp:22-33.) */
+int krb_relay_timeout_probe(int S, int H, int K, int tiles, float timeout_ms, uint32_t *status_out);
+
+/* Host view of the tp_split relay plan for (S, H, tiles, k, rank, bn): JSON
+ * {R, Rk, num_n, rs_expect, ag_expect, nseg, blocks: [[tile, first_owner,
+ * last_owner] per 128-row block]} -- the row routing the device epilogue uses
+ * and the counter targets the consumer waits for (per layer and run). */
+int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, char *out, size_t cap);
 
 /* ---------------------------------------------------------------- per-rank engine */
 typedef struct krb_engine krb_engine;
@@ -123,14 +144,14 @@ int krb_engine_stage_times(krb_engine *e, char *out, size_t cap);
 /* last-row logits vs ref files; JSON {argmax, ref_argmax, maxdiff, abs_mean, has_ref} */
 int krb_engine_verify(krb_engine *e, char *out, size_t cap);
 int krb_engine_last_logits(krb_engine *e, float *out, int n);
-/* copy the bf16 residual stream after the final layer ([S,H], rank 0) to host */
-int krb_engine_final_hidden(krb_engine *e, uint16_t *out, size_t n);
+/* copy the fp32 residual stream after the final layer ([S,H], rank 0) to host */
+int krb_engine_final_hidden(krb_engine *e, float *out, size_t n);
 /* keep a copy of the residual stream after every layer of the next runs
  * (test-sized models: L*S*H*2 bytes of device memory) */
 int krb_engine_layer_dump(krb_engine *e, int on);
-/* bf16 bits [S, H] of the residual after `layer` (the last layer's entry is
- * the pre-norm final hidden state; rank 0 only) */
-int krb_engine_layer_hidden(krb_engine *e, int layer, uint16_t *out, size_t n);
+/* fp32 [S, H] residual after `layer` (the last layer's entry is the pre-norm
+ * final hidden state, rank 0 only) */
+int krb_engine_layer_hidden(krb_engine *e, int layer, float *out, size_t n);
 /* describe the engine: JSON {H, I, L, V, seq, world, rank, lm_rows, bn_*} */
 int krb_engine_info(krb_engine *e, char *out, size_t cap);
 

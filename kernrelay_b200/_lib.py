@@ -41,7 +41,8 @@ SIGNATURES = [
     ("kr_qwen_profile_many", c_int, [c_char_p, c_char_p, c_int, c_int, c_char_p, c_size_t]),
     ("krb_last_error", c_char_p, []),
     ("krb_device_count", c_int, []),
-    ("krb_synth_normal_host", c_int, [c_char_p, c_u64, ctypes.c_double, c_u64, c_u64, c_void_p]),
+    ("krb_synth_normal_host", c_int, [c_char_p, c_u64, ctypes.c_double, ctypes.c_double, c_u64,
+                                      c_u64, c_void_p]),
     ("krb_gemm_bf16", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long, c_void_p,
                               c_int, c_int, c_int, c_int, c_void_p]),
     ("krb_gemm_silu_bf16", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long, c_int,
@@ -50,6 +51,8 @@ SIGNATURES = [
                                  c_void_p]),
     ("krb_add_rmsnorm_bf16", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_int, c_int, c_float, c_void_p]),
+    ("krb_add_rmsnorm_res_f32", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                        c_int, c_float, c_void_p]),
     ("krb_embed_bf16", c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                                c_void_p]),
     ("krb_qk_norm_rope_bf16", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
@@ -59,6 +62,8 @@ SIGNATURES = [
     ("krb_relay_down_single", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_int, c_int, c_int, c_int, c_float, c_int, c_void_p,
                                       c_void_p]),
+    ("krb_relay_timeout_probe", c_int, [c_int, c_int, c_int, c_int, c_float, c_u32p]),
+    ("krb_relay_plan", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_char_p, c_size_t]),
     ("krb_engine_create", c_int, [c_char_p, c_char_p, c_int, c_int, c_int, c_int, c_int,
                                   ctypes.POINTER(c_void_p)]),
     ("krb_engine_destroy", None, [c_void_p]),
@@ -175,6 +180,17 @@ def add_rmsnorm(a, b, gamma, eps, stream=None):
     return y, s
 
 
+def add_rmsnorm_res(res, delta, gamma, eps, stream=None):
+    """fp32 residual form: (y bf16, sum fp32) with sum = res + delta."""
+    import torch
+    rows, H = res.shape
+    y = torch.empty((rows, H), dtype=torch.bfloat16, device=res.device)
+    s = torch.empty_like(res)
+    check(lib().krb_add_rmsnorm_res_f32(_ptr(res), _ptr(delta), _ptr(gamma), _ptr(y), _ptr(s), rows,
+                                        H, eps, _stream(stream)), "add_rmsnorm_res")
+    return y, s
+
+
 def embed(ids, table, status=None, stream=None):
     import torch
     S = ids.shape[0]
@@ -202,24 +218,40 @@ def attention(qkv, HQ, HKV, D, scale, stream=None):
 
 
 def relay_down_single(act, w_down, resid, gamma, tiles, eps, bn=0, status=None, stream=None):
+    """resid fp32 [S,H] -> (sum fp32 [S,H], x bf16 [S,H])."""
     import torch
     S, K = act.shape
     H = w_down.shape[0]
-    s = torch.empty((S, H), dtype=torch.bfloat16, device=act.device)
-    x = torch.empty_like(s)
+    s = torch.empty((S, H), dtype=torch.float32, device=act.device)
+    x = torch.empty((S, H), dtype=torch.bfloat16, device=act.device)
     check(lib().krb_relay_down_single(_ptr(act), _ptr(w_down), _ptr(resid), _ptr(gamma), _ptr(s),
                                       _ptr(x), S, H, K, tiles, eps, bn, _ptr(status),
                                       _stream(stream)), "relay_down_single")
     return s, x
 
 
-def synth_normal(name: str, seed: int, std: float, n: int, offset: int = 0):
+def synth_normal(name: str, seed: int, std: float, n: int, offset: int = 0, mean: float = 0.0):
     """bf16 bit pattern (uint16 numpy array) of a synthetic tensor (host, no GPU)."""
     import numpy as np
     out = np.empty(n, dtype=np.uint16)
-    check(lib().krb_synth_normal_host(name.encode(), seed, std, offset, n,
+    check(lib().krb_synth_normal_host(name.encode(), seed, std, mean, offset, n,
                                       out.ctypes.data_as(ctypes.c_void_p)), "synth")
     return out
+
+
+def relay_timeout_probe(S, H, K, tiles, timeout_ms):
+    """Status word of a relay whose only peer never runs (see kernrelay_b200.h)."""
+    v = ctypes.c_uint32()
+    check(lib().krb_relay_timeout_probe(S, H, K, tiles, timeout_ms, ctypes.byref(v)), "probe")
+    return v.value
+
+
+def relay_plan(S, H, tiles, k, rank, bn):
+    buf = ctypes.create_string_buffer(1 << 16)
+    rc = lib().krb_relay_plan(S, H, tiles, k, rank, bn, buf, len(buf))
+    if rc != 0:
+        raise KrbError(buf.value.decode(errors="replace"))
+    return json.loads(buf.value.decode())
 
 
 # ---------------------------------------------------------------- per-rank engine
@@ -317,11 +349,11 @@ class Engine:
         check(lib().krb_engine_layer_dump(self.h, 1 if on else 0), "layer_dump")
 
     def layer_hidden(self, layer):
-        """Residual stream after `layer` as float32 numpy [S, H]."""
+        """fp32 residual stream after `layer` as numpy [S, H]."""
         import numpy as np
         info = self.info()
         n = info["seq"] * info["H"]
-        out = np.empty(n, dtype=np.uint16)
+        out = np.empty(n, dtype=np.float32)
         check(lib().krb_engine_layer_hidden(self.h, layer, out.ctypes.data_as(c_void_p), n),
               "layer_hidden")
-        return (out.astype(np.uint32) << 16).view(np.float32).reshape(info["seq"], info["H"])
+        return out.reshape(info["seq"], info["H"])

@@ -408,8 +408,8 @@ KRB_EXPORT int krb_device_count(void) {
   return n;
 }
 
-KRB_EXPORT int krb_synth_normal_host(const char *name, uint64_t seed, double std_, uint64_t offset,
-                                     uint64_t n, uint16_t *out) {
+KRB_EXPORT int krb_synth_normal_host(const char *name, uint64_t seed, double std_, double mean,
+                                     uint64_t offset, uint64_t n, uint16_t *out) {
   try {
     if (!name || !out) throw std::runtime_error("null argument");
     const uint64_t key = krb::synth_key(name, seed);
@@ -419,7 +419,8 @@ KRB_EXPORT int krb_synth_normal_host(const char *name, uint64_t seed, double std
     for (unsigned t = 0; t < nt; ++t)
       th.emplace_back([=] {
         const uint64_t lo = n * t / nt, hi = n * (t + 1) / nt;
-        for (uint64_t i = lo; i < hi; ++i) out[i] = krb::synth_normal_bf16(key, offset + i, scale);
+        for (uint64_t i = lo; i < hi; ++i)
+          out[i] = krb::synth_normal_bf16(key, offset + i, scale, mean);
       });
     for (auto &x : th) x.join();
     return 0;
@@ -469,6 +470,15 @@ KRB_EXPORT int krb_add_rmsnorm_bf16(const void *a, const void *b, const void *ga
   krb::add_rmsnorm_bf16(static_cast<const bf *>(a), static_cast<const bf *>(b),
                         static_cast<const bf *>(gamma), static_cast<bf *>(y), rstd,
                         static_cast<bf *>(sum), rows, H, eps, as_stream(stream));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_add_rmsnorm_res_f32(const float *res, const void *delta, const void *gamma,
+                                       void *y, float *sum, int rows, int H, float eps,
+                                       void *stream) {
+  KRB_OP_BEGIN
+  krb::add_rmsnorm_res_f32(res, static_cast<const bf *>(delta), static_cast<const bf *>(gamma),
+                           static_cast<bf *>(y), sum, rows, H, eps, as_stream(stream));
   KRB_OP_END
 }
 
@@ -530,9 +540,9 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(scratch) + L.epoch());
     ra.layer = 0;
     ra.L = 1;
-    ra.resid = static_cast<const bf *>(resid);
+    ra.resid = static_cast<const float *>(resid);
     ra.gamma = static_cast<const bf *>(gamma);
-    ra.sum_out = static_cast<bf *>(sum_out);
+    ra.sum_out = static_cast<float *>(sum_out);
     ra.x_out = static_cast<bf *>(x_out);
     ra.eps = eps;
     ra.do_norm = 1;
@@ -549,6 +559,102 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
       cudaFree(scratch);
     }
     return fail(e);
+  }
+}
+
+// Failure-detection probe: rank 0 of a two-rank relay whose peer never runs.
+// The "peer" region is a second local allocation nobody signals, so rank 0's
+// bounded waits for the peer's partials must expire after `timeout_ms`, set
+// the status bits and return with the context intact.
+KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float timeout_ms,
+                                       uint32_t *status_out) {
+  void *mine = nullptr, *ghost = nullptr, *bufs = nullptr;
+  try {
+    if (!status_out) throw std::runtime_error("null status");
+    const int k = 2;
+    krb::SymLayout L = krb::SymLayout::make(S, H, tiles, k);
+    KRB_CUDA(cudaMalloc(&mine, L.bytes));
+    KRB_CUDA(cudaMalloc(&ghost, L.bytes));
+    const size_t act_b = size_t(S) * K * 2, w_b = size_t(H) * K * 2, res_b = size_t(S) * H * 4;
+    KRB_CUDA(cudaMalloc(&bufs, act_b + w_b + 2 * res_b + size_t(S) * H * 2 + H * 2 + 256));
+    KRB_CUDA(cudaMemset(mine, 0, L.bytes));
+    KRB_CUDA(cudaMemset(ghost, 0, L.bytes));
+    KRB_CUDA(cudaMemset(bufs, 0, act_b + w_b + 2 * res_b + size_t(S) * H * 2 + H * 2 + 256));
+    uint8_t *p = static_cast<uint8_t *>(bufs);
+    const bf *act = reinterpret_cast<const bf *>(p);
+    const bf *w = reinterpret_cast<const bf *>(p + act_b);
+    float *res = reinterpret_cast<float *>(p + act_b + w_b);
+    float *sum = reinterpret_cast<float *>(p + act_b + w_b + res_b);
+    bf *x = reinterpret_cast<bf *>(p + act_b + w_b + 2 * res_b);
+    bf *gamma = reinterpret_cast<bf *>(p + act_b + w_b + 2 * res_b + size_t(S) * H * 2);
+    uint32_t *status = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(gamma) + H * 2);
+    krb::bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(mine) + L.epoch()), nullptr);
+    krb::RelayArgs ra{};
+    ra.S = S;
+    ra.H = H;
+    ra.K = K;
+    ra.T = tiles;
+    ra.k = k;
+    ra.rank = 0;
+    ra.R = S / tiles;
+    ra.Rk = ra.R / k;
+    krb::relay_expectations(S, H, tiles, k, 0, 256, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.peer_base[0] = static_cast<uint8_t *>(mine);
+    ra.peer_base[1] = static_cast<uint8_t *>(ghost);
+    ra.local_base = static_cast<uint8_t *>(mine);
+    ra.rs_off = L.rs_off;
+    ra.ag_off = L.ag_off;
+    ra.flag_off = L.flag_off;
+    ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(mine) + L.epoch());
+    ra.layer = 0;
+    ra.L = 1;
+    ra.resid = res;
+    ra.gamma = gamma;
+    ra.sum_out = sum;
+    ra.x_out = x;
+    ra.eps = 1e-6f;
+    ra.do_norm = 1;
+    ra.timeout_ns = uint64_t(double(timeout_ms) * 1e6);
+    ra.status = status;
+    krb::relay_down_layer(act, K, w, K, 256, ra, nullptr);
+    KRB_CUDA(cudaDeviceSynchronize());
+    KRB_CUDA(cudaMemcpy(status_out, status, 4, cudaMemcpyDeviceToHost));
+    cudaFree(mine);
+    cudaFree(ghost);
+    cudaFree(bufs);
+    return 0;
+  } catch (const std::exception &e) {
+    cudaDeviceSynchronize();
+    if (mine) cudaFree(mine);
+    if (ghost) cudaFree(ghost);
+    if (bufs) cudaFree(bufs);
+    return fail(e);
+  }
+}
+
+KRB_EXPORT int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, char *out,
+                              size_t cap) {
+  try {
+    if (tiles < 1 || S % tiles || (S / tiles) % 128 || k < 1 || (S / tiles) % k || rank < 0 ||
+        rank >= k || (bn != 128 && bn != 224 && bn != 256))
+      throw std::runtime_error("relay plan: unsupported shape");
+    uint32_t rs = 0, ag = 0;
+    int nseg = 0;
+    krb::relay_expectations(S, H, tiles, k, rank, bn, &rs, &ag, &nseg);
+    const int R = S / tiles, Rk = R / k;
+    std::ostringstream os;
+    os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"num_n\":" << (H + bn - 1) / bn
+       << ",\"rs_expect\":" << rs << ",\"ag_expect\":" << ag << ",\"nseg\":" << nseg
+       << ",\"blocks\":[";
+    for (int b = 0; b < S / 128; ++b) {
+      const krb::RowRoute f = krb::relay_route(b * 128, R, Rk);
+      const krb::RowRoute l = krb::relay_route(b * 128 + 127, R, Rk);
+      os << (b ? "," : "") << "[" << f.tile << "," << f.owner << "," << l.owner << "]";
+    }
+    os << "]}";
+    return write_out(os.str(), out, cap);
+  } catch (const std::exception &e) {
+    return write_error(e.what(), out, cap);
   }
 }
 
@@ -724,14 +830,15 @@ KRB_EXPORT int krb_engine_last_logits(krb_engine *h, float *out, int n) {
   KRB_OP_END
 }
 
-KRB_EXPORT int krb_engine_final_hidden(krb_engine *h, uint16_t *out, size_t n) {
+KRB_EXPORT int krb_engine_final_hidden(krb_engine *h, float *out, size_t n) {
   KRB_OP_BEGIN
   const krb::ModelCfg &c = h->e->cfg();
   const size_t need = size_t(c.seq) * c.H;
   if (n < need) throw std::runtime_error("buffer too small");
+  if (h->e->rank() != 0) throw std::runtime_error("only rank 0 holds the final hidden state");
   KRB_CUDA(cudaSetDevice(h->e->device()));
   KRB_CUDA(cudaStreamSynchronize(h->e->stream()));
-  KRB_CUDA(cudaMemcpy(out, h->e->hidden_ptr(), need * 2, cudaMemcpyDeviceToHost));
+  KRB_CUDA(cudaMemcpy(out, h->e->hidden_ptr(), need * 4, cudaMemcpyDeviceToHost));
   KRB_OP_END
 }
 
@@ -743,7 +850,8 @@ KRB_EXPORT int krb_engine_info(krb_engine *h, char *out, size_t cap) {
        << ",\"HKV\":" << c.HKV << ",\"D\":" << c.D << ",\"V\":" << c.V << ",\"seq\":" << c.seq
        << ",\"world\":" << h->e->world() << ",\"rank\":" << h->e->rank()
        << ",\"lm_rows\":" << h->e->lm_rows() << ",\"split\":" << (h->e->mode().split ? "true" : "false")
-       << ",\"device\":" << h->e->device() << "}";
+       << ",\"device\":" << h->e->device() << ",\"launches_per_run\":" << h->e->launches()
+       << ",\"graph\":" << (h->e->mode().graph ? "true" : "false") << "}";
     return write_out(os.str(), out, cap);
   } catch (const std::exception &e) {
     return write_error(e.what(), out, cap);
@@ -756,10 +864,10 @@ KRB_EXPORT int krb_engine_layer_dump(krb_engine *h, int on) {
   KRB_OP_END
 }
 
-KRB_EXPORT int krb_engine_layer_hidden(krb_engine *h, int layer, uint16_t *out, size_t n) {
+KRB_EXPORT int krb_engine_layer_hidden(krb_engine *h, int layer, float *out, size_t n) {
   KRB_OP_BEGIN
-  std::vector<uint16_t> v = h->e->layer_hidden(layer);
+  std::vector<float> v = h->e->layer_hidden(layer);
   if (n < v.size()) throw std::runtime_error("buffer too small");
-  std::memcpy(out, v.data(), v.size() * 2);
+  std::memcpy(out, v.data(), v.size() * 4);
   KRB_OP_END
 }

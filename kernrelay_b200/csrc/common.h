@@ -56,6 +56,13 @@ void rmsnorm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloa
 void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
                       const __nv_bfloat16 *gamma, __nv_bfloat16 *y, float *rstd,
                       __nv_bfloat16 *sum, int rows, int H, float eps, cudaStream_t stream);
+// fp32 residual stream: sum = res + delta (fp32, unrounded); y = rmsnorm(sum) * gamma
+void add_rmsnorm_res_f32(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
+                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
+                         cudaStream_t stream);
+// embedding gather into an fp32 residual row
+void embed_f32(const int64_t *ids, const __nv_bfloat16 *table, float *out, int S, int H, int V,
+               uint32_t *status, cudaStream_t stream);
 // In-place per-head RMSNorm over D (optional) + rotate-half RoPE on the q and k
 // heads of a fused [S, (HQ+2*HKV)*D] qkv buffer; positions 0..S-1.
 void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,

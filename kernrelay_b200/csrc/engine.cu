@@ -65,6 +65,7 @@ Manifest load_manifest(const std::string &dir) {
       t.kind = s.string_or("kind", "normal");
       t.std_ = s.number_or("std", 0.02);
       t.value = s.number_or("value", 1.0);
+      t.mean = s.number_or("mean", 0.0);
       t.seed = uint64_t(s.number_or("seed", double(g.seed)));
       t.alias = s.string_or("of", "");
     } else {
@@ -205,7 +206,7 @@ void Engine::fetch(const std::string &name, __nv_bfloat16 *staging) {
   const size_t n = t.numel();
   if (t.synth) {
     if (t.kind == "normal") {
-      synth_normal_device(staging, n, synth_key(name.c_str(), t.seed), t.std_, stream_);
+      synth_normal_device(staging, n, synth_key(name.c_str(), t.seed), t.std_, t.mean, stream_);
     } else if (t.kind == "const") {
       fill_const_device(staging, n, float(t.value), stream_);
     } else if (t.kind == "transpose_of") {
@@ -349,8 +350,9 @@ void Engine::alloc_activations() {
   const ModelCfg &c = m_.cfg;
   const size_t S = size_t(opts_.seq), H = size_t(c.H);
   auto A = [&](size_t elems) { return static_cast<__nv_bfloat16 *>(alloc(elems * 2)); };
-  h0_ = A(S * H);
-  h1_ = A(S * H);
+  auto F = [&](size_t elems) { return static_cast<float *>(alloc(elems * 4)); };
+  h0_ = F(S * H);
+  h1_ = F(S * H);
   x_ = A(S * H);
   qkv_ = A(S * size_t(nqkv_));
   attn_ = A(S * size_t(c.HQ) * c.D);
@@ -358,7 +360,7 @@ void Engine::alloc_activations() {
   act_ = A(S * size_t(Iloc_));
   down_ = A(S * H);
   if (mode_.tp && mode_.world > 1 && !mode_.split) red_ = A(S * H);
-  hf_ = A(S * H);
+  hf_ = F(S * H);
   xf_ = A(S * H);
   if (opts_.rank == 0) logits_ = A(size_t(lm_rows_) * size_t(c.V));
   last_f32_ = static_cast<float *>(alloc(size_t(c.V) * 4));
@@ -406,24 +408,28 @@ thread_local std::vector<std::pair<double *, std::pair<cudaEvent_t, cudaEvent_t>
 void Engine::prologue(StageTimes *st) {
   const ModelCfg &c = m_.cfg;
   StageRec rec(stream_, st, g_events);
-  if (mode_.split) bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch()), stream_);
+  if (mode_.split) {
+    bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch()), stream_);
+    ++launches_;
+  }
   rec.begin(st ? &st->embed : nullptr);
-  embed_bf16(ids_, embed_, h0_, opts_.seq, c.H, c.V, status_, stream_);
-  rmsnorm_bf16(h0_, lw_[0].ln1, x_, nullptr, opts_.seq, c.H, float(c.eps), stream_);
+  embed_f32(ids_, embed_, h0_, opts_.seq, c.H, c.V, status_, stream_);
+  add_rmsnorm_res_f32(h0_, nullptr, lw_[0].ln1, x_, nullptr, opts_.seq, c.H, float(c.eps), stream_);
+  launches_ += 2;
   rec.end();
 }
 
-// Add + RMSNorm: one fused kernel, or (unfused serial modes, qwen_main.cpp:976-979)
-// an add pass followed by a separate RMSNorm pass.
-void Engine::add_norm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
-                      __nv_bfloat16 *y, __nv_bfloat16 *sum) {
+// Add + RMSNorm on the fp32 residual stream: one fused kernel, or (unfused serial
+// modes, qwen_main.cpp:976-979) an add pass followed by a separate RMSNorm pass.
+void Engine::add_norm(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
+                      __nv_bfloat16 *y, float *sum) {
   const ModelCfg &c = m_.cfg;
   const float eps = float(c.eps);
-  if (mode_.fused) {
-    add_rmsnorm_bf16(a, b, gamma, y, nullptr, sum, opts_.seq, c.H, eps, stream_);
-  } else {
-    add_rmsnorm_bf16(a, b, gamma, y, nullptr, sum, opts_.seq, c.H, eps, stream_);
-    rmsnorm_bf16(sum, gamma, y, nullptr, opts_.seq, c.H, eps, stream_);
+  add_rmsnorm_res_f32(res, delta, gamma, y, sum, opts_.seq, c.H, eps, stream_);
+  launches_ += 1;
+  if (!mode_.fused) {
+    add_rmsnorm_res_f32(sum, nullptr, gamma, y, nullptr, opts_.seq, c.H, eps, stream_);
+    launches_ += 1;
   }
 }
 
@@ -433,6 +439,7 @@ void Engine::layer(int l, StageTimes *st) {
   const float eps = float(c.eps);
   const LayerW &w = lw_[l];
   StageRec rec(stream_, st, g_events);
+  launches_ += 5;  // qkv, rope, attention, o, gate/up (+ add_norm counted there)
   rec.begin(st ? &st->qkv : nullptr);
   gemm_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, nqkv_, H, 0, 0, status_,
             stream_);
@@ -456,7 +463,7 @@ void Engine::layer(int l, StageTimes *st) {
 
   const bool last = (l + 1 == c.L);
   const __nv_bfloat16 *gamma = last ? final_norm_ : lw_[l + 1].ln1;
-  __nv_bfloat16 *sum_out = last ? hf_ : h0_;
+  float *sum_out = last ? hf_ : h0_;
   __nv_bfloat16 *x_out = last ? xf_ : x_;
   const bool do_norm = !last || opts_.rank == 0;
   if (mode_.split) {
@@ -493,9 +500,11 @@ void Engine::layer(int l, StageTimes *st) {
     ra.status = status_;
     rec.begin(st ? &st->relay : nullptr);
     relay_down_layer(act_, Iloc_, w.wdown, Iloc_, bn_down_, ra, stream_);
+    ++launches_;
     rec.end();
     return;
   }
+  ++launches_;
   rec.begin(st ? &st->down : nullptr);
   gemm_bf16(act_, Iloc_, w.wdown, Iloc_, down_, H, nullptr, S, H, Iloc_, bn_down_, 0, status_, stream_);
   rec.end();
@@ -519,6 +528,7 @@ void Engine::epilogue(StageTimes *st) {
   if (opts_.rank != 0) return;
   const ModelCfg &c = m_.cfg;
   StageRec rec(stream_, st, g_events);
+  ++launches_;
   rec.begin(st ? &st->lm_head : nullptr);
   const int r0 = opts_.seq - lm_rows_;
   gemm_bf16(xf_ + size_t(r0) * c.H, c.H, wlm_, c.H, logits_, c.V, nullptr, lm_rows_, c.V, c.H, 0, 0,
@@ -528,6 +538,7 @@ void Engine::epilogue(StageTimes *st) {
 
 void Engine::enqueue() {
   KRB_CUDA(cudaSetDevice(opts_.device));
+  launches_ = 0;
   prologue(nullptr);
   const size_t SH = size_t(opts_.seq) * m_.cfg.H;
   for (int l = 0; l < m_.cfg.L; ++l) {
@@ -535,7 +546,7 @@ void Engine::enqueue() {
     if (dump_) {
       const bool last = (l + 1 == m_.cfg.L);
       if (!last || opts_.rank == 0)
-        KRB_CUDA(cudaMemcpyAsync(dump_ + size_t(l) * SH, last ? hf_ : h0_, SH * 2,
+        KRB_CUDA(cudaMemcpyAsync(dump_ + size_t(l) * SH, last ? hf_ : h0_, SH * 4,
                                  cudaMemcpyDeviceToDevice, stream_));
     }
   }
@@ -545,20 +556,20 @@ void Engine::enqueue() {
 void Engine::set_layer_dump(bool on) {
   KRB_CUDA(cudaSetDevice(opts_.device));
   if (on && !dump_) {
-    dump_ = static_cast<__nv_bfloat16 *>(alloc(size_t(m_.cfg.L) * opts_.seq * m_.cfg.H * 2));
+    dump_ = static_cast<float *>(alloc(size_t(m_.cfg.L) * opts_.seq * m_.cfg.H * 4));
   } else if (!on) {
     dump_ = nullptr;  // memory stays in allocs_ until destruction
   }
 }
 
-std::vector<uint16_t> Engine::layer_hidden(int l) {
+std::vector<float> Engine::layer_hidden(int l) {
   if (!dump_) throw std::runtime_error("layer dumps are off");
   if (l < 0 || l >= m_.cfg.L) throw std::runtime_error("layer out of range");
   const size_t SH = size_t(opts_.seq) * m_.cfg.H;
-  std::vector<uint16_t> out(SH);
+  std::vector<float> out(SH);
   KRB_CUDA(cudaSetDevice(opts_.device));
   KRB_CUDA(cudaStreamSynchronize(stream_));
-  KRB_CUDA(cudaMemcpy(out.data(), dump_ + size_t(l) * SH, SH * 2, cudaMemcpyDeviceToHost));
+  KRB_CUDA(cudaMemcpy(out.data(), dump_ + size_t(l) * SH, SH * 4, cudaMemcpyDeviceToHost));
   return out;
 }
 
@@ -622,6 +633,7 @@ StageTimes Engine::instrumented_run() {
   KRB_CUDA(cudaEventCreate(&a));
   KRB_CUDA(cudaEventCreate(&b));
   KRB_CUDA(cudaEventRecord(a, stream_));
+  launches_ = 0;
   try {
     prologue(&st);
     for (int l = 0; l < m_.cfg.L; ++l) layer(l, &st);
@@ -659,7 +671,7 @@ std::vector<float> Engine::last_logits() {
   return out;
 }
 
-const __nv_bfloat16 *Engine::hidden_ptr() const { return hf_; }
+const float *Engine::hidden_ptr() const { return hf_; }
 
 Engine::Verdict Engine::verify() {
   Verdict v;

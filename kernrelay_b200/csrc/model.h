@@ -36,9 +36,10 @@ struct TensorSpec {
   std::vector<int64_t> shape;
   size_t offset = 0, bytes = 0;
   bool synth = false;
-  std::string kind;    // "normal" | "const" | "alias_t" (transpose of another tensor)
+  std::string kind;    // "normal" | "const" | "transpose_of" (another tensor, transposed)
   double std_ = 0.02;
-  double value = 1.0;
+  double value = 1.0;   // const fill value
+  double mean = 0.0;    // normal mean
   uint64_t seed = 0;
   std::string alias;
   size_t numel() const {
@@ -126,13 +127,15 @@ class Engine {
   Verdict verify();
   std::vector<float> last_logits();
   // device pointers for tests / profiling
-  const __nv_bfloat16 *hidden_ptr() const;  // residual stream after the last layer (hf or h0)
+  const float *hidden_ptr() const;  // fp32 residual stream after the last layer (hf)
   int lm_rows() const { return lm_rows_; }
+  // kernels of this library launched by the last enqueue (one prefill)
+  int launches() const { return launches_; }
   // per-op k-slice timing table (kr_qwen_profile_many)
   std::string profile_many(const std::string &spec_path);
   // dump the residual stream after every layer into host memory on the next run
   void set_layer_dump(bool on);
-  std::vector<uint16_t> layer_hidden(int l);  // bf16 bits [S, H]
+  std::vector<float> layer_hidden(int l);  // fp32 residual [S, H]
 
  private:
   void load_weights();
@@ -141,14 +144,15 @@ class Engine {
   void layer(int l, StageTimes *st);
   void prologue(StageTimes *st);
   void epilogue(StageTimes *st);
-  void add_norm(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
-                __nv_bfloat16 *y, __nv_bfloat16 *sum);
+  void add_norm(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
+                __nv_bfloat16 *y, float *sum);
 
   EngineOpts opts_;
   Manifest m_;
   Mode mode_;
   int Iloc_ = 0, nqkv_ = 0, bn_gu_ = 256, bn_down_ = 256, gu_rows_ = 0;
   int lm_rows_ = 0;
+  int launches_ = 0;
   cudaStream_t stream_ = nullptr;
   cudaGraphExec_t graph_ = nullptr;
   ncclComm_t nccl_ = nullptr;
@@ -168,13 +172,15 @@ class Engine {
   std::string weight_map_dir_;
 
   // activations
-  __nv_bfloat16 *h0_ = nullptr, *h1_ = nullptr, *x_ = nullptr, *qkv_ = nullptr,
-                *attn_ = nullptr, *o_ = nullptr, *act_ = nullptr, *down_ = nullptr,
-                *red_ = nullptr, *hf_ = nullptr, *xf_ = nullptr, *logits_ = nullptr;
+  // residual stream in fp32 (h0: layer input, h1: after attention, hf: final);
+  // everything the GEMMs read or write is bf16
+  float *h0_ = nullptr, *h1_ = nullptr, *hf_ = nullptr;
+  __nv_bfloat16 *x_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *o_ = nullptr, *act_ = nullptr,
+                *down_ = nullptr, *red_ = nullptr, *xf_ = nullptr, *logits_ = nullptr;
   int64_t *ids_ = nullptr;
   uint32_t *status_ = nullptr;
   float *last_f32_ = nullptr;
-  __nv_bfloat16 *dump_ = nullptr;  // [L, S, H] when layer dumps are on
+  float *dump_ = nullptr;  // [L, S, H] fp32 when layer dumps are on
 
   // relay
   SymLayout sym_layout_{};
@@ -194,7 +200,7 @@ void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *
                         uint32_t *ag_expect, int *nseg);
 
 // device-side synthesis / fill (synth.cu)
-void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_,
+void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_, double mean,
                          cudaStream_t stream);
 void fill_const_device(__nv_bfloat16 *dst, size_t n, float value, cudaStream_t stream);
 void bump_epoch(uint32_t *epoch, cudaStream_t stream);

@@ -26,6 +26,44 @@ __global__ void embed_kernel(const int64_t *__restrict__ ids, const uint4 *__res
   for (int i = lane; i < hv; i += 32) dst[i] = __ldg(src + i);
 }
 
+// fp32 residual variant: out[s, :] = float(table[ids[s], :])
+__global__ void embed_f32_kernel(const int64_t *__restrict__ ids, const uint4 *__restrict__ table,
+                                 float4 *__restrict__ out, int S, int hv, int V, uint32_t *status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= S) return;
+  const int64_t id = ids[warp];
+  float4 *dst = out + static_cast<long>(warp) * hv * 2;
+  const bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) report_status(status, kStatusBadArgs);
+  for (int i = lane; i < hv; i += 32) {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (ok) {
+      const uint4 w = __ldg(table + id * hv + i);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 t = unpack_bf16x2(ws[e]);
+        f[2 * e] = t.x;
+        f[2 * e + 1] = t.y;
+      }
+    }
+    dst[2 * i] = make_float4(f[0], f[1], f[2], f[3]);
+    dst[2 * i + 1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+void embed_f32(const int64_t *ids, const __nv_bfloat16 *table, float *out, int S, int H, int V,
+               uint32_t *status, cudaStream_t stream) {
+  if (H % 8) throw CudaError("embed: H % 8 != 0");
+  const int threads = 256;
+  const int blocks = (S * 32 + threads - 1) / threads;
+  embed_f32_kernel<<<blocks, threads, 0, stream>>>(ids, reinterpret_cast<const uint4 *>(table),
+                                                   reinterpret_cast<float4 *>(out), S, H / 8, V,
+                                                   status);
+  KRB_CUDA(cudaGetLastError());
+}
+
 void embed_bf16(const int64_t *ids, const __nv_bfloat16 *table, __nv_bfloat16 *out, int S, int H,
                 int V, uint32_t *status, cudaStream_t stream) {
   if (H % 8) throw CudaError("embed: H % 8 != 0");
@@ -63,14 +101,34 @@ __device__ __forceinline__ uint4 pack8(const float *f) {
   return w;
 }
 
+// 8 elements of a residual row as fp32 (from fp32 or bf16 storage)
+__device__ __forceinline__ void load8(const float *p, long v, float *f) {
+  const float4 *q = reinterpret_cast<const float4 *>(p) + v * 2;
+  const float4 x = __ldg(q), y = __ldg(q + 1);
+  f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
+  f[4] = y.x; f[5] = y.y; f[6] = y.z; f[7] = y.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, long v, float *f) {
+  unpack8(__ldg(reinterpret_cast<const uint4 *>(p) + v), f);
+}
+__device__ __forceinline__ void store8(float *p, long v, const float *f) {
+  float4 *q = reinterpret_cast<float4 *>(p) + v * 2;
+  q[0] = make_float4(f[0], f[1], f[2], f[3]);
+  q[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
 // One warp per row; NV = max 8-element vectors per lane (H <= NV*256).
-// If b != null: s = bf16(a + b) (written to sum if non-null) and the norm is
-// taken over the bf16-rounded s, as the stored residual is what later layers see.
-template <int NV>
-__global__ void add_rmsnorm_kernel(const uint4 *__restrict__ a, const uint4 *__restrict__ b,
+//   s = a (+ b)            a: residual (fp32 or bf16), b: bf16 delta or null
+//   sum_f <- s (fp32, unrounded)   or   sum_b <- bf16(s) and the norm uses bf16(s)
+//   y = s * rsqrt(mean(s^2) + eps) * gamma  (bf16)
+// With a bf16 sum the norm is taken over the rounded value, as the stored
+// bf16 residual is what later layers see (aclnnAddRmsNorm semantics).
+template <int NV, typename TA>
+__global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const uint4 *__restrict__ b,
                                    const uint4 *__restrict__ gamma, uint4 *__restrict__ y,
-                                   float *__restrict__ rstd, uint4 *__restrict__ sum, int rows,
-                                   int hv, float inv_h, float eps) {
+                                   float *__restrict__ rstd, float *__restrict__ sum_f,
+                                   uint4 *__restrict__ sum_b, int rows, int hv, float inv_h,
+                                   float eps) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -81,14 +139,19 @@ __global__ void add_rmsnorm_kernel(const uint4 *__restrict__ a, const uint4 *__r
   for (int i = 0; i < NV; ++i) {
     const int v = lane + i * 32;
     if (v < hv) {
-      unpack8(__ldg(a + base + v), x[i]);
+      load8(a, base + v, x[i]);
       if (b) {
         float t[8];
         unpack8(__ldg(b + base + v), t);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = bf16_round(x[i][e] + t[e]);
-        if (sum) sum[base + v] = pack8(x[i]);
+        for (int e = 0; e < 8; ++e) x[i][e] += t[e];
       }
+      if (sum_b) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = bf16_round(x[i][e]);
+        sum_b[base + v] = pack8(x[i]);
+      }
+      if (sum_f) store8(sum_f, base + v, x[i]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss += x[i][e] * x[i][e];
     }
@@ -109,28 +172,27 @@ __global__ void add_rmsnorm_kernel(const uint4 *__restrict__ a, const uint4 *__r
   }
 }
 
-static void launch_add_rmsnorm(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
-                               const __nv_bfloat16 *gamma, __nv_bfloat16 *y, float *rstd,
-                               __nv_bfloat16 *sum, int rows, int H, float eps,
-                               cudaStream_t stream) {
+template <typename TA>
+static void launch_add_rmsnorm(const TA *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
+                               __nv_bfloat16 *y, float *rstd, float *sum_f, __nv_bfloat16 *sum_b,
+                               int rows, int H, float eps, cudaStream_t stream) {
   if (H % 8) throw CudaError("rmsnorm: H % 8 != 0");
   const int hv = H / 8;
   const int threads = 128;
   const int blocks = (rows * 32 + threads - 1) / threads;
-  const auto *a4 = reinterpret_cast<const uint4 *>(a);
   const auto *b4 = reinterpret_cast<const uint4 *>(b);
   const auto *g4 = reinterpret_cast<const uint4 *>(gamma);
   auto *y4 = reinterpret_cast<uint4 *>(y);
-  auto *s4 = reinterpret_cast<uint4 *>(sum);
+  auto *s4 = reinterpret_cast<uint4 *>(sum_b);
   const float inv_h = 1.0f / float(H);
   if (hv <= 4 * 32)
-    add_rmsnorm_kernel<4><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<4, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 8 * 32)
-    add_rmsnorm_kernel<8><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<8, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 16 * 32)
-    add_rmsnorm_kernel<16><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<16, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 32 * 32)
-    add_rmsnorm_kernel<32><<<blocks, threads, 0, stream>>>(a4, b4, g4, y4, rstd, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<32, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else
     throw CudaError("rmsnorm: H too large");
   KRB_CUDA(cudaGetLastError());
@@ -138,13 +200,20 @@ static void launch_add_rmsnorm(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
 
 void rmsnorm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *y,
                   float *rstd, int rows, int H, float eps, cudaStream_t stream) {
-  launch_add_rmsnorm(x, nullptr, gamma, y, rstd, nullptr, rows, H, eps, stream);
+  launch_add_rmsnorm<__nv_bfloat16>(x, nullptr, gamma, y, rstd, nullptr, nullptr, rows, H, eps,
+                                    stream);
 }
 
 void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
                       __nv_bfloat16 *y, float *rstd, __nv_bfloat16 *sum, int rows, int H,
                       float eps, cudaStream_t stream) {
-  launch_add_rmsnorm(a, b, gamma, y, rstd, sum, rows, H, eps, stream);
+  launch_add_rmsnorm<__nv_bfloat16>(a, b, gamma, y, rstd, nullptr, sum, rows, H, eps, stream);
+}
+
+void add_rmsnorm_res_f32(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
+                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
+                         cudaStream_t stream) {
+  launch_add_rmsnorm<float>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H, eps, stream);
 }
 
 // ------------------------------------------------------------------ QK-norm + RoPE

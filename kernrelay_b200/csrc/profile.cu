@@ -79,8 +79,7 @@ std::string Engine::profile_many(const std::string &spec_path) {
       shape = "add_rmsnorm|" + std::to_string(S) + "x" + std::to_string(H);
       call = [=](int i) {
         const size_t off = size_t(i) * per * H;
-        add_rmsnorm_bf16(h0_ + off, o_ + off, w.ln2, x_ + off, nullptr, h1_ + off, per, H, eps,
-                         stream_);
+        add_rmsnorm_res_f32(h0_ + off, o_ + off, w.ln2, x_ + off, h1_ + off, per, H, eps, stream_);
       };
     } else if (op == "rope") {
       shape = "rope|" + std::to_string(S) + "x" + std::to_string(nq + nkv);
@@ -92,8 +91,8 @@ std::string Engine::profile_many(const std::string &spec_path) {
     } else if (op == "embedding") {
       shape = "embedding|" + std::to_string(S) + "x" + std::to_string(H);
       call = [=](int i) {
-        embed_bf16(ids_ + size_t(i) * per, embed_, h0_ + size_t(i) * per * H, per, H, c.V, status_,
-                   stream_);
+        embed_f32(ids_ + size_t(i) * per, embed_, h0_ + size_t(i) * per * H, per, H, c.V, status_,
+                  stream_);
       };
     } else if (op == "attention") {
       if (c.HQ % k) continue;

@@ -88,12 +88,9 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
     }
     tc_fence_after();
     const int g = mb * kBM + quad * 32 + lane;      // global row (< S: S % 128 == 0)
-    const int rt = g / ra.R;                        // row tile
-    const int within = g - rt * ra.R;
-    const int owner = within / ra.Rk;
-    const int i = within - owner * ra.Rk;
-    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(ra.peer_base[owner] + ra.rs_off) +
-                         ((static_cast<size_t>(rt) * ra.k + ra.rank) * ra.Rk + i) *
+    const RowRoute rr = relay_route(g, ra.R, ra.Rk);
+    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(ra.peer_base[rr.owner] + ra.rs_off) +
+                         ((static_cast<size_t>(rr.tile) * ra.k + ra.rank) * ra.Rk + rr.local) *
                              static_cast<size_t>(ra.H);
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
 #pragma unroll 1
@@ -113,15 +110,13 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
     fence_sys();                  // this thread's pushes visible system-wide
     named_bar_sync(1, 128);
     if (warp == 2 && lane == 0) {
-      const int r0 = mb * kBM;
-      const int rt0 = r0 / ra.R;
-      const int w0 = r0 - rt0 * ra.R;
-      const int j0 = w0 / ra.Rk;
-      const int j1 = (w0 + kBM - 1) / ra.Rk;
-      for (int j = j0; j <= j1 && j < ra.k; ++j)
-        red_add_release_sys(flag_ptr(ra.peer_base[j], ra.flag_off +
-                                                          (size_t(rt0) * ra.k + ra.rank) * 128),
-                            1u);
+      // one release per owner whose slice this 128-row block touches
+      const RowRoute first = relay_route(mb * kBM, ra.R, ra.Rk);
+      const RowRoute last = relay_route(mb * kBM + kBM - 1, ra.R, ra.Rk);
+      for (int j = first.owner; j <= last.owner; ++j)
+        red_add_release_sys(
+            flag_ptr(ra.peer_base[j], ra.flag_off + (size_t(first.tile) * ra.k + ra.rank) * 128),
+            1u);
     }
   }
 }
@@ -216,30 +211,30 @@ __device__ void relay_consumer(const RelayArgs &ra) {
     if (!ag_ok || !ra.do_norm) continue;
     for (int q = gw; q < ra.R; q += GW) {
       const size_t g = size_t(t) * ra.R + q;
-      const __nv_bfloat16 *hr = ra.resid + g * ra.H;
+      const float4 *hr = reinterpret_cast<const float4 *>(ra.resid + g * ra.H);
       const __nv_bfloat16 *ar = ag_local + g * ra.H;
-      __nv_bfloat16 *so = ra.sum_out + g * ra.H;
+      float4 *so = reinterpret_cast<float4 *>(ra.sum_out + g * ra.H);
       float ss = 0.f;
       for (int col = lane * 8; col < ra.H; col += 256) {
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        acc8_cg(a, hr + col);
         acc8_cg(a, ar + col);
+        const float4 r0 = __ldcg(hr + col / 4), r1 = __ldcg(hr + col / 4 + 1);
+        a[0] += r0.x; a[1] += r0.y; a[2] += r0.z; a[3] += r0.w;
+        a[4] += r1.x; a[5] += r1.y; a[6] += r1.z; a[7] += r1.w;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          a[e] = bf16_round(a[e]);
-          ss += a[e] * a[e];
-        }
-        *reinterpret_cast<uint4 *>(so + col) = pack8f(a);
+        for (int e = 0; e < 8; ++e) ss += a[e] * a[e];
+        so[col / 4] = make_float4(a[0], a[1], a[2], a[3]);
+        so[col / 4 + 1] = make_float4(a[4], a[5], a[6], a[7]);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float r = rsqrtf(ss * inv_h + ra.eps);
       __nv_bfloat16 *xo = ra.x_out + g * ra.H;
       for (int col = lane * 8; col < ra.H; col += 256) {
-        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float gm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        acc8_cg(a, so + col);
         acc8_cg(gm, ra.gamma + col);
+        const float4 s0 = so[col / 4], s1 = so[col / 4 + 1];
+        float a[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) a[e] = a[e] * r * gm[e];
         *reinterpret_cast<uint4 *>(xo + col) = pack8f(a);
@@ -326,16 +321,19 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   }
 }
 
-// Expected counter increments for the relay (host helper).
+// Expected counter increments for the relay (host helper): owner `rank`
+// receives one rs increment per (n block, 128-row block touching its slice)
+// from every source, and one ag increment per reduced 256-column unit of each
+// owner's slice.
 void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
                         uint32_t *ag_expect, int *nseg) {
   const int R = S / T, Rk = R / k;
   const int num_n = (H + bn - 1) / bn;
   int touching = 0;
   for (int b = 0; b < R / kBM; ++b) {
-    const int lo = b * kBM, hi = lo + kBM;  // rows [lo, hi) within the tile
-    const int olo = rank * Rk, ohi = olo + Rk;
-    if (lo < ohi && olo < hi) ++touching;
+    const RowRoute first = relay_route(b * kBM, R, Rk);
+    const RowRoute last = relay_route(b * kBM + kBM - 1, R, Rk);
+    if (first.owner <= rank && rank <= last.owner) ++touching;
   }
   *rs_expect = uint32_t(num_n * touching);
   *nseg = (H + 255) / 256;

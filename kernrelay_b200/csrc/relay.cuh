@@ -10,6 +10,28 @@ namespace krb {
 
 constexpr int kMaxRanks = 8;
 
+#ifdef __CUDACC__
+#define KRB_RELAY_HD __host__ __device__ __forceinline__
+#else
+#define KRB_RELAY_HD inline
+#endif
+
+// Row ownership of the tp_split relay: global row g of the S rows lies in row
+// tile rt = g / R; within the tile the rows are cut into k contiguous owner
+// slices of Rk = R / k rows.  Used by the device epilogue (where to push a
+// partial row) and by the host (expected counter increments).
+struct RowRoute {
+  int tile, owner, local;
+};
+KRB_RELAY_HD RowRoute relay_route(int g, int R, int Rk) {
+  RowRoute r;
+  r.tile = g / R;
+  const int within = g - r.tile * R;
+  r.owner = within / Rk;
+  r.local = within - r.owner * Rk;
+  return r;
+}
+
 // Per-rank symmetric region (one allocation, mapped by every peer):
 //   rs_buf  [T][k][Rk][H] bf16   partial rows pushed by each source rank for the
 //                                 rows this rank owns (owner slice of each tile)
@@ -51,9 +73,9 @@ struct RelayArgs {
   uint32_t ag_expect;   // increments per (tile, owner) per layer on every rank
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;
-  const __nv_bfloat16 *resid;  // h1 [S, H]
+  const float *resid;          // h1 [S, H] fp32 residual stream
   const __nv_bfloat16 *gamma;  // [H]
-  __nv_bfloat16 *sum_out;      // h0 (or hf) [S, H]
+  float *sum_out;              // h0 (or hf) [S, H] fp32
   __nv_bfloat16 *x_out;        // x (or xf) [S, H]
   float eps;
   int do_norm;

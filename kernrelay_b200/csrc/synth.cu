@@ -5,20 +5,21 @@
 
 namespace krb {
 
-__global__ void synth_normal_kernel(uint16_t *dst, size_t n, uint64_t key, double scale) {
+__global__ void synth_normal_kernel(uint16_t *dst, size_t n, uint64_t key, double scale,
+                                    double mean) {
   const size_t stride = size_t(gridDim.x) * blockDim.x;
   for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
-    dst[i] = synth_normal_bf16(key, i, scale);
+    dst[i] = synth_normal_bf16(key, i, scale, mean);
 }
 
-void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_,
+void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_, double mean,
                          cudaStream_t stream) {
   if (!n) return;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   const int blocks = sm_count(dev) * 8;
   synth_normal_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<uint16_t *>(dst), n, key,
-                                                  synth_scale(std_));
+                                                  synth_scale(std_), mean);
   KRB_CUDA(cudaGetLastError());
 }
 

@@ -7,7 +7,7 @@
 //   h_j  = mix64(key + (12*i/2 + j + 1) * GAMMA), j = 0..5   (SplitMix64 stream)
 //   u    = the low and high 24-bit fields of each h_j -> 12 integers in [0, 2^24)
 //   c    = sum(u) - 6*(2^24 - 1)                        (exact in int64)
-//   x    = double(c) * (std * 2^-24)                      (Irwin-Hall(12) ~ N(0, std^2))
+//   x    = mean + double(c) * (std * 2^-24)               (Irwin-Hall(12) ~ N(mean, std^2))
 //   bf16 = round-to-nearest-even(float(x))
 // Every step is exact integer work or a single correctly rounded IEEE operation,
 // so host and device produce bit-identical values.
@@ -56,7 +56,8 @@ KRB_HD inline uint16_t f32_to_bf16_bits(float f) {
   return static_cast<uint16_t>(u >> 16);
 }
 
-KRB_HD inline uint16_t synth_normal_bf16(uint64_t key, uint64_t i, double scale /* std*2^-24 */) {
+KRB_HD inline uint16_t synth_normal_bf16(uint64_t key, uint64_t i, double scale /* std*2^-24 */,
+                                         double mean = 0.0) {
   int64_t s = 0;
 #pragma unroll
   for (int j = 0; j < 6; ++j) {
@@ -64,7 +65,7 @@ KRB_HD inline uint16_t synth_normal_bf16(uint64_t key, uint64_t i, double scale 
     s += static_cast<int64_t>(h & 0xFFFFFFull) + static_cast<int64_t>((h >> 32) & 0xFFFFFFull);
   }
   const int64_t c = s - 6ll * ((1ll << 24) - 1ll);
-  const double x = static_cast<double>(c) * scale;
+  const double x = mean + static_cast<double>(c) * scale;
 #ifdef __CUDA_ARCH__
   const float f = __double2float_rn(x);
 #else

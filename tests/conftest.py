@@ -12,6 +12,7 @@ if str(REPO) not in sys.path:
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
     config.addinivalue_line("markers", "multigpu: needs at least 2 GPUs")
+    config.addinivalue_line("markers", "slow: long-running (full-size model) test")
 
 
 def _have_gpu():

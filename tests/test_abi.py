@@ -1,0 +1,106 @@
+"""CPU: the C-ABI library loads without a GPU, exports exactly the symbols its headers
+declare, and its error paths return the reference's conventions (rc + JSON error)."""
+import json
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _declared():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(kr_\w+|krb_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_exports_match_headers(krlib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(krlib.lib_path())],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    exported = {n for n in exported if n.startswith(("kr_", "krb_"))}
+    declared = _declared()
+    assert declared == exported, (declared - exported, exported - declared)
+    # the reference's six entry points are all there (include/kernrelay.h:11-69)
+    for n in ("kr_version", "kr_plan_run", "kr_qwen_run", "kr_qwen_pp_run", "kr_qwen_tp_run",
+              "kr_qwen_profile_many"):
+        assert n in exported
+    # and the ctypes table binds every one of them
+    assert {n for n, _, _ in krlib.SIGNATURES} == declared
+
+
+def test_version(krlib):
+    from kernrelay_b200 import libapi
+    assert libapi.version().startswith("KernRelay")
+
+
+def test_plan_run_conventions(krlib, tmp_path):
+    from kernrelay_b200 import libapi
+    L = krlib.lib()
+    assert L.kr_plan_run(None, 1, 1, None, None, b"x") == 2      # kr_api.cpp:27
+    sched = tmp_path / "s.json"
+    sched.write_text(json.dumps({"ranks": 1, "tasks": []}))
+    r = libapi.plan_run(sched, devices="0", mode="direct", out_json=tmp_path / "o.json")
+    assert r["_rc"] != 0 and "error" in r
+    r = libapi.plan_run(sched, devices="0", mode="bogus", out_json=tmp_path / "o2.json")
+    assert r["_rc"] != 0 and "unknown plan mode" in r["error"]
+
+
+def test_run_errors_are_json_without_gpu(krlib, tmp_path):
+    """Every runtime entry point reports failures as rc != 0 + {"error": ...}."""
+    from kernrelay_b200 import libapi
+    r = libapi.qwen_run(tmp_path / "missing", mode="serial", seq=64)
+    assert r["_rc"] == 1 and "error" in r
+    r = libapi.qwen_tp_run(tmp_path / "missing", mode="tp2_split", seq=64, dev0=0, dev1=0)
+    assert r["_rc"] == 1 and "error" in r
+    r = libapi.qwen_tp_run(tmp_path / "missing", mode="tp3", seq=64)
+    assert r["_rc"] == 1 and "error" in r
+    r = libapi.qwen_profile_many(tmp_path / "missing", [{"op": "rmsnorm", "k": 1}], seq=64)
+    assert r["_rc"] == 1 and "error" in r
+    r = libapi.qwen_pp_run(tmp_path / "missing", mode="pp", seq=64)
+    assert r["_rc"] == 1 and "error" in r
+
+
+def test_small_output_buffer_is_an_error(krlib, tmp_path):
+    import ctypes
+    buf = ctypes.create_string_buffer(8)
+    rc = krlib.lib().kr_qwen_run(str(tmp_path).encode(), b"serial", 64, 0, 0, 1, buf, len(buf))
+    assert rc == 1 and buf.value.startswith(b'{"err')
+
+
+def test_device_count_never_fails(krlib):
+    assert krlib.lib().krb_device_count() >= 0
+
+
+@pytest.mark.parametrize("S,H,T,k,bn", [(2048, 3584, 4, 8, 256), (2048, 3584, 4, 2, 224),
+                                        (512, 896, 4, 1, 256), (4096, 4096, 4, 8, 256),
+                                        (2048, 2560, 2, 4, 128)])
+def test_relay_plan_counts(krlib, S, H, T, k, bn):
+    """Every source's epilogue releases exactly rs_expect increments on each owner per
+    tile, and the owners' reduced units sum to ag_expect (restated from the plan)."""
+    plans = [krlib.relay_plan(S, H, T, k, r, bn) for r in range(k)]
+    p0 = plans[0]
+    assert p0["R"] == S // T and p0["Rk"] * k == p0["R"]
+    counts = {}
+    for b, (tile, j0, j1) in enumerate(p0["blocks"]):
+        assert tile == (b * 128) // p0["R"]
+        for j in range(j0, j1 + 1):
+            counts[(tile, j)] = counts.get((tile, j), 0) + p0["num_n"]
+    for j in range(k):
+        for t in range(T):
+            assert counts[(t, j)] == plans[j]["rs_expect"], (t, j)
+        assert plans[j]["ag_expect"] == p0["Rk"] * ((H + 255) // 256)
+
+
+def test_relay_plan_rejects_bad_shapes(krlib):
+    with pytest.raises(krlib.KrbError):
+        krlib.relay_plan(2048, 3584, 3, 2, 0, 256)     # 2048 % 3
+    with pytest.raises(krlib.KrbError):
+        krlib.relay_plan(2048, 3584, 32, 1, 0, 256)    # 64-row tiles < 128
+    with pytest.raises(krlib.KrbError):
+        krlib.relay_plan(2048, 3584, 4, 2, 2, 256)     # rank out of range

@@ -1,0 +1,122 @@
+"""End-to-end prefill parity: libkernrelay's engine (C ABI) against the fp32 CPU oracle
+on the same seeded random-init model and tokens.
+
+Bar: identical last-position argmax, and per-layer
+hidden-state max relative error  max|gpu - oracle| / max|oracle|  <= 1e-2 for
+the bf16 build against the fp32 reference."""
+import json
+
+import numpy as np
+import pytest
+
+from kernrelay_b200 import libapi, model_gen
+from oracle import qwen_ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _maxrel(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def tiny_models(tmp_path_factory, krlib):
+    out = {}
+    for name, L, seq in (("tiny-qwen2", 3, 256), ("tiny-qwen3", 3, 256)):
+        cfg = model_gen.config_with(name, L=L)
+        d = model_gen.write_model(tmp_path_factory.mktemp(name) / "m", cfg, seq, norm_std=0.1)
+        ref = qwen_ref.prefill(qwen_ref.Model(d))
+        qwen_ref.write_refs(d, ref)
+        out[name] = (d, ref)
+    return out
+
+
+def _check(eng, ref, L, label):
+    for l in range(L):
+        got = eng.layer_hidden(l)
+        err = _maxrel(got, ref["hidden"][l].numpy())
+        assert err <= TOL, f"{label}: layer {l} max rel err {err:.3g}"
+    logits = eng.last_logits()
+    assert int(np.argmax(logits)) == int(np.argmax(ref["logits_last"])), label
+    assert _maxrel(logits, ref["logits_last"]) <= 2 * TOL, label
+
+
+@pytest.mark.parametrize("mode", ["serial_fused", "serial", "graph_whole", "relay_flag",
+                                  "tp1", "tp1_split"])
+@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-qwen3"])
+def test_engine_matches_oracle(cuda, krlib, tiny_models, model, mode):
+    d, ref = tiny_models[model]
+    eng = krlib.Engine(d, mode, 256, tiles=2)
+    try:
+        eng.layer_dump(True)
+        if mode == "graph_whole":
+            eng.capture()
+        for _ in range(2):  # second run exercises epochs / graph replay
+            eng.run()
+        eng.sync()
+        assert eng.status() == 0
+        _check(eng, ref, 3, f"{model}/{mode}")
+    finally:
+        eng.close()
+
+
+def test_kr_qwen_run_reports_reference_fields(cuda, tiny_models):
+    d, ref = tiny_models["tiny-qwen2"]
+    r = libapi.qwen_run(d, mode="graph_whole", seq=256, device=0, warmup=1, iters=3)
+    assert r["_rc"] == 0, r
+    for key in ("mode", "seq", "device", "warmup", "iters", "best_us", "typical_us", "samples_us",
+                "argmax", "ref_argmax", "maxdiff", "abs_mean", "flag_edges", "flag_timeouts",
+                "host_best_us", "host_typical_us"):
+        assert key in r, key
+    assert r["argmax"] == r["ref_argmax"] == int(np.argmax(ref["logits_last"]))
+    assert r["flag_timeouts"] == 0 and len(r["samples_us"]) == 3
+
+
+def test_kr_qwen_run_errors_are_json(cuda, tmp_path):
+    r = libapi.qwen_run(tmp_path / "nope", mode="serial", seq=64)
+    assert r["_rc"] != 0 and "error" in r
+    r = libapi.qwen_run(tmp_path, mode="bogus_mode", seq=64)
+    assert r["_rc"] != 0 and "error" in r
+
+
+def test_profile_many_table(cuda, tiny_models):
+    d, _ = tiny_models["tiny-qwen3"]
+    ops = ("embedding", "rmsnorm", "add", "add_rmsnorm", "rope", "matmul_q", "matmul_k",
+           "matmul_v", "attention", "matmul_o", "matmul_gate", "matmul_up", "silu", "mul",
+           "matmul_down", "matmul_lm")
+    cases = [{"op": op, "k": k} for op in ops for k in (1, 2)]
+    r = libapi.qwen_profile_many(d, cases, seq=256, device=0)
+    assert r["_rc"] == 0, r
+    got = {(c["op"], c["k"]): c for c in r["cases"]}
+    for op in ops:
+        for k in (1, 2):
+            c = got[(op, k)]
+            assert "error" not in c, c
+            if "fused_into" not in c:
+                assert c["best_us"] > 0
+
+
+@pytest.mark.slow
+def test_qwen25_05b_full_model_parity(cuda, tmp_path):
+    """Qwen2.5-0.5B architecture, S=512, 24 layers, vs the CPU oracle."""
+    cfg = model_gen.CONFIGS["qwen2.5-0.5b"]
+    d = model_gen.write_model(tmp_path / "m05", cfg, 512)
+    ref = qwen_ref.prefill(qwen_ref.Model(d))
+    qwen_ref.write_refs(d, ref)
+    from kernrelay_b200 import _lib
+    eng = _lib.Engine(d, "graph_whole", 512)
+    try:
+        eng.layer_dump(True)
+        eng.capture()
+        eng.run()
+        eng.sync()
+        assert eng.status() == 0
+        _check(eng, ref, cfg.L, "qwen2.5-0.5b")
+        v = eng.verify()
+        assert v["argmax"] == v["ref_argmax"]
+    finally:
+        eng.close()
