@@ -39,6 +39,8 @@ from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
+# stdout carries exactly one JSON line: keep NCCL's banner off it
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 METRIC = "Qwen2.5-7B prefill tok/s @seq2048 at 1/2/4/8 B200; tp_split vs tp speedup"
 # the reference's published numbers for this metric (Ascend 910B3, real weights)
@@ -130,7 +132,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                 "-lms", "50", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                 text=True)
         except OSError:
             self.proc = None

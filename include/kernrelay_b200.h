@@ -48,6 +48,11 @@ int krb_synth_normal_host(const char *name, uint64_t seed, double std_, double m
 int krb_gemm_bf16(const void *A, long lda, const void *B, long ldb, void *C, long ldc,
                   const void *bias, int M, int N, int K, int bn, void *stream);
 
+/* out[M,N] = A[M,K] . B[N,K]^T in fp32 (unrounded; row pitch ld) -- the o_proj and
+ * single-device down_proj form whose output feeds the fp32 residual stream. */
+int krb_gemm_f32out(const void *A, long lda, const void *B, long ldb, float *out, long ld, int M,
+                    int N, int K, int bn, void *stream);
+
 /* act[M, n_out] = silu(A.Bg^T) * (A.Bu^T) where Bgu interleaves gate and up
  * rows in blocks of bn: rows [b*bn, b*bn+bn/2) = gate rows [b*bn/2, (b+1)*bn/2),
  * rows [b*bn+bn/2, (b+1)*bn) = the matching up rows (bn = 128 or 256).
@@ -84,9 +89,13 @@ int krb_qk_norm_rope_bf16(void *qkv, int S, int HQ, int HKV, int D, const void *
                           void *stream);
 
 /* out[S, HQ*D] = causal GQA attention of the q/k/v heads of qkv with the given
- * scale.  Replaces aclnnFlashAttentionScore (qwen_main.cpp:591-614). */
+ * scale.  impl: 0 = automatic (tcgen05/TMEM kernel for D = 128, else mma.sync),
+ * 1 = mma.sync kernel, 2 = tcgen05 kernel (D = 128 only; uses a V^T scratch of
+ * HKV*D*S bf16 allocated and freed stream-ordered on `stream`).  Wait timeouts
+ * set bits in *status (may be NULL).  Replaces aclnnFlashAttentionScore
+ * (qwen_main.cpp:591-614). */
 int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HKV, int D,
-                               float scale, void *stream);
+                               float scale, int impl, uint32_t *status, void *stream);
 
 /* Fused down-GEMM + row-tile relay + Add+RMSNorm on ONE device (tp degree 1):
  *   down = act[S,K] . w_down[H,K]^T (bf16 partial), released to the consumer
@@ -131,6 +140,13 @@ int krb_engine_open_peers(krb_engine *e, const void *handles, size_t bytes);
 /* tp (NCCL baseline): rank 0 creates the id (128 bytes), every rank joins. */
 int krb_nccl_unique_id(void *out, size_t cap);
 int krb_engine_init_nccl(krb_engine *e, const void *id, size_t bytes);
+
+/* One process driving k engines (ranks 0..k-1, one device each): enable peer
+ * access and wire the relay regions directly (tp_split), or create the NCCL
+ * communicators with ncclCommInitAll (tp).  Run the engines from one host
+ * thread each (NCCL's rule for one process and several devices). */
+int krb_engines_link(krb_engine **engines, int n);
+int krb_engines_init_nccl(krb_engine **engines, int n);
 
 int krb_engine_capture(krb_engine *e);          /* capture one prefill into a CUDA graph */
 int krb_engine_run(krb_engine *e);              /* enqueue one prefill (async) */

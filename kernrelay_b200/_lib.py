@@ -45,6 +45,8 @@ SIGNATURES = [
                                       c_u64, c_void_p]),
     ("krb_gemm_bf16", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long, c_void_p,
                               c_int, c_int, c_int, c_int, c_void_p]),
+    ("krb_gemm_f32out", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long, c_int, c_int,
+                                c_int, c_int, c_void_p]),
     ("krb_gemm_silu_bf16", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long, c_int,
                                    c_int, c_int, c_int, c_void_p]),
     ("krb_rmsnorm_bf16", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
@@ -58,7 +60,7 @@ SIGNATURES = [
     ("krb_qk_norm_rope_bf16", c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_float, c_void_p]),
     ("krb_attention_prefill_bf16", c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int,
-                                           c_float, c_void_p]),
+                                           c_float, c_int, c_void_p, c_void_p]),
     ("krb_relay_down_single", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_int, c_int, c_int, c_int, c_float, c_int, c_void_p,
                                       c_void_p]),
@@ -71,6 +73,8 @@ SIGNATURES = [
     ("krb_engine_open_peers", c_int, [c_void_p, c_void_p, c_size_t]),
     ("krb_nccl_unique_id", c_int, [c_void_p, c_size_t]),
     ("krb_engine_init_nccl", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("krb_engines_link", c_int, [ctypes.POINTER(c_void_p), c_int]),
+    ("krb_engines_init_nccl", c_int, [ctypes.POINTER(c_void_p), c_int]),
     ("krb_engine_capture", c_int, [c_void_p]),
     ("krb_engine_run", c_int, [c_void_p]),
     ("krb_engine_run_host", c_int, [c_void_p, c_void_p, c_void_p]),
@@ -134,6 +138,18 @@ def gemm(A, B, bias=None, out=None, bn=0, stream=None):
         out = torch.empty((M, N), dtype=torch.bfloat16, device=A.device)
     check(lib().krb_gemm_bf16(_ptr(A), A.stride(0), _ptr(B), B.stride(0), _ptr(out), out.stride(0),
                               _ptr(bias), M, N, K, bn, _stream(stream)), "gemm")
+    return out
+
+
+def gemm_f32(A, B, out=None, bn=0, stream=None):
+    """fp32 C = A @ B.T (unrounded)."""
+    import torch
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    check(lib().krb_gemm_f32out(_ptr(A), A.stride(0), _ptr(B), B.stride(0), _ptr(out),
+                                out.stride(0), M, N, K, bn, _stream(stream)), "gemm_f32")
     return out
 
 
@@ -208,12 +224,13 @@ def qk_norm_rope(qkv, HQ, HKV, D, cos, sin, q_norm=None, k_norm=None, eps=1e-6, 
     return qkv
 
 
-def attention(qkv, HQ, HKV, D, scale, stream=None):
+def attention(qkv, HQ, HKV, D, scale, impl=0, status=None, stream=None):
+    """impl 0 auto, 1 mma.sync, 2 tcgen05 (D=128)."""
     import torch
     S = qkv.shape[0]
     out = torch.empty((S, HQ * D), dtype=torch.bfloat16, device=qkv.device)
-    check(lib().krb_attention_prefill_bf16(_ptr(qkv), _ptr(out), S, HQ, HKV, D, scale,
-                                           _stream(stream)), "attention")
+    check(lib().krb_attention_prefill_bf16(_ptr(qkv), _ptr(out), S, HQ, HKV, D, scale, impl,
+                                           _ptr(status), _stream(stream)), "attention")
     return out
 
 
@@ -297,6 +314,16 @@ class Engine:
     def init_nccl(self, uid: bytes):
         buf = ctypes.create_string_buffer(uid, len(uid))
         check(lib().krb_engine_init_nccl(self.h, buf, len(uid)), "init_nccl")
+
+    @staticmethod
+    def link(engines):
+        arr = (c_void_p * len(engines))(*[e.h for e in engines])
+        check(lib().krb_engines_link(arr, len(engines)), "engines_link")
+
+    @staticmethod
+    def init_nccl_all(engines):
+        arr = (c_void_p * len(engines))(*[e.h for e in engines])
+        check(lib().krb_engines_init_nccl(arr, len(engines)), "engines_init_nccl")
 
     def capture(self):
         check(lib().krb_engine_capture(self.h), "capture")

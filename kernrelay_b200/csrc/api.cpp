@@ -374,10 +374,10 @@ KRB_EXPORT int kr_qwen_tp_run(const char *model_dir, const char *mode, int seq, 
     }
     bar.wait();
     for (auto &t : th) t.join();
+    eng.clear();  // graphs that hold NCCL work go before the communicators
     for (int r = 0; r < k; ++r) {
       if (comms[r]) ncclCommDestroy(comms[r]);
     }
-    eng.clear();
     if (!err.empty()) throw std::runtime_error(err);
     double best, typ;
     stats(wall, &best, &typ);
@@ -473,6 +473,14 @@ KRB_EXPORT int krb_add_rmsnorm_bf16(const void *a, const void *b, const void *ga
   KRB_OP_END
 }
 
+KRB_EXPORT int krb_gemm_f32out(const void *A, long lda, const void *B, long ldb, float *out,
+                               long ld, int M, int N, int K, int bn, void *stream) {
+  KRB_OP_BEGIN
+  krb::gemm_f32out(static_cast<const bf *>(A), lda, static_cast<const bf *>(B), ldb, out, ld, M, N,
+                   K, bn, nullptr, as_stream(stream));
+  KRB_OP_END
+}
+
 KRB_EXPORT int krb_add_rmsnorm_res_f32(const float *res, const void *delta, const void *gamma,
                                        void *y, float *sum, int rows, int H, float eps,
                                        void *stream) {
@@ -501,10 +509,30 @@ KRB_EXPORT int krb_qk_norm_rope_bf16(void *qkv, int S, int HQ, int HKV, int D, c
 }
 
 KRB_EXPORT int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HKV, int D,
-                                          float scale, void *stream) {
+                                          float scale, int impl, uint32_t *status, void *stream) {
   KRB_OP_BEGIN
-  krb::attention_prefill_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(out), S, HQ, HKV, D,
-                              scale, as_stream(stream));
+  const bool tc = impl == 2 || (impl == 0 && D == 128);
+  if (impl < 0 || impl > 2) throw std::runtime_error("attention: impl must be 0, 1 or 2");
+  if (!tc) {
+    krb::attention_prefill_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(out), S, HQ, HKV,
+                                D, scale, as_stream(stream));
+  } else {
+    // V^T scratch, stream-ordered: allocated and released on the caller's stream
+    cudaStream_t s = as_stream(stream);
+    const long ldv = (long(S) + 7) / 8 * 8;
+    void *vt = nullptr;
+    KRB_CUDA(cudaMallocAsync(&vt, size_t(HKV) * D * ldv * 2, s));
+    try {
+      krb::attention_vt_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(vt), ldv, S, HQ, HKV,
+                             D, s);
+      krb::attention_tc_bf16(static_cast<const bf *>(qkv), static_cast<const bf *>(vt), ldv,
+                             static_cast<bf *>(out), S, HQ, HKV, D, scale, status, s);
+    } catch (...) {
+      cudaFreeAsync(vt, s);
+      throw;
+    }
+    KRB_CUDA(cudaFreeAsync(vt, s));
+  }
   KRB_OP_END
 }
 
@@ -695,10 +723,10 @@ KRB_EXPORT void krb_engine_destroy(krb_engine *h) {
   if (!h) return;
   if (h->e) cudaSetDevice(h->e->device());
   if (h->e) cudaStreamSynchronize(h->e->stream());
+  h->e.reset();  // the engine's graph may hold NCCL work: release it first
   for (void *p : h->opened)
     if (p) cudaIpcCloseMemHandle(p);
   if (h->comm) ncclCommDestroy(h->comm);
-  h->e.reset();
   delete h;
 }
 
@@ -754,6 +782,49 @@ KRB_EXPORT int krb_engine_init_nccl(krb_engine *h, const void *id, size_t bytes)
   ncclResult_t r = ncclCommInitRank(&h->comm, h->e->world(), uid, h->e->rank());
   if (r != ncclSuccess) throw std::runtime_error(std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
   h->e->set_nccl(h->comm);
+  KRB_OP_END
+}
+
+// In-process wiring of k engines (one per device, ranks 0..k-1 in order): peer
+// access between every pair and direct peer pointers to the relay regions.
+KRB_EXPORT int krb_engines_link(krb_engine **hs, int n) {
+  KRB_OP_BEGIN
+  if (!hs || n < 1 || n > krb::kMaxRanks) throw std::runtime_error("bad engine list");
+  std::vector<void *> bases(n);
+  for (int r = 0; r < n; ++r) {
+    if (!hs[r] || hs[r]->e->rank() != r || hs[r]->e->world() != n)
+      throw std::runtime_error("engines must be ranks 0..n-1 of one tp group");
+    bases[r] = hs[r]->e->sym_base();
+  }
+  for (int i = 0; i < n; ++i)
+    for (int j = 0; j < n; ++j) {
+      if (i == j) continue;
+      const int di = hs[i]->e->device(), dj = hs[j]->e->device();
+      int can = 0;
+      KRB_CUDA(cudaDeviceCanAccessPeer(&can, di, dj));
+      if (!can) throw std::runtime_error("no peer access between devices");
+      KRB_CUDA(cudaSetDevice(di));
+      cudaError_t r = cudaDeviceEnablePeerAccess(dj, 0);
+      if (r == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else KRB_CUDA(r);
+    }
+  for (int r = 0; r < n; ++r) hs[r]->e->set_peers(bases);
+  KRB_OP_END
+}
+
+// In-process NCCL communicators for k engines (ncclCommInitAll).
+KRB_EXPORT int krb_engines_init_nccl(krb_engine **hs, int n) {
+  KRB_OP_BEGIN
+  if (!hs || n < 1 || n > krb::kMaxRanks) throw std::runtime_error("bad engine list");
+  std::vector<int> devs(n);
+  std::vector<ncclComm_t> comms(n, nullptr);
+  for (int r = 0; r < n; ++r) devs[r] = hs[r]->e->device();
+  if (ncclCommInitAll(comms.data(), n, devs.data()) != ncclSuccess)
+    throw std::runtime_error("ncclCommInitAll failed");
+  for (int r = 0; r < n; ++r) {
+    hs[r]->comm = comms[r];
+    hs[r]->e->set_nccl(comms[r]);
+  }
   KRB_OP_END
 }
 

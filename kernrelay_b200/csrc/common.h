@@ -37,6 +37,10 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
                __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int N, int K,
                int bn, int grid_limit, uint32_t *status, cudaStream_t stream);
 
+// fp32 output: out[M,N] = A . B^T unrounded (row pitch ld), for residual updates.
+void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb, float *out,
+                 long ld, int M, int N, int K, int bn, uint32_t *status, cudaStream_t stream);
+
 // act[M, n_out] = silu(gate) * up, with B rows interleaved in blocks of bn:
 // rows [b*bn, b*bn+bn/2) gate, [b*bn+bn/2, (b+1)*bn) up for outputs [b*bn/2, (b+1)*bn/2).
 void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
@@ -57,7 +61,11 @@ void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b,
                       const __nv_bfloat16 *gamma, __nv_bfloat16 *y, float *rstd,
                       __nv_bfloat16 *sum, int rows, int H, float eps, cudaStream_t stream);
 // fp32 residual stream: sum = res + delta (fp32, unrounded); y = rmsnorm(sum) * gamma
+// (delta bf16 or fp32, or null)
 void add_rmsnorm_res_f32(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
+                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
+                         cudaStream_t stream);
+void add_rmsnorm_res_f32(const float *res, const float *delta, const __nv_bfloat16 *gamma,
                          __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
                          cudaStream_t stream);
 // embedding gather into an fp32 residual row
@@ -77,6 +85,13 @@ void attention_prefill_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *out, int S,
 void attention_heads_bf16(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *v,
                           long ld, __nv_bfloat16 *out, long ldo, int S, int nq, int group, int D,
                           float scale, cudaStream_t stream);
+// tcgen05 attention (head_dim 128): V^T scratch [HKV*D][ldv >= S] from qkv,
+// then the attention itself reading Q/K from qkv and V from V^T.
+void attention_vt_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *vt, long ldv, int S, int HQ,
+                       int HKV, int D, cudaStream_t stream);
+void attention_tc_bf16(const __nv_bfloat16 *qkv, const __nv_bfloat16 *vt, long ldv,
+                       __nv_bfloat16 *out, int S, int HQ, int HKV, int D, float scale,
+                       uint32_t *status, cudaStream_t stream);
 // Transpose a row-major [rows, cols] bf16 matrix into [cols, rows] (dst pitch ld_dst).
 void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, long ld_dst,
                     int rows, int cols, cudaStream_t stream);

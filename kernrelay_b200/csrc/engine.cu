@@ -361,9 +361,17 @@ void Engine::alloc_activations() {
   down_ = A(S * H);
   if (mode_.tp && mode_.world > 1 && !mode_.split) red_ = A(S * H);
   hf_ = F(S * H);
+  delta_ = F(S * H);
   xf_ = A(S * H);
   if (opts_.rank == 0) logits_ = A(size_t(lm_rows_) * size_t(c.V));
   last_f32_ = static_cast<float *>(alloc(size_t(c.V) * 4));
+  // tcgen05 attention for head_dim 128 (KRB_ATTN=mma selects the mma.sync kernel)
+  const char *ae = std::getenv("KRB_ATTN");
+  attn_tc_ = (c.D == 128) && !(ae && std::string(ae) == "mma");
+  if (attn_tc_) {
+    ldvt_ = (long(S) + 7) / 8 * 8;
+    vt_ = A(size_t(c.HKV) * c.D * ldvt_);
+  }
   // token ids (ids.bin int64 [S], reference UploadIds :473-485)
   ids_ = static_cast<int64_t *>(alloc(S * 8));
   std::ifstream f(m_.dir + "/ids.bin", std::ios::binary | std::ios::ate);
@@ -414,7 +422,8 @@ void Engine::prologue(StageTimes *st) {
   }
   rec.begin(st ? &st->embed : nullptr);
   embed_f32(ids_, embed_, h0_, opts_.seq, c.H, c.V, status_, stream_);
-  add_rmsnorm_res_f32(h0_, nullptr, lw_[0].ln1, x_, nullptr, opts_.seq, c.H, float(c.eps), stream_);
+  add_rmsnorm_res_f32(h0_, static_cast<const float *>(nullptr), lw_[0].ln1, x_, nullptr, opts_.seq,
+                      c.H, float(c.eps), stream_);
   launches_ += 2;
   rec.end();
 }
@@ -428,7 +437,8 @@ void Engine::add_norm(const float *res, const __nv_bfloat16 *delta, const __nv_b
   add_rmsnorm_res_f32(res, delta, gamma, y, sum, opts_.seq, c.H, eps, stream_);
   launches_ += 1;
   if (!mode_.fused) {
-    add_rmsnorm_res_f32(sum, nullptr, gamma, y, nullptr, opts_.seq, c.H, eps, stream_);
+    add_rmsnorm_res_f32(sum, static_cast<const float *>(nullptr), gamma, y, nullptr, opts_.seq, c.H,
+                        eps, stream_);
     launches_ += 1;
   }
 }
@@ -449,14 +459,34 @@ void Engine::layer(int l, StageTimes *st) {
                     c.qk_norm ? w.kn : nullptr, eps, stream_);
   rec.end();
   rec.begin(st ? &st->attn : nullptr);
-  attention_prefill_bf16(qkv_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))), stream_);
+  if (attn_tc_) {
+    attention_vt_bf16(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);
+    attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
+                      status_, stream_);
+    ++launches_;
+  } else {
+    attention_prefill_bf16(qkv_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
+                           stream_);
+  }
   rec.end();
-  rec.begin(st ? &st->o : nullptr);
-  gemm_bf16(attn_, c.HQ * D, w.wo, c.HQ * D, o_, H, nullptr, S, H, c.HQ * D, 0, 0, status_, stream_);
-  rec.end();
-  rec.begin(st ? &st->addnorm : nullptr);
-  add_norm(h0_, o_, w.ln2, x_, h1_);
-  rec.end();
+  if (mode_.fused) {
+    // o_proj output kept in fp32 (no bf16 rounding of o); residual add fused into the norm
+    rec.begin(st ? &st->o : nullptr);
+    gemm_f32out(attn_, c.HQ * D, w.wo, c.HQ * D, delta_, H, S, H, c.HQ * D, 0, status_, stream_);
+    rec.end();
+    rec.begin(st ? &st->addnorm : nullptr);
+    add_rmsnorm_res_f32(h0_, delta_, w.ln2, x_, h1_, S, H, eps, stream_);
+    ++launches_;
+    rec.end();
+  } else {
+    rec.begin(st ? &st->o : nullptr);
+    gemm_bf16(attn_, c.HQ * D, w.wo, c.HQ * D, o_, H, nullptr, S, H, c.HQ * D, 0, 0, status_,
+              stream_);
+    rec.end();
+    rec.begin(st ? &st->addnorm : nullptr);
+    add_norm(h0_, o_, w.ln2, x_, h1_);
+    rec.end();
+  }
   rec.begin(st ? &st->gateup : nullptr);
   gemm_silu_bf16(x_, H, w.wgu, H, act_, Iloc_, S, Iloc_, H, bn_gu_, 0, status_, stream_);
   rec.end();
@@ -505,6 +535,17 @@ void Engine::layer(int l, StageTimes *st) {
     return;
   }
   ++launches_;
+  if (mode_.fused && opts_.world == 1) {
+    // single device: down output kept in fp32, residual add fused into the norm
+    rec.begin(st ? &st->down : nullptr);
+    gemm_f32out(act_, Iloc_, w.wdown, Iloc_, delta_, H, S, H, Iloc_, bn_down_, status_, stream_);
+    rec.end();
+    rec.begin(st ? &st->addnorm2 : nullptr);
+    add_rmsnorm_res_f32(h1_, delta_, gamma, x_out, sum_out, S, H, eps, stream_);
+    ++launches_;
+    rec.end();
+    return;
+  }
   rec.begin(st ? &st->down : nullptr);
   gemm_bf16(act_, Iloc_, w.wdown, Iloc_, down_, H, nullptr, S, H, Iloc_, bn_down_, 0, status_, stream_);
   rec.end();

@@ -150,7 +150,7 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
-  EpiArgs ea{C, ldc, bias, N};
+  EpiArgs ea{C, ldc, bias, N, nullptr};
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   switch (bn) {
     case 256: {
@@ -173,6 +173,37 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
   }
 }
 
+void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb, float *out,
+                 long ld, int M, int N, int K, int bn, uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_f32out: empty shape");
+  if (N % 4 != 0 || ld % 4 != 0) throw CudaError("gemm_f32out: N and ld must be multiples of 4");
+  if (reinterpret_cast<uintptr_t>(out) % 16) throw CudaError("gemm_f32out: out must be 16B aligned");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
+  EpiArgs ea{nullptr, ld, nullptr, N, out};
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  switch (bn) {
+    case 256: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
+      launch_gemm<256, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    case 224: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
+      launch_gemm<224, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    case 128: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
+      launch_gemm<128, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    default:
+      throw CudaError("gemm_f32out: unsupported bn " + std::to_string(bn));
+  }
+}
+
 void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
                     __nv_bfloat16 *act, long ldact, int M, int n_out, int K, int bn,
                     int grid_limit, uint32_t *status, cudaStream_t stream) {
@@ -184,7 +215,7 @@ void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, 
   const int half = bn / 2;
   const int nblk = (n_out + half - 1) / half;
   const int n_b_rows = nblk * bn;
-  EpiArgs ea{act, ldact, nullptr, n_out};
+  EpiArgs ea{act, ldact, nullptr, n_out, nullptr};
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   switch (bn) {
     case 256: {

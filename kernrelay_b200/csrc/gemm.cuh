@@ -27,17 +27,17 @@ constexpr int kBM = 128;        // UMMA M (cta_group::1)
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of bf16
 constexpr int kUmmaK = 16;      // K per tcgen05.mma kind::f16
 constexpr int kGemmThreads = 192;
-constexpr uint64_t kMbarLimitNs = 2000000000ull;  // 2 s: far beyond any legal wait
 
 enum EpiMode : int {
   kEpiStore = 0,    // C = bf16(acc [+ bias])
   kEpiSiluMul = 1,  // C[:, j] = bf16(silu(acc[:, g(j)]) * acc[:, u(j)]), interleaved blocks
+  kEpiStoreF32 = 2, // out_f32 = acc (fp32, unrounded; consumed by the residual Add+RMSNorm)
 };
 
 template <int BN>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
-  static constexpr int kStages = (BN >= 256) ? 4 : (BN >= 224 ? 5 : 6);
+  static constexpr int kStages = (BN >= 224) ? 4 : 6;
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -45,9 +45,14 @@ struct GemmCfg {
   // TMEM accumulator spacing (power of two) and total allocation.
   static constexpr uint32_t kAccStride = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t kTmemCols = 2 * kAccStride;
+  // epilogue staging: one 32 x 32 fp32 chunk per epilogue warp, rows padded to 36
+  static constexpr uint32_t kStageRow = 36;
+  static constexpr uint32_t kEpiBytes = 4 * 32 * kStageRow * 4;
   // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
-  static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16;
-  static constexpr uint32_t kSmemBytes = kTileBytes + kBarBytes + 1024;  // +1024 alignment slack
+  // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
+  static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16 + 64;
+  static constexpr uint32_t kSmemBytes =
+      kTileBytes + kEpiBytes + kBarBytes + 1024;  // +1024 alignment slack
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms");
 };
 
@@ -74,19 +79,23 @@ struct GemmSmemView {
   uint64_t *tempty;
   uint32_t *tmem_slot;
   volatile int *abort;
+  float *epi;  // 4 x [32][kStageRow] fp32 staging chunks (epilogue warps)
+  float *scratch;  // 16 floats for the relay warps
   __device__ __forceinline__ static GemmSmemView carve(uint8_t *raw) {
     using C = GemmCfg<BN>;
     GemmSmemView v;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) &
                                                 ~uintptr_t(1023));
     v.tiles = base;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::kTileBytes);
+    v.epi = reinterpret_cast<float *>(base + C::kTileBytes);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + C::kTileBytes + C::kEpiBytes);
     v.full = bars;
     v.empty = bars + C::kStages;
     v.tfull = bars + 2 * C::kStages;
     v.tempty = bars + 2 * C::kStages + 2;
     v.tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * C::kStages + 4);
     v.abort = reinterpret_cast<volatile int *>(v.tmem_slot + 1);
+    v.scratch = reinterpret_cast<float *>(v.tmem_slot + 4);
     return v;
   }
 };
@@ -256,9 +265,82 @@ struct EpiArgs {
   long ldc;                   // output row pitch (elements)
   const __nv_bfloat16 *bias;  // [N] or null (kEpiStore only)
   int n_out;                  // valid output columns
+  float *out_f32;             // kEpiStoreF32: output [M, ldc] fp32
 };
 
-// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul
+// The accumulator chunk a warp holds is row-per-thread (thread = TMEM lane = row,
+// 32 consecutive columns).  Writing that straight to HBM gives 32 scattered
+// 16-byte pieces per instruction.  Instead each warp stages the 32 x 32 fp32
+// chunk in its own padded shared-memory block and writes it back row-contiguous:
+// 64 bytes per row for bf16 outputs (4 lanes per row), 128 bytes per row for fp32
+// outputs (8 lanes per row).  Padding rows to 36 floats keeps both the row-wise
+// writes and the column-block reads free of bank conflicts.
+__device__ __forceinline__ void epi_stage_put(float *stage, const float *v) {
+  const int lane = threadIdx.x & 31;
+  float4 *row = reinterpret_cast<float4 *>(stage + lane * 36);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) row[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+}
+
+// bf16 write-back: lane l covers row (l/4 + 8*it) columns [8*(l%4), +8)
+template <typename RowPtr>
+__device__ __forceinline__ void epi_stage_store_bf16(const float *stage, RowPtr row_ptr,
+                                                     const __nv_bfloat16 *bias, int col0,
+                                                     int valid_cols) {
+  const int lane = threadIdx.x & 31;
+  const int piece = lane & 3;
+  const int c = piece * 8;
+  float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (bias && c < valid_cols) {
+    const uint4 w = __ldg(reinterpret_cast<const uint4 *>(bias + col0 + c));
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(ws[e]);
+      b[2 * e] = f.x;
+      b[2 * e + 1] = f.y;
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2);
+    const float4 x = *reinterpret_cast<const float4 *>(stage + r * 36 + c);
+    const float4 y = *reinterpret_cast<const float4 *>(stage + r * 36 + c + 4);
+    __nv_bfloat16 *dst = row_ptr(r);
+    if (dst && c < valid_cols) {
+      uint4 w;
+      w.x = pack_bf16x2(x.x + b[0], x.y + b[1]);
+      w.y = pack_bf16x2(x.z + b[2], x.w + b[3]);
+      w.z = pack_bf16x2(y.x + b[4], y.y + b[5]);
+      w.w = pack_bf16x2(y.z + b[6], y.w + b[7]);
+      *reinterpret_cast<uint4 *>(dst + col0 + c) = w;
+    }
+  }
+  __syncwarp();
+}
+
+// fp32 write-back: lane l covers row (l/8 + 4*it) columns [4*(l%8), +4), i.e. 128
+// contiguous bytes per row and instruction group.  Store-only: an epilogue that
+// also reads HBM (e.g. a residual) holds the TMEM accumulator for a full memory
+// latency per chunk and throttles the MMA.
+__device__ __forceinline__ void epi_stage_store_f32(const float *stage, float *out, long ld,
+                                                    int row0, int M, int col0, int valid_cols) {
+  const int lane = threadIdx.x & 31;
+  const int c = (lane & 7) * 4;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const int grow = row0 + r;
+    if (grow < M && c < valid_cols) {
+      const float4 a = *reinterpret_cast<const float4 *>(stage + r * 36 + c);
+      *reinterpret_cast<float4 *>(out + static_cast<size_t>(grow) * ld + col0 + c) = a;
+    }
+  }
+  __syncwarp();
+}
+
+// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32
 template <int BN, int MODE>
 __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
                                               int M, const EpiArgs &ea, uint32_t *status) {
@@ -267,6 +349,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
   const int lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const uint32_t tmem = *s.tmem_slot;
+  float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
     int mb, nb;
@@ -279,9 +362,12 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
       break;
     }
     tc_fence_after();
-    const int row = mb * kBM + quad * 32 + lane;
+    const int row0 = mb * kBM + quad * 32;
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
-    if constexpr (MODE == kEpiStore) {
+    auto bf16_row = [&](int r) -> __nv_bfloat16 * {
+      return (row0 + r < M) ? ea.c + static_cast<long>(row0 + r) * ea.ldc : nullptr;
+    };
+    if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = nb * BN + c * 32;
@@ -292,28 +378,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (ea.bias) {
-          const uint4 *b4 = reinterpret_cast<const uint4 *>(ea.bias + col0);
-          const int valid = min(32, ea.n_out - col0);
-          if (valid >= 32) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint4 w = __ldg(b4 + q);
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = unpack_bf16x2(ws[e]);
-                v[q * 8 + e * 2] += f.x;
-                v[q * 8 + e * 2 + 1] += f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < valid) v[j] += __bfloat162float(ea.bias[col0 + j]);
-          }
-        }
-        if (row < M) store_row32_bf16(ea.c + row * ea.ldc + col0, v, min(32, ea.n_out - col0));
+        epi_stage_put(stage, v);
+        if constexpr (MODE == kEpiStore)
+          epi_stage_store_bf16(stage, bf16_row, ea.bias, col0, ea.n_out - col0);
+        else
+          epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, ea.n_out - col0);
       }
     } else {
       constexpr int HALF = BN / 2;
@@ -330,7 +399,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-        if (row < M) store_row32_bf16(ea.c + row * ea.ldc + col0, v, min(32, ea.n_out - col0));
+        epi_stage_put(stage, v);
+        epi_stage_store_bf16(stage, bf16_row, nullptr, col0, ea.n_out - col0);
       }
     }
     tc_fence_before();

@@ -175,12 +175,16 @@ class Engine {
   // residual stream in fp32 (h0: layer input, h1: after attention, hf: final);
   // everything the GEMMs read or write is bf16
   float *h0_ = nullptr, *h1_ = nullptr, *hf_ = nullptr;
+  float *delta_ = nullptr;  // fp32 o_proj / down output before the residual add
   __nv_bfloat16 *x_ = nullptr, *qkv_ = nullptr, *attn_ = nullptr, *o_ = nullptr, *act_ = nullptr,
                 *down_ = nullptr, *red_ = nullptr, *xf_ = nullptr, *logits_ = nullptr;
   int64_t *ids_ = nullptr;
   uint32_t *status_ = nullptr;
   float *last_f32_ = nullptr;
   float *dump_ = nullptr;  // [L, S, H] fp32 when layer dumps are on
+  __nv_bfloat16 *vt_ = nullptr;  // V^T [HKV*D, ldvt_] for the tcgen05 attention
+  long ldvt_ = 0;
+  bool attn_tc_ = false;
 
   // relay
   SymLayout sym_layout_{};

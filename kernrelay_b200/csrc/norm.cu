@@ -123,8 +123,8 @@ __device__ __forceinline__ void store8(float *p, long v, const float *f) {
 //   y = s * rsqrt(mean(s^2) + eps) * gamma  (bf16)
 // With a bf16 sum the norm is taken over the rounded value, as the stored
 // bf16 residual is what later layers see (aclnnAddRmsNorm semantics).
-template <int NV, typename TA>
-__global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const uint4 *__restrict__ b,
+template <int NV, typename TA, typename TB>
+__global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restrict__ b,
                                    const uint4 *__restrict__ gamma, uint4 *__restrict__ y,
                                    float *__restrict__ rstd, float *__restrict__ sum_f,
                                    uint4 *__restrict__ sum_b, int rows, int hv, float inv_h,
@@ -142,7 +142,7 @@ __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const uint4 *__rest
       load8(a, base + v, x[i]);
       if (b) {
         float t[8];
-        unpack8(__ldg(b + base + v), t);
+        load8(b, base + v, t);
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[i][e] += t[e];
       }
@@ -172,27 +172,26 @@ __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const uint4 *__rest
   }
 }
 
-template <typename TA>
-static void launch_add_rmsnorm(const TA *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
+template <typename TA, typename TB>
+static void launch_add_rmsnorm(const TA *a, const TB *b, const __nv_bfloat16 *gamma,
                                __nv_bfloat16 *y, float *rstd, float *sum_f, __nv_bfloat16 *sum_b,
                                int rows, int H, float eps, cudaStream_t stream) {
   if (H % 8) throw CudaError("rmsnorm: H % 8 != 0");
   const int hv = H / 8;
   const int threads = 128;
   const int blocks = (rows * 32 + threads - 1) / threads;
-  const auto *b4 = reinterpret_cast<const uint4 *>(b);
   const auto *g4 = reinterpret_cast<const uint4 *>(gamma);
   auto *y4 = reinterpret_cast<uint4 *>(y);
   auto *s4 = reinterpret_cast<uint4 *>(sum_b);
   const float inv_h = 1.0f / float(H);
   if (hv <= 4 * 32)
-    add_rmsnorm_kernel<4, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<4, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 8 * 32)
-    add_rmsnorm_kernel<8, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<8, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 16 * 32)
-    add_rmsnorm_kernel<16, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<16, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else if (hv <= 32 * 32)
-    add_rmsnorm_kernel<32, TA><<<blocks, threads, 0, stream>>>(a, b4, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
+    add_rmsnorm_kernel<32, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
   else
     throw CudaError("rmsnorm: H too large");
   KRB_CUDA(cudaGetLastError());
@@ -200,20 +199,29 @@ static void launch_add_rmsnorm(const TA *a, const __nv_bfloat16 *b, const __nv_b
 
 void rmsnorm_bf16(const __nv_bfloat16 *x, const __nv_bfloat16 *gamma, __nv_bfloat16 *y,
                   float *rstd, int rows, int H, float eps, cudaStream_t stream) {
-  launch_add_rmsnorm<__nv_bfloat16>(x, nullptr, gamma, y, rstd, nullptr, nullptr, rows, H, eps,
-                                    stream);
+  launch_add_rmsnorm<__nv_bfloat16, __nv_bfloat16>(x, nullptr, gamma, y, rstd, nullptr, nullptr,
+                                                   rows, H, eps, stream);
 }
 
 void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv_bfloat16 *gamma,
                       __nv_bfloat16 *y, float *rstd, __nv_bfloat16 *sum, int rows, int H,
                       float eps, cudaStream_t stream) {
-  launch_add_rmsnorm<__nv_bfloat16>(a, b, gamma, y, rstd, nullptr, sum, rows, H, eps, stream);
+  launch_add_rmsnorm<__nv_bfloat16, __nv_bfloat16>(a, b, gamma, y, rstd, nullptr, sum, rows, H,
+                                                   eps, stream);
 }
 
 void add_rmsnorm_res_f32(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
                          __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
                          cudaStream_t stream) {
-  launch_add_rmsnorm<float>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H, eps, stream);
+  launch_add_rmsnorm<float, __nv_bfloat16>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H,
+                                           eps, stream);
+}
+
+void add_rmsnorm_res_f32(const float *res, const float *delta, const __nv_bfloat16 *gamma,
+                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
+                         cudaStream_t stream) {
+  launch_add_rmsnorm<float, float>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H, eps,
+                                   stream);
 }
 
 // ------------------------------------------------------------------ QK-norm + RoPE

@@ -26,6 +26,9 @@ enum StatusBits : uint32_t {
   kStatusBadArgs = 1u << 7,      // kernel refused its arguments
 };
 
+// Limit of every mbarrier wait: far beyond any legal wait inside one kernel.
+constexpr uint64_t kMbarLimitNs = 2000000000ull;
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -89,7 +92,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2D tiled TMA load (no multicast) completing on `bar` with byte accounting.
+// 2D tiled TMA load into this CTA's shared memory, completing on `bar` (byte count).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
                                             int32_t c_inner, int32_t c_outer) {
   asm volatile(

@@ -27,6 +27,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.h"
 #include "gemm.cuh"
@@ -34,8 +35,9 @@
 
 namespace krb {
 
-constexpr int kRelayThreads = 320;
-constexpr int kRelayWarp0 = 6;
+constexpr int kRelayWarp0 = 6;                      // warps 0..5: GEMM roles
+constexpr int kRelayWarps = 8;                      // consumer warps per CTA
+constexpr int kRelayThreads = (kRelayWarp0 + kRelayWarps) * 32;
 
 __device__ __forceinline__ uint32_t *flag_ptr(uint8_t *base, size_t off) {
   return reinterpret_cast<uint32_t *>(base + off);
@@ -44,6 +46,17 @@ __device__ __forceinline__ uint32_t *flag_ptr(uint8_t *base, size_t off) {
 // fp32 accumulate of 8 bf16 from a 16-byte vector (L2-coherent load)
 __device__ __forceinline__ void acc8_cg(float *acc, const __nv_bfloat16 *p) {
   const uint4 w = __ldcg(reinterpret_cast<const uint4 *>(p));
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = unpack_bf16x2(ws[e]);
+    acc[2 * e] += f.x;
+    acc[2 * e + 1] += f.y;
+  }
+}
+
+// fp32 accumulate of 8 bf16 held in a 16-byte register vector
+__device__ __forceinline__ void acc8_bits(float *acc, const uint4 &w) {
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
@@ -63,6 +76,10 @@ __device__ __forceinline__ uint4 pack8f(const float *f) {
 }
 
 // ---------------------------------------------------------------- push epilogue
+// Peer region bases, copied from the kernel parameters into shared memory so the
+// epilogue can index them by owner rank without a local-memory copy.
+__shared__ uint8_t *g_peer_base[kMaxRanks];
+
 template <int BN>
 __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
                                                     const RelayArgs &ra) {
@@ -87,12 +104,16 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
       break;
     }
     tc_fence_after();
-    const int g = mb * kBM + quad * 32 + lane;      // global row (< S: S % 128 == 0)
-    const RowRoute rr = relay_route(g, ra.R, ra.Rk);
-    __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(ra.peer_base[rr.owner] + ra.rs_off) +
-                         ((static_cast<size_t>(rr.tile) * ra.k + ra.rank) * ra.Rk + rr.local) *
-                             static_cast<size_t>(ra.H);
+    const int row0 = mb * kBM + quad * 32;           // first row of this warp (< S)
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
+    float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
+    // destination row of rs_buf on the owner of global row row0 + r
+    auto push_row = [&](int r) -> __nv_bfloat16 * {
+      const RowRoute rr = relay_route(row0 + r, ra.R, ra.Rk);
+      return reinterpret_cast<__nv_bfloat16 *>(g_peer_base[rr.owner] + ra.rs_off) +
+             ((static_cast<size_t>(rr.tile) * ra.k + ra.rank) * ra.Rk + rr.local) *
+                 static_cast<size_t>(ra.H);
+    };
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col0 = nb * BN + c * 32;
@@ -103,7 +124,13 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-      store_row32_bf16(dst + col0, v, min(32, ra.H - col0));
+      epi_stage_put(stage, v);
+      if (ra.k == 1)
+        // one rank: nothing to reduce; the fp32 partial goes straight into sum_out
+        // (store-only epilogue) and the relay warps add the residual in place
+        epi_stage_store_f32(stage, ra.sum_out, ra.H, row0, ra.S, col0, ra.H - col0);
+      else
+        epi_stage_store_bf16(stage, push_row, nullptr, col0, ra.H - col0);
     }
     tc_fence_before();
     mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
@@ -115,138 +142,238 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
       const RowRoute last = relay_route(mb * kBM + kBM - 1, ra.R, ra.Rk);
       for (int j = first.owner; j <= last.owner; ++j)
         red_add_release_sys(
-            flag_ptr(ra.peer_base[j], ra.flag_off + (size_t(first.tile) * ra.k + ra.rank) * 128),
+            flag_ptr(g_peer_base[j], ra.flag_off + (size_t(first.tile) * ra.k + ra.rank) * 128),
             1u);
     }
   }
 }
 
 // ---------------------------------------------------------------- relay warps
+// One thread per CTA polls the k counters of tile t (bounded); the relay warps
+// then meet at named barrier 2 and every thread performs its own acquire load
+// (already satisfied, no spinning) so its later loads are ordered after the
+// peers' releases.  Returns false (all threads) if the wait expired.
 __device__ __forceinline__ bool wait_all_sources(const RelayArgs &ra, size_t cnt_base, int t,
-                                                 uint32_t target, uint32_t code) {
-  const int lane = threadIdx.x & 31;
-  int ok = 1;
-  if (lane == 0) {
+                                                 uint32_t target, uint32_t code,
+                                                 uint64_t timeout_ns, volatile int *flag_smem) {
+  if (threadIdx.x == kRelayWarp0 * 32) {
+    int ok = 1;
     for (int src = 0; src < ra.k; ++src) {
       const uint32_t *p = flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128);
-      if (!wait_counter_geq(p, target, ra.timeout_ns)) {
+      if (!wait_counter_geq(p, target, timeout_ns)) {
         report_status(ra.status, code);
         ok = 0;
         break;
       }
     }
+    *flag_smem = ok;
   }
-  ok = __shfl_sync(0xffffffffu, ok, 0);
+  named_bar_sync(2, kRelayWarps * 32);
+  const bool ok = *flag_smem != 0;
   if (ok) {
-    // every lane performs its own acquire so its later loads are ordered
     for (int src = 0; src < ra.k; ++src)
       (void)ld_acquire_sys(flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128));
   }
-  return ok != 0;
+  named_bar_sync(2, kRelayWarps * 32);  // flag_smem may be rewritten by the next wait
+  return ok;
 }
 
-__device__ void relay_consumer(const RelayArgs &ra) {
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Residual update + RMSNorm of one row by a PAIR of relay warps (half a row each).
+// The half row stays in registers between the sum and the normalisation, so HBM is
+// read once and every load of the half row is in flight at the same time:
+//   h[c] = resid[c] + delta[c]  (delta: bf16 reduced rows, or fp32 partial in place)
+//   sum_out[c] = h[c];  x[c] = h[c] * rsqrt(mean(h^2) + eps) * gamma[c]
+// The two halves exchange their sums of squares through shared memory at the
+// pair's own named barrier (ids 3..6, 64 threads).
+constexpr int kHalfVec = 8;  // 16-byte vectors per lane per half row: H <= 2*8*256 = 4096
+
+template <bool kDeltaF32>
+__device__ __forceinline__ void pair_addnorm_row(const float *resid, const void *delta, float *sum_out,
+                                                 const __nv_bfloat16 *gamma, __nv_bfloat16 *x_out,
+                                                 int hv, float inv_h, float eps, bool do_norm,
+                                                 int pair, int half, float *pair_ss) {
   const int lane = threadIdx.x & 31;
-  const int wl = (threadIdx.x >> 5) - kRelayWarp0;   // 0..3
-  const int gw = blockIdx.x * 4 + wl;
-  const int GW = gridDim.x * 4;
+  const int hv0 = (hv + 1) / 2;                  // vectors of half 0
+  const int vbeg = half ? hv0 : 0;
+  const int vend = half ? hv : hv0;
+  float h[kHalfVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+      const float4 r0 = __ldcg(reinterpret_cast<const float4 *>(resid) + 2 * v);
+      const float4 r1 = __ldcg(reinterpret_cast<const float4 *>(resid) + 2 * v + 1);
+      h[i][0] = r0.x; h[i][1] = r0.y; h[i][2] = r0.z; h[i][3] = r0.w;
+      h[i][4] = r1.x; h[i][5] = r1.y; h[i][6] = r1.z; h[i][7] = r1.w;
+      if constexpr (kDeltaF32) {
+        const float4 d0 = __ldcg(reinterpret_cast<const float4 *>(delta) + 2 * v);
+        const float4 d1 = __ldcg(reinterpret_cast<const float4 *>(delta) + 2 * v + 1);
+        h[i][0] += d0.x; h[i][1] += d0.y; h[i][2] += d0.z; h[i][3] += d0.w;
+        h[i][4] += d1.x; h[i][5] += d1.y; h[i][6] += d1.z; h[i][7] += d1.w;
+      } else {
+        acc8_bits(h[i], __ldcg(reinterpret_cast<const uint4 *>(delta) + v));
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += h[i][e] * h[i][e];
+      reinterpret_cast<float4 *>(sum_out)[2 * v] = make_float4(h[i][0], h[i][1], h[i][2], h[i][3]);
+      reinterpret_cast<float4 *>(sum_out)[2 * v + 1] = make_float4(h[i][4], h[i][5], h[i][6], h[i][7]);
+    }
+  }
+  ss = warp_allsum(ss);
+  if (lane == 0) pair_ss[pair * 2 + half] = ss;
+  named_bar_sync(3 + pair, 64);
+  const float tot = pair_ss[pair * 2] + pair_ss[pair * 2 + 1];
+  named_bar_sync(3 + pair, 64);  // both halves read before the slots are reused
+  if (!do_norm) return;
+  const float r = rsqrtf(tot * inv_h + eps);
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+      float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      acc8_bits(g, __ldg(reinterpret_cast<const uint4 *>(gamma) + v));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[i][e] = h[i][e] * r * g[e];
+      reinterpret_cast<uint4 *>(x_out)[v] = pack8f(h[i]);
+    }
+  }
+}
+
+
+template <int KR>  // number of ranks (compile-time so the partial registers fit)
+__device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int *flag_smem,
+                                               float *pair_ss) {
+  // reduce-scatter units in flight per warp: KR partial vectors each
+  constexpr int kRsBatch = KR <= 2 ? 2 : 1;
+  const int lane = threadIdx.x & 31;
+  const int wl = (threadIdx.x >> 5) - kRelayWarp0;
+  const int gw = blockIdx.x * kRelayWarps + wl;
+  const int GW = gridDim.x * kRelayWarps;
+  const int pair = wl >> 1, half = wl & 1;
+  const int gp = blockIdx.x * (kRelayWarps / 2) + pair;
+  const int GP = gridDim.x * (kRelayWarps / 2);
   const uint32_t seq = (*ra.epoch - 1u) * uint32_t(ra.L) + uint32_t(ra.layer) + 1u;
   const uint32_t rs_target = seq * ra.rs_expect;
   const uint32_t ag_target = seq * ra.ag_expect;
   const size_t rs_cnt_base = ra.flag_off;
   const size_t ag_cnt_base = ra.flag_off + size_t(ra.T) * ra.k * 128;
   const int units = ra.Rk * ra.nseg;
+  const int hv = ra.H / 8;
   const __nv_bfloat16 *rs_local =
       reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.rs_off);
   const __nv_bfloat16 *ag_local =
       reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.ag_off);
   const float inv_h = 1.0f / float(ra.H);
   // after any earlier failure (status word set) do not wait again: give up fast
-  RelayArgs rq = ra;
-  if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) rq.timeout_ns = 0;
+  uint64_t timeout = ra.timeout_ns;
+  if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) timeout = 0;
+
+  if constexpr (KR == 1) {
+    // single rank: the fp32 partial rows of tile t sit in sum_out once the tile's
+    // GEMM tiles are released; sum_out = resid + partial in place, then RMSNorm
+    for (int t = 0; t < ra.T; ++t) {
+      const bool ok =
+          wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusLocalWait, timeout, flag_smem);
+      if (!ok) {
+        timeout = 0;
+        continue;
+      }
+      for (int q = gp; q < ra.R; q += GP) {
+        const size_t g = size_t(t) * ra.R + q;
+        pair_addnorm_row<true>(ra.resid + g * ra.H, ra.sum_out + g * ra.H, ra.sum_out + g * ra.H,
+                               ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0,
+                               pair, half, pair_ss);
+      }
+    }
+    return;
+  }
 
   for (int t = 0; t < ra.T; ++t) {
     // ---- reduce-scatter half: wait for every source's partial of my slice
-    const bool rs_ok = wait_all_sources(rq, rs_cnt_base, t, rs_target, kStatusRsWait);
-    int done = 0;
+    const bool rs_ok =
+        wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
     if (rs_ok) {
-      for (int u = gw; u < units; u += GW) {
-        const int i = u / ra.nseg;
-        const int sg = u - i * ra.nseg;
-        const int col = sg * 256 + lane * 8;
-        if (col < ra.H) {
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int src = 0; src < ra.k; ++src)
-            acc8_cg(acc, rs_local + ((size_t(t) * ra.k + src) * ra.Rk + i) * size_t(ra.H) + col);
-          const uint4 w = pack8f(acc);
-          const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
-          for (int p = 0; p < ra.k; ++p) {
-            uint4 *dst = reinterpret_cast<uint4 *>(
-                reinterpret_cast<__nv_bfloat16 *>(ra.peer_base[p] + ra.ag_off) + g * ra.H + col);
-            *dst = w;
+      for (int u0 = gw * kRsBatch; u0 < units; u0 += GW * kRsBatch) {
+        uint4 part[kRsBatch][KR];
+#pragma unroll
+        for (int b = 0; b < kRsBatch; ++b) {
+          const int u = u0 + b;
+          const int i = u / ra.nseg;
+          const int col = (u - i * ra.nseg) * 256 + lane * 8;
+          if (u < units && col < ra.H) {
+#pragma unroll
+            for (int src = 0; src < KR; ++src)
+              part[b][src] = __ldcg(reinterpret_cast<const uint4 *>(
+                  rs_local + ((size_t(t) * KR + src) * ra.Rk + i) * size_t(ra.H) + col));
           }
         }
-        ++done;
+#pragma unroll
+        for (int b = 0; b < kRsBatch; ++b) {
+          const int u = u0 + b;
+          const int i = u / ra.nseg;
+          const int col = (u - i * ra.nseg) * 256 + lane * 8;
+          if (u < units && col < ra.H) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int src = 0; src < KR; ++src) acc8_bits(acc, part[b][src]);
+            const uint4 w = pack8f(acc);
+            const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
+#pragma unroll
+            for (int p = 0; p < KR; ++p)
+              *reinterpret_cast<uint4 *>(
+                  reinterpret_cast<__nv_bfloat16 *>(g_peer_base[p] + ra.ag_off) + g * ra.H + col) = w;
+          }
+        }
       }
     }
     // ---- all-gather release: one signal per CTA and destination rank
     fence_sys();
-    named_bar_sync(2, 128);
-    if (wl == 0 && lane == 0 && rs_ok) {
+    named_bar_sync(2, kRelayWarps * 32);
+    if (threadIdx.x == kRelayWarp0 * 32 && rs_ok) {
       uint32_t cta_units = 0;
-      for (int w = 0; w < 4; ++w) {
-        const int g0 = blockIdx.x * 4 + w;
-        if (g0 < units) cta_units += uint32_t((units - 1 - g0) / GW + 1);
+      for (int w = 0; w < kRelayWarps; ++w) {
+        const int g0 = (blockIdx.x * kRelayWarps + w) * kRsBatch;
+        for (int b = 0; b < kRsBatch; ++b)
+          if (g0 + b < units) cta_units += uint32_t((units - 1 - (g0 + b)) / (GW * kRsBatch) + 1);
       }
       if (cta_units)
         for (int p = 0; p < ra.k; ++p)
           red_add_release_sys(
-              flag_ptr(ra.peer_base[p], ag_cnt_base + (size_t(t) * ra.k + ra.rank) * 128),
+              flag_ptr(g_peer_base[p], ag_cnt_base + (size_t(t) * ra.k + ra.rank) * 128),
               cta_units);
     }
-    (void)done;
     // ---- wait for every owner's reduced slice of tile t, then Add+RMSNorm
-    const bool ag_ok = wait_all_sources(rq, ag_cnt_base, t, ag_target, kStatusAgWait);
-    if (!rs_ok || !ag_ok) rq.timeout_ns = 0;
-    if (!ag_ok || !ra.do_norm) continue;
-    for (int q = gw; q < ra.R; q += GW) {
+    const bool ag_ok =
+        wait_all_sources(ra, ag_cnt_base, t, ag_target, kStatusAgWait, timeout, flag_smem);
+    if (!rs_ok || !ag_ok) timeout = 0;
+    if (!ag_ok) continue;
+    for (int q = gp; q < ra.R; q += GP) {
       const size_t g = size_t(t) * ra.R + q;
-      const float4 *hr = reinterpret_cast<const float4 *>(ra.resid + g * ra.H);
-      const __nv_bfloat16 *ar = ag_local + g * ra.H;
-      float4 *so = reinterpret_cast<float4 *>(ra.sum_out + g * ra.H);
-      float ss = 0.f;
-      for (int col = lane * 8; col < ra.H; col += 256) {
-        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        acc8_cg(a, ar + col);
-        const float4 r0 = __ldcg(hr + col / 4), r1 = __ldcg(hr + col / 4 + 1);
-        a[0] += r0.x; a[1] += r0.y; a[2] += r0.z; a[3] += r0.w;
-        a[4] += r1.x; a[5] += r1.y; a[6] += r1.z; a[7] += r1.w;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss += a[e] * a[e];
-        so[col / 4] = make_float4(a[0], a[1], a[2], a[3]);
-        so[col / 4 + 1] = make_float4(a[4], a[5], a[6], a[7]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float r = rsqrtf(ss * inv_h + ra.eps);
-      __nv_bfloat16 *xo = ra.x_out + g * ra.H;
-      for (int col = lane * 8; col < ra.H; col += 256) {
-        float gm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        acc8_cg(gm, ra.gamma + col);
-        const float4 s0 = so[col / 4], s1 = so[col / 4 + 1];
-        float a[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = a[e] * r * gm[e];
-        *reinterpret_cast<uint4 *>(xo + col) = pack8f(a);
-      }
+      pair_addnorm_row<false>(ra.resid + g * ra.H, ag_local + g * ra.H, ra.sum_out + g * ra.H,
+                              ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0,
+                              pair, half, pair_ss);
     }
   }
 }
 
-template <int BN>
+template <int BN, int KR>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
-                      const __grid_constant__ CUtensorMap tb, TileSched ts, RelayArgs ra) {
+                      const __grid_constant__ CUtensorMap tb, TileSched ts,
+                      const __grid_constant__ RelayArgs ra) {
   extern __shared__ uint8_t smem_raw[];
   const GemmSmemView<BN> s = GemmSmemView<BN>::carve(smem_raw);
   const int warp = threadIdx.x >> 5;
@@ -255,7 +382,11 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
   }
-  gemm_setup<BN>(s, 128);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < kMaxRanks; ++i) g_peer_base[i] = ra.peer_base[i];
+  }
+  gemm_setup<BN>(s, 128);  // ends with __syncthreads
   if (warp == 0) {
     if (lane == 0) gemm_producer<BN>(s, &ta, &tb, ts, ra.K, ra.status);
   } else if (warp == 1) {
@@ -263,17 +394,17 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN>(s, ts, ra);
   } else {
-    relay_consumer(ra);
+    relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch);
   }
   gemm_teardown<BN>(s);
 }
 
 // ------------------------------------------------------------------ host side
-template <int BN>
+template <int BN, int KR>
 static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, long ldb,
                          TileSched ts, const RelayArgs &ra, int grid, cudaStream_t stream) {
   using C = GemmCfg<BN>;
-  auto kern = relay_down_kernel<BN>;
+  auto kern = relay_down_kernel<BN, KR>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static bool configured[64] = {false};
@@ -313,10 +444,20 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   ts.num_n = 0;
   const CUtensorMap tma = make_tmap_2d_bf16(act, ra.S, ra.K, lda, kBM, kBK);
   const int grid = sm_count(dev);
+  auto by_ranks = [&](auto bn_tag) {
+    constexpr int B = decltype(bn_tag)::value;
+    switch (ra.k) {
+      case 1: launch_relay<B, 1>(tma, w_down, ldb, ts, ra, grid, stream); break;
+      case 2: launch_relay<B, 2>(tma, w_down, ldb, ts, ra, grid, stream); break;
+      case 4: launch_relay<B, 4>(tma, w_down, ldb, ts, ra, grid, stream); break;
+      case 8: launch_relay<B, 8>(tma, w_down, ldb, ts, ra, grid, stream); break;
+      default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
+    }
+  };
   switch (bn) {
-    case 256: launch_relay<256>(tma, w_down, ldb, ts, ra, grid, stream); break;
-    case 224: launch_relay<224>(tma, w_down, ldb, ts, ra, grid, stream); break;
-    case 128: launch_relay<128>(tma, w_down, ldb, ts, ra, grid, stream); break;
+    case 256: by_ranks(std::integral_constant<int, 256>{}); break;
+    case 224: by_ranks(std::integral_constant<int, 224>{}); break;
+    case 128: by_ranks(std::integral_constant<int, 128>{}); break;
     default: throw CudaError("relay: unsupported bn");
   }
 }

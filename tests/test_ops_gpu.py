@@ -43,6 +43,20 @@ def test_gemm(cuda, krlib, M, N, K, bn):
     _close(C, ref)
 
 
+@pytest.mark.parametrize("M,N,K,bn", [(256, 3584, 512, 224), (200, 896, 640, 256),
+                                      (384, 512, 2368, 128)])
+def test_gemm_f32_output(cuda, krlib, M, N, K, bn):
+    import torch
+    g = torch.Generator().manual_seed(M + N)
+    A = _bf(torch.randn(M, K, generator=g)).to(cuda)
+    B = _bf(torch.randn(N, K, generator=g) * 0.05).to(cuda)
+    C = krlib.gemm_f32(A, B, bn=bn)
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().T
+    # fp32 accumulate, no output rounding: far tighter than the bf16-output bound
+    _close(C, ref, rel=1e-4, abs_=1e-4)
+
+
 def test_gemm_bias_and_pitch(cuda, krlib):
     import torch
     g = torch.Generator().manual_seed(3)
@@ -206,15 +220,21 @@ def _attn_ref(qkv, S, HQ, HKV, D, scale):
     return torch.einsum("hqk,khd->qhd", p, v).reshape(S, HQ * D)
 
 
-@pytest.mark.parametrize("S,HQ,HKV,D", [(128, 4, 2, 64), (200, 4, 1, 128), (512, 8, 2, 128),
-                                        (70, 2, 2, 64)])
-def test_attention(cuda, krlib, S, HQ, HKV, D):
+@pytest.mark.parametrize("S,HQ,HKV,D,impl", [
+    (128, 4, 2, 64, 1), (200, 4, 1, 128, 1), (512, 8, 2, 128, 1), (70, 2, 2, 64, 1),
+    # tcgen05/TMEM kernel: multiples of the 128-row tile, ragged S, GQA groups, MHA
+    (128, 2, 1, 128, 2), (512, 8, 2, 128, 2), (200, 4, 1, 128, 2), (1000, 4, 4, 128, 2),
+    (2048, 28, 4, 128, 2),
+])
+def test_attention(cuda, krlib, S, HQ, HKV, D, impl):
     import torch
-    g = torch.Generator().manual_seed(S + D)
+    g = torch.Generator().manual_seed(S + D + impl)
     qkv = _bf(torch.randn(S, (HQ + 2 * HKV) * D, generator=g)).to(cuda)
     scale = 1.0 / math.sqrt(D)
-    out = krlib.attention(qkv, HQ, HKV, D, scale)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    out = krlib.attention(qkv, HQ, HKV, D, scale, impl=impl, status=status)
     torch.cuda.synchronize()
+    assert status.item() == 0
     ref = _attn_ref(qkv, S, HQ, HKV, D, scale)
     _close(out, ref, rel=2e-2, abs_=1e-2)
 
