@@ -163,14 +163,17 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ workload model
-def model_dir(cfg_name: str, seq: int, seed: int, d: Dist) -> Path:
+def model_dir(cfg_name: str, seq: int, seed: int, d: Dist, layers: int | None = None) -> Path:
     """Synthetic model directory (manifest + small tensors; large ones generated on the GPU)."""
     from kernrelay_b200 import model_gen
     root = Path(os.environ.get("KRB_MODEL_CACHE", tempfile.gettempdir())) / "krb_models"
-    out = root / f"{cfg_name}_s{seq}_seed{seed}_synth"
+    cfg = model_gen.CONFIGS[cfg_name]
+    if layers:
+        cfg = model_gen.config_with(cfg_name, L=layers)
+    out = root / f"{cfg_name}_L{cfg.L}_s{seq}_seed{seed}_synth"
     if d.rank == 0 and not (out / "manifest.json").exists():
         tmp = root / f".{out.name}.{os.getpid()}"
-        model_gen.write_model(tmp, model_gen.CONFIGS[cfg_name], seq, seed=seed, materialize=False)
+        model_gen.write_model(tmp, cfg, seq, seed=seed, materialize=False)
         os.replace(tmp, out) if not out.exists() else None
     d.barrier()
     return out
@@ -376,8 +379,10 @@ def run_ours(args, d: Dist):
             build.build()
         d.barrier()
     cfg = model_gen.CONFIGS[args.config]
+    if args.layers:
+        cfg = model_gen.config_with(args.config, L=args.layers)
     S, N = args.seq, d.world
-    mdir = model_dir(args.config, S, args.seed, d)
+    mdir = model_dir(args.config, S, args.seed, d, args.layers)
     pk = peaks()
     clocks = Clocks(d.local) if d.rank == 0 else None
     split = run_mode(d, mdir, f"tp{N}_split", S, args.tiles, args.steps, args.warmup, True, clocks)
@@ -401,7 +406,8 @@ def run_ours(args, d: Dist):
         "vs_baseline": round(toks / PUBLISHED_TOKS[N], 3) if N in PUBLISHED_TOKS else None,
         "dtype": "bf16",
         "data": "synthetic: seeded random-init weights N(0,0.02) (norms 1), uniform random token ids (seed 1234)",
-        "config": {"workload": f"{args.config} prefill S={S} batch 1, tp{N}_split tiles={args.tiles}",
+        "config": {"workload": f"{args.config} prefill S={S} batch 1, tp{N}_split tiles={args.tiles}"
+                               + (f" (PROFILING: {cfg.L} layers)" if args.layers else ""),
                    "model": "Qwen2.5-7B architecture (28 layers, H 3584, I 18944, 28/4 heads, V 152064)",
                    "global_batch": 1, "seq_len": S, "parallelism": f"tp{N} MLP (attention replicated)",
                    "mode": split["mode"], "tiles": args.tiles, "graph": True,
@@ -479,6 +485,8 @@ def main():
     ap.add_argument("--no-tp", action="store_true", help="skip the NCCL tp baseline")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: fewer decoder layers (not a valid benchmark number)")
     args = ap.parse_args()
     d = Dist()
     if args.impl == "reference":

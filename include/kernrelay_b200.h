@@ -168,6 +168,11 @@ int krb_engine_layer_dump(krb_engine *e, int on);
 /* fp32 [S, H] residual after `layer` (the last layer's entry is the pre-norm
  * final hidden state, rank 0 only) */
 int krb_engine_layer_hidden(krb_engine *e, int layer, float *out, size_t n);
+/* Relay phase trace of the last relay launch (engine built with KRB_RELAY_TRACE=1):
+ * per CTA kTraceSlots globaltimer stamps (ns) -- start, GEMM epilogue done, relay
+ * done, then per row tile: partials arrived, reduced+pushed, all-gather arrived,
+ * Add+RMSNorm done.  *written = number of values (0 when tracing is off). */
+int krb_engine_relay_trace(krb_engine *e, unsigned long long *out, size_t n, size_t *written);
 /* describe the engine: JSON {H, I, L, V, seq, world, rank, lm_rows, bn_*} */
 int krb_engine_info(krb_engine *e, char *out, size_t cap);
 

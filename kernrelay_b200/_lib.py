@@ -88,6 +88,7 @@ SIGNATURES = [
     ("krb_engine_layer_dump", c_int, [c_void_p, c_int]),
     ("krb_engine_layer_hidden", c_int, [c_void_p, c_int, c_void_p, c_size_t]),
     ("krb_engine_info", c_int, [c_void_p, c_char_p, c_size_t]),
+    ("krb_engine_relay_trace", c_int, [c_void_p, c_void_p, c_size_t, ctypes.POINTER(c_size_t)]),
 ]
 
 
@@ -371,6 +372,15 @@ class Engine:
         out = np.empty(n, dtype=np.float32)
         check(lib().krb_engine_last_logits(self.h, out.ctypes.data_as(c_void_p), n), "last_logits")
         return out
+
+    def relay_trace(self):
+        """[grid, 35] globaltimer stamps of the last relay launch (KRB_RELAY_TRACE=1)."""
+        import numpy as np
+        out = np.zeros(4096 * 35, dtype=np.uint64)
+        n = c_size_t()
+        check(lib().krb_engine_relay_trace(self.h, out.ctypes.data_as(c_void_p), out.size,
+                                           ctypes.byref(n)), "relay_trace")
+        return out[: n.value].reshape(-1, 35) if n.value else None
 
     def layer_dump(self, on=True):
         check(lib().krb_engine_layer_dump(self.h, 1 if on else 0), "layer_dump")

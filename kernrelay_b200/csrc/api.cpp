@@ -562,8 +562,8 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
     krb::relay_expectations(S, H, tiles, 1, 0, dev_bn, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
     ra.peer_base[0] = static_cast<uint8_t *>(scratch);
     ra.local_base = static_cast<uint8_t *>(scratch);
-    ra.rs_off = L.rs_off;
-    ra.ag_off = L.ag_off;
+    ra.part_off = L.part_off;
+    ra.red_off = L.red_off;
     ra.flag_off = L.flag_off;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(scratch) + L.epoch());
     ra.layer = 0;
@@ -576,6 +576,7 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
     ra.do_norm = 1;
     ra.timeout_ns = 2000000000ull;
     ra.status = status;
+    ra.trace = nullptr;
     krb::relay_down_layer(static_cast<const bf *>(act), K, static_cast<const bf *>(w_down), K, dev_bn,
                           ra, s);
     KRB_CUDA(cudaStreamSynchronize(s));
@@ -630,8 +631,8 @@ KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float tim
     ra.peer_base[0] = static_cast<uint8_t *>(mine);
     ra.peer_base[1] = static_cast<uint8_t *>(ghost);
     ra.local_base = static_cast<uint8_t *>(mine);
-    ra.rs_off = L.rs_off;
-    ra.ag_off = L.ag_off;
+    ra.part_off = L.part_off;
+    ra.red_off = L.red_off;
     ra.flag_off = L.flag_off;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(mine) + L.epoch());
     ra.layer = 0;
@@ -673,6 +674,7 @@ KRB_EXPORT int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, 
     std::ostringstream os;
     os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"num_n\":" << (H + bn - 1) / bn
        << ",\"rs_expect\":" << rs << ",\"ag_expect\":" << ag << ",\"nseg\":" << nseg
+       << ",\"direct_expect\":" << krb::relay_direct_expect(S, H, tiles, bn)
        << ",\"blocks\":[";
     for (int b = 0; b < S / 128; ++b) {
       const krb::RowRoute f = krb::relay_route(b * 128, R, Rk);
@@ -922,7 +924,8 @@ KRB_EXPORT int krb_engine_info(krb_engine *h, char *out, size_t cap) {
        << ",\"world\":" << h->e->world() << ",\"rank\":" << h->e->rank()
        << ",\"lm_rows\":" << h->e->lm_rows() << ",\"split\":" << (h->e->mode().split ? "true" : "false")
        << ",\"device\":" << h->e->device() << ",\"launches_per_run\":" << h->e->launches()
-       << ",\"graph\":" << (h->e->mode().graph ? "true" : "false") << "}";
+       << ",\"graph\":" << (h->e->mode().graph ? "true" : "false") << ",\"relay\":\""
+       << h->e->relay_kind() << "\"}";
     return write_out(os.str(), out, cap);
   } catch (const std::exception &e) {
     return write_error(e.what(), out, cap);
@@ -940,5 +943,15 @@ KRB_EXPORT int krb_engine_layer_hidden(krb_engine *h, int layer, float *out, siz
   std::vector<float> v = h->e->layer_hidden(layer);
   if (n < v.size()) throw std::runtime_error("buffer too small");
   std::memcpy(out, v.data(), v.size() * 4);
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_relay_trace(krb_engine *h, unsigned long long *out, size_t n,
+                                      size_t *written) {
+  KRB_OP_BEGIN
+  std::vector<unsigned long long> v = h->e->relay_trace();
+  if (n < v.size()) throw std::runtime_error("buffer too small");
+  if (!v.empty()) std::memcpy(out, v.data(), v.size() * 8);
+  if (written) *written = v.size();
   KRB_OP_END
 }

@@ -179,6 +179,21 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
     KRB_CUDA(cudaMalloc(&sym_, sym_layout_.bytes));
     KRB_CUDA(cudaMemset(sym_, 0, sym_layout_.bytes));
     relay_expectations(S, c.H, T, k, opts_.rank, bn_down_, &rs_expect_, &ag_expect_, &nseg_);
+    // KRB_RELAY=direct|rsag; default: direct all-pull for k <= 2, where it moves the
+    // same NVLink bytes as reduce-scatter + all-gather with one sync instead of two
+    relay_direct_ = k <= 2 ? 1 : 0;
+    if (const char *e = std::getenv("KRB_RELAY")) {
+      if (!std::strcmp(e, "direct")) relay_direct_ = 1;
+      else if (!std::strcmp(e, "rsag")) relay_direct_ = 0;
+      else throw std::runtime_error("KRB_RELAY must be direct or rsag");
+    }
+    if (relay_direct_) rs_expect_ = relay_direct_expect(S, c.H, T, bn_down_);
+    if (const char *e = std::getenv("KRB_RELAY_TRACE"))
+      if (std::atoi(e) > 0) {
+        const size_t n = size_t(sm_count(opts_.device)) * kTraceSlots;
+        trace_ = static_cast<unsigned long long *>(alloc(n * 8));
+        KRB_CUDA(cudaMemset(trace_, 0, n * 8));
+      }
     peers_.assign(k, nullptr);
     peers_[opts_.rank] = sym_;
   }
@@ -512,11 +527,12 @@ void Engine::layer(int l, StageTimes *st) {
       ra.peer_base[i] = static_cast<uint8_t *>(peers_[i]);
     }
     ra.local_base = static_cast<uint8_t *>(sym_);
-    ra.rs_off = sym_layout_.rs_off;
-    ra.ag_off = sym_layout_.ag_off;
+    ra.part_off = sym_layout_.part_off;
+    ra.red_off = sym_layout_.red_off;
     ra.flag_off = sym_layout_.flag_off;
     ra.rs_expect = rs_expect_;
     ra.ag_expect = ag_expect_;
+    ra.direct = relay_direct_;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch());
     ra.layer = l;
     ra.L = c.L;
@@ -528,6 +544,7 @@ void Engine::layer(int l, StageTimes *st) {
     ra.do_norm = do_norm ? 1 : 0;
     ra.timeout_ns = flag_timeout_ns_;
     ra.status = status_;
+    ra.trace = trace_;
     rec.begin(st ? &st->relay : nullptr);
     relay_down_layer(act_, Iloc_, w.wdown, Iloc_, bn_down_, ra, stream_);
     ++launches_;
@@ -713,6 +730,17 @@ std::vector<float> Engine::last_logits() {
 }
 
 const float *Engine::hidden_ptr() const { return hf_; }
+
+std::vector<unsigned long long> Engine::relay_trace() {
+  std::vector<unsigned long long> out;
+  if (!trace_) return out;
+  const size_t n = size_t(sm_count(opts_.device)) * kTraceSlots;
+  out.resize(n);
+  KRB_CUDA(cudaSetDevice(opts_.device));
+  KRB_CUDA(cudaStreamSynchronize(stream_));
+  KRB_CUDA(cudaMemcpy(out.data(), trace_, n * 8, cudaMemcpyDeviceToHost));
+  return out;
+}
 
 Engine::Verdict Engine::verify() {
   Verdict v;

@@ -34,7 +34,9 @@ enum EpiMode : int {
   kEpiStoreF32 = 2, // out_f32 = acc (fp32, unrounded; consumed by the residual Add+RMSNorm)
 };
 
-template <int BN>
+// RELAY selects the fused relay kernel's instantiation (same layout today; kept
+// as a separate template parameter so its budget can diverge from plain GEMMs).
+template <int BN, int RELAY = 0>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
   static constexpr int kStages = (BN >= 224) ? 4 : 6;
@@ -47,13 +49,15 @@ struct GemmCfg {
   static constexpr uint32_t kTmemCols = 2 * kAccStride;
   // epilogue staging: one 32 x 32 fp32 chunk per epilogue warp, rows padded to 36
   static constexpr uint32_t kStageRow = 36;
-  static constexpr uint32_t kEpiBytes = 4 * 32 * kStageRow * 4;
+  static constexpr uint32_t kWarpEpiBytes = 32 * kStageRow * 4;
+  static constexpr uint32_t kEpiBytes = 4 * kWarpEpiBytes;
   // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
   // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16 + 64;
   static constexpr uint32_t kSmemBytes =
       kTileBytes + kEpiBytes + kBarBytes + 1024;  // +1024 alignment slack
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct TileSched {
@@ -70,7 +74,7 @@ struct TileSched {
   }
 };
 
-template <int BN>
+template <int BN, int RELAY = 0>
 struct GemmSmemView {
   uint8_t *tiles;
   uint64_t *full;
@@ -82,7 +86,7 @@ struct GemmSmemView {
   float *epi;  // 4 x [32][kStageRow] fp32 staging chunks (epilogue warps)
   float *scratch;  // 16 floats for the relay warps
   __device__ __forceinline__ static GemmSmemView carve(uint8_t *raw) {
-    using C = GemmCfg<BN>;
+    using C = GemmCfg<BN, RELAY>;
     GemmSmemView v;
     uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) &
                                                 ~uintptr_t(1023));
@@ -102,9 +106,9 @@ struct GemmSmemView {
 
 // One-time CTA setup: barriers by thread 0, TMEM by warp 1.  Ends with
 // __syncthreads so every role sees the TMEM base address.
-template <int BN>
-__device__ __forceinline__ void gemm_setup(const GemmSmemView<BN> &s, int epi_threads) {
-  using C = GemmCfg<BN>;
+template <int BN, int RELAY = 0>
+__device__ __forceinline__ void gemm_setup(const GemmSmemView<BN, RELAY> &s, int epi_threads) {
+  using C = GemmCfg<BN, RELAY>;
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::kStages; ++i) {
@@ -127,9 +131,9 @@ __device__ __forceinline__ void gemm_setup(const GemmSmemView<BN> &s, int epi_th
   tc_fence_after();
 }
 
-template <int BN>
-__device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN> &s) {
-  using C = GemmCfg<BN>;
+template <int BN, int RELAY = 0>
+__device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN, RELAY> &s) {
+  using C = GemmCfg<BN, RELAY>;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -137,11 +141,11 @@ __device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN> &s) {
 }
 
 // ---- warp 0, one thread: TMA producer
-template <int BN>
-__device__ __forceinline__ void gemm_producer(const GemmSmemView<BN> &s, const CUtensorMap *ta,
+template <int BN, int RELAY = 0>
+__device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, const CUtensorMap *ta,
                                               const CUtensorMap *tb, const TileSched &ts, int K,
                                               uint32_t *status) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, RELAY>;
   const int nkb = (K + kBK - 1) / kBK;
   int stage = 0;
   uint32_t phase = 0;
@@ -190,10 +194,10 @@ drain:
 }
 
 // ---- warp 1, one thread: tcgen05.mma issuer
-template <int BN>
-__device__ __forceinline__ void gemm_mma(const GemmSmemView<BN> &s, const TileSched &ts, int K,
-                                         uint32_t *status) {
-  using C = GemmCfg<BN>;
+template <int BN, int RELAY = 0>
+__device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const TileSched &ts,
+                                         int K, uint32_t *status) {
+  using C = GemmCfg<BN, RELAY>;
   constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
   const uint32_t tmem = *s.tmem_slot;
   const int nkb = (K + kBK - 1) / kBK;

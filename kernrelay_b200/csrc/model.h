@@ -131,6 +131,9 @@ class Engine {
   int lm_rows() const { return lm_rows_; }
   // kernels of this library launched by the last enqueue (one prefill)
   int launches() const { return launches_; }
+  const char *relay_kind() const {
+    return mode_.split ? (relay_direct_ ? "direct" : "rsag") : "none";
+  }
   // per-op k-slice timing table (kr_qwen_profile_many)
   std::string profile_many(const std::string &spec_path);
   // dump the residual stream after every layer into host memory on the next run
@@ -191,8 +194,14 @@ class Engine {
   void *sym_ = nullptr;
   std::vector<void *> peers_;
   uint32_t rs_expect_ = 0, ag_expect_ = 0;
+  int relay_direct_ = 0;  // 1: direct all-pull relay, 0: reduce-scatter + all-gather
   int nseg_ = 0;
   uint64_t flag_timeout_ns_ = 2000000000ull;
+  unsigned long long *trace_ = nullptr;  // relay phase trace (KRB_RELAY_TRACE=1)
+ public:
+  // copy of the relay trace of the last relay launch: [grid][kTraceSlots] ns
+  std::vector<unsigned long long> relay_trace();
+ private:
 
   void *alloc(size_t bytes);
 };
@@ -200,6 +209,7 @@ class Engine {
 // relay launcher (relay.cu)
 void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w_down, long ldb,
                       int bn, const RelayArgs &ra, cudaStream_t stream);
+uint32_t relay_direct_expect(int S, int H, int T, int bn);
 void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
                         uint32_t *ag_expect, int *nseg);
 

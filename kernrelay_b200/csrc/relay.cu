@@ -6,24 +6,34 @@
 //   red_t = AllReduce_sum(down_t)        (HcclAllReduce on the comm stream)
 //   h0_t, x_t = AddRmsNorm(h1_t, red_t)  (aclnnAddRmsNorm)
 //
-// B200 design: ONE persistent cooperative kernel per layer and rank, 320 threads:
-//   warps 0..5  tcgen05 GEMM (producer, MMA, 4 push-epilogue warps) over the
-//               output tiles in row-tile order.  The epilogue stores each row of
-//               its partial tile directly into the OWNER rank's rs_buf (owner =
-//               row slice of the row tile; remote rows go over NVLink through the
-//               peer mapping), fences at system scope and releases the owner's
-//               rs_cnt[t][rank] counter (the GM-flag publish).
-//   warps 6..9  relay: for t = 0..T-1, acquire rs_cnt[t][*] (the GM-flag wait,
-//               bounded), sum the k partial slices of this rank's owned rows in
-//               fp32, round once to bf16 and push the reduced rows to every
-//               rank's ag_buf (all-gather), release ag_cnt[t][rank] on each
-//               rank; then acquire ag_cnt[t][*] and apply h0 = h1 + red,
-//               x = RMSNorm(h0) * gamma to the tile's rows.
-// The reduction of tile t and its Add+RMSNorm overlap the GEMM of later tiles.
-// No kernel ever waits on another kernel of the same GPU: the waits inside
-// this kernel target (a) other CTAs of this co-resident cooperative grid and
-// (b) the same kernel on peer GPUs.  Counters are monotone; targets are derived
-// from the run epoch and layer index, so CUDA-graph replays need no reset.
+// B200 design: ONE persistent cooperative kernel per layer and rank, 14 warps:
+//   warps 0..5   tcgen05 GEMM (TMA producer, MMA issuer, 4 epilogue warps) over
+//                the output tiles in row-tile order.  The epilogue writes the
+//                bf16 partial tile into this rank's `part` buffer (local,
+//                coalesced) and, after a CTA barrier, one thread fences at system
+//                scope and releases rs_cnt[t][rank] on every rank whose owner
+//                slice the tile touches (the GM-flag publish).
+//   warps 6..13  relay, per row tile t, one of two variants:
+//                direct (default for k <= 2): acquire rs_cnt[t][*] (the bounded
+//                GM-flag wait), then h0 = h1 + sum_src part_src (the k partial rows
+//                pulled from every rank's `part`, local or over NVLink, summed in
+//                fp32), x = RMSNorm(h0) * gamma, two warps per row, the half row
+//                held in registers.  One synchronisation per tile.
+//                rsag (k >= 4, software-pipelined): acquire rs_cnt[t][*]; PULL the
+//                k partial slices of the rows this rank owns, sum in fp32, round
+//                once, store into the local `red` buffer and release
+//                ag_cnt[t][rank] on every rank; acquire ag_cnt[t][*] and apply the
+//                Add+RMSNorm with the reduced rows pulled from each row's owner.
+//                NVLink bytes per rank and tile: direct (k-1)/k * k = k-1 tiles,
+//                rsag 2(k-1)/k tiles; equal at k = 2, where direct saves the second
+//                system-scope synchronisation (~17 us per tile measured).
+// Every region is written only by its own rank, so every system-scope fence
+// covers local stores only (a fence after remote stores costs ~5-12 us on B200
+// while the link drains; after local stores ~2 us); all NVLink traffic is loads.
+// No kernel waits on another kernel of the same GPU: the waits target other CTAs
+// of this co-resident cooperative grid and the same kernel on the peer GPUs.
+// Counters are monotone; targets derive from the run epoch and the layer, so
+// CUDA-graph replays need no reset.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -41,6 +51,10 @@ constexpr int kRelayThreads = (kRelayWarp0 + kRelayWarps) * 32;
 
 __device__ __forceinline__ uint32_t *flag_ptr(uint8_t *base, size_t off) {
   return reinterpret_cast<uint32_t *>(base + off);
+}
+
+__device__ __forceinline__ void trace_mark(const RelayArgs &ra, int slot) {
+  if (ra.trace) ra.trace[size_t(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
 }
 
 // fp32 accumulate of 8 bf16 from a 16-byte vector (L2-coherent load)
@@ -81,13 +95,15 @@ __device__ __forceinline__ uint4 pack8f(const float *f) {
 __shared__ uint8_t *g_peer_base[kMaxRanks];
 
 template <int BN>
-__device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
-                                                    const RelayArgs &ra) {
-  using C = GemmCfg<BN>;
+__device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s,
+                                                    const TileSched &ts, const RelayArgs &ra) {
+  using C = GemmCfg<BN, 1>;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quad = warp & 3;
   const uint32_t tmem = *s.tmem_slot;
+  __nv_bfloat16 *part = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.part_off);
+  float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
     int mb, nb;
@@ -104,15 +120,10 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
       break;
     }
     tc_fence_after();
-    const int row0 = mb * kBM + quad * 32;           // first row of this warp (< S)
+    const int row0 = mb * kBM + quad * 32;  // first row of this warp (< S)
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
-    float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
-    // destination row of rs_buf on the owner of global row row0 + r
-    auto push_row = [&](int r) -> __nv_bfloat16 * {
-      const RowRoute rr = relay_route(row0 + r, ra.R, ra.Rk);
-      return reinterpret_cast<__nv_bfloat16 *>(g_peer_base[rr.owner] + ra.rs_off) +
-             ((static_cast<size_t>(rr.tile) * ra.k + ra.rank) * ra.Rk + rr.local) *
-                 static_cast<size_t>(ra.H);
+    auto part_row = [&](int r) -> __nv_bfloat16 * {
+      return part + static_cast<size_t>(row0 + r) * ra.H;
     };
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
@@ -127,25 +138,29 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN> &s, c
       epi_stage_put(stage, v);
       if (ra.k == 1)
         // one rank: nothing to reduce; the fp32 partial goes straight into sum_out
-        // (store-only epilogue) and the relay warps add the residual in place
+        // and the relay warps add the residual in place
         epi_stage_store_f32(stage, ra.sum_out, ra.H, row0, ra.S, col0, ra.H - col0);
       else
-        epi_stage_store_bf16(stage, push_row, nullptr, col0, ra.H - col0);
+        epi_stage_store_bf16(stage, part_row, nullptr, col0, ra.H - col0);
     }
     tc_fence_before();
     mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
-    fence_sys();                  // this thread's pushes visible system-wide
-    named_bar_sync(1, 128);
+    named_bar_sync(1, 128);       // all four epilogue warps' stores are issued
     if (warp == 2 && lane == 0) {
-      // one release per owner whose slice this 128-row block touches
+      fence_sys();                // cumulative: orders those local stores before the release
+      // one release per owner whose slice this 128-row block touches (direct
+      // all-pull: per rank, since every rank reads every row)
       const RowRoute first = relay_route(mb * kBM, ra.R, ra.Rk);
       const RowRoute last = relay_route(mb * kBM + kBM - 1, ra.R, ra.Rk);
-      for (int j = first.owner; j <= last.owner; ++j)
+      const int j0 = ra.direct ? 0 : first.owner;
+      const int j1 = ra.direct ? ra.k - 1 : last.owner;
+      for (int j = j0; j <= j1; ++j)
         red_add_release_sys(
             flag_ptr(g_peer_base[j], ra.flag_off + (size_t(first.tile) * ra.k + ra.rank) * 128),
             1u);
     }
   }
+  if (warp == 2 && lane == 0) trace_mark(ra, 1);
 }
 
 // ---------------------------------------------------------------- relay warps
@@ -168,12 +183,12 @@ __device__ __forceinline__ bool wait_all_sources(const RelayArgs &ra, size_t cnt
     }
     *flag_smem = ok;
   }
+  // The poller's acquire loads observed every source's release; the CTA barrier
+  // orders them before the other relay threads' loads (cumulativity through the
+  // barrier, the same pattern as a cooperative grid sync).  Payload loads go to
+  // L2 (ld.global.cg), so no stale L1 line can be hit.
   named_bar_sync(2, kRelayWarps * 32);
   const bool ok = *flag_smem != 0;
-  if (ok) {
-    for (int src = 0; src < ra.k; ++src)
-      (void)ld_acquire_sys(flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128));
-  }
   named_bar_sync(2, kRelayWarps * 32);  // flag_smem may be rewritten by the next wait
   return ok;
 }
@@ -193,8 +208,12 @@ __device__ __forceinline__ float warp_allsum(float v) {
 // pair's own named barrier (ids 3..6, 64 threads).
 constexpr int kHalfVec = 8;  // 16-byte vectors per lane per half row: H <= 2*8*256 = 4096
 
-template <bool kDeltaF32>
-__device__ __forceinline__ void pair_addnorm_row(const float *resid, const void *delta, float *sum_out,
+//   kSrc = 0: delta is one fp32 row; kSrc = 1: delta is one bf16 row;
+//   kSrc >= 2: delta is the sum of the kSrc ranks' bf16 partial rows, rank s's at
+//   g_peer_base[s] + part_off, element offset part_elem (pulled over NVLink)
+template <int kSrc>
+__device__ __forceinline__ void pair_addnorm_row(const float *resid, const void *delta,
+                                                 size_t part_off, size_t part_elem, float *sum_out,
                                                  const __nv_bfloat16 *gamma, __nv_bfloat16 *x_out,
                                                  int hv, float inv_h, float eps, bool do_norm,
                                                  int pair, int half, float *pair_ss) {
@@ -212,13 +231,24 @@ __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void 
       const float4 r1 = __ldcg(reinterpret_cast<const float4 *>(resid) + 2 * v + 1);
       h[i][0] = r0.x; h[i][1] = r0.y; h[i][2] = r0.z; h[i][3] = r0.w;
       h[i][4] = r1.x; h[i][5] = r1.y; h[i][6] = r1.z; h[i][7] = r1.w;
-      if constexpr (kDeltaF32) {
+      if constexpr (kSrc == 0) {
         const float4 d0 = __ldcg(reinterpret_cast<const float4 *>(delta) + 2 * v);
         const float4 d1 = __ldcg(reinterpret_cast<const float4 *>(delta) + 2 * v + 1);
         h[i][0] += d0.x; h[i][1] += d0.y; h[i][2] += d0.z; h[i][3] += d0.w;
         h[i][4] += d1.x; h[i][5] += d1.y; h[i][6] += d1.z; h[i][7] += d1.w;
-      } else {
+      } else if constexpr (kSrc == 1) {
         acc8_bits(h[i], __ldcg(reinterpret_cast<const uint4 *>(delta) + v));
+      } else {
+        // the partials are summed in fp32 first (same association as the
+        // reduce-scatter path), then added to the residual
+        float d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int src = 0; src < kSrc; ++src)
+          acc8_bits(d, __ldcg(reinterpret_cast<const uint4 *>(
+                              reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[src] + part_off) +
+                              part_elem) + v));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[i][e] += d[e];
       }
     }
   }
@@ -257,7 +287,7 @@ template <int KR>  // number of ranks (compile-time so the partial registers fit
 __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int *flag_smem,
                                                float *pair_ss) {
   // reduce-scatter units in flight per warp: KR partial vectors each
-  constexpr int kRsBatch = KR <= 2 ? 2 : 1;
+  constexpr int kRsBatch = KR <= 2 ? 4 : (KR == 4 ? 2 : 1);
   const int lane = threadIdx.x & 31;
   const int wl = (threadIdx.x >> 5) - kRelayWarp0;
   const int gw = blockIdx.x * kRelayWarps + wl;
@@ -272,10 +302,6 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
   const size_t ag_cnt_base = ra.flag_off + size_t(ra.T) * ra.k * 128;
   const int units = ra.Rk * ra.nseg;
   const int hv = ra.H / 8;
-  const __nv_bfloat16 *rs_local =
-      reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.rs_off);
-  const __nv_bfloat16 *ag_local =
-      reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.ag_off);
   const float inv_h = 1.0f / float(ra.H);
   // after any earlier failure (status word set) do not wait again: give up fast
   uint64_t timeout = ra.timeout_ns;
@@ -287,25 +313,54 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     for (int t = 0; t < ra.T; ++t) {
       const bool ok =
           wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusLocalWait, timeout, flag_smem);
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
       if (!ok) {
         timeout = 0;
         continue;
       }
       for (int q = gp; q < ra.R; q += GP) {
         const size_t g = size_t(t) * ra.R + q;
-        pair_addnorm_row<true>(ra.resid + g * ra.H, ra.sum_out + g * ra.H, ra.sum_out + g * ra.H,
-                               ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0,
-                               pair, half, pair_ss);
+        pair_addnorm_row<0>(ra.resid + g * ra.H, ra.sum_out + g * ra.H, 0, 0, ra.sum_out + g * ra.H,
+                            ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair,
+                            half, pair_ss);
       }
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
     }
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
     return;
   }
 
-  for (int t = 0; t < ra.T; ++t) {
-    // ---- reduce-scatter half: wait for every source's partial of my slice
+  if (ra.direct) {
+    // direct all-pull: once every rank released tile t, each pair of warps sums
+    // the k partial rows (local + NVLink loads) inside its Add+RMSNorm
+    for (int t = 0; t < ra.T; ++t) {
+      const bool ok =
+          wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
+      if (!ok) {
+        timeout = 0;
+        continue;
+      }
+      for (int q = gp; q < ra.R; q += GP) {
+        const size_t g = size_t(t) * ra.R + q;
+        pair_addnorm_row<KR>(ra.resid + g * ra.H, nullptr, ra.part_off, g * ra.H,
+                             ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h,
+                             ra.eps, ra.do_norm != 0, pair, half, pair_ss);
+      }
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+    }
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
+    return;
+  }
+
+  // reduce-scatter step of tile t: wait for every source's partial of my slice,
+  // sum in fp32, round once, push the reduced rows to every rank, release ag_cnt
+  auto rs_phase = [&](int t) -> bool {
     const bool rs_ok =
         wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
     if (rs_ok) {
+      __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
       for (int u0 = gw * kRsBatch; u0 < units; u0 += GW * kRsBatch) {
         uint4 part[kRsBatch][KR];
 #pragma unroll
@@ -313,11 +368,14 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
           const int u = u0 + b;
           const int i = u / ra.nseg;
           const int col = (u - i * ra.nseg) * 256 + lane * 8;
+          const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
           if (u < units && col < ra.H) {
+            // pull: every source's partial row g (remote for src != rank)
 #pragma unroll
             for (int src = 0; src < KR; ++src)
               part[b][src] = __ldcg(reinterpret_cast<const uint4 *>(
-                  rs_local + ((size_t(t) * KR + src) * ra.Rk + i) * size_t(ra.H) + col));
+                  reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[src] + ra.part_off) +
+                  g * ra.H + col));
           }
         }
 #pragma unroll
@@ -329,20 +387,19 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int src = 0; src < KR; ++src) acc8_bits(acc, part[b][src]);
-            const uint4 w = pack8f(acc);
             const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
-#pragma unroll
-            for (int p = 0; p < KR; ++p)
-              *reinterpret_cast<uint4 *>(
-                  reinterpret_cast<__nv_bfloat16 *>(g_peer_base[p] + ra.ag_off) + g * ra.H + col) = w;
+            *reinterpret_cast<uint4 *>(red + g * ra.H + col) = pack8f(acc);
           }
         }
       }
     }
-    // ---- all-gather release: one signal per CTA and destination rank
-    fence_sys();
+    // release of my reduced rows: one signal per CTA and rank, issued by one thread
+    // after the CTA barrier (its system-scope fence is cumulative over the other
+    // relay threads' local stores that the barrier ordered before it)
     named_bar_sync(2, kRelayWarps * 32);
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 4 + 4 * t);
     if (threadIdx.x == kRelayWarp0 * 32 && rs_ok) {
+      fence_sys();
       uint32_t cta_units = 0;
       for (int w = 0; w < kRelayWarps; ++w) {
         const int g0 = (blockIdx.x * kRelayWarps + w) * kRsBatch;
@@ -350,23 +407,40 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
           if (g0 + b < units) cta_units += uint32_t((units - 1 - (g0 + b)) / (GW * kRsBatch) + 1);
       }
       if (cta_units)
-        for (int p = 0; p < ra.k; ++p)
+        for (int p = 0; p < KR; ++p)
           red_add_release_sys(
-              flag_ptr(g_peer_base[p], ag_cnt_base + (size_t(t) * ra.k + ra.rank) * 128),
+              flag_ptr(g_peer_base[p], ag_cnt_base + (size_t(t) * KR + ra.rank) * 128),
               cta_units);
     }
+    if (!rs_ok) timeout = 0;
+    return rs_ok;
+  };
+
+  // Software pipeline over the row tiles: the reduce-scatter of tile t+1 runs
+  // while the all-gather of tile t is still in flight on the other ranks.
+  bool rs_ok_next = rs_phase(0);
+  for (int t = 0; t < ra.T; ++t) {
+    const bool rs_ok = rs_ok_next;
+    if (t + 1 < ra.T) rs_ok_next = rs_phase(t + 1);
     // ---- wait for every owner's reduced slice of tile t, then Add+RMSNorm
     const bool ag_ok =
         wait_all_sources(ra, ag_cnt_base, t, ag_target, kStatusAgWait, timeout, flag_smem);
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 5 + 4 * t);
     if (!rs_ok || !ag_ok) timeout = 0;
     if (!ag_ok) continue;
     for (int q = gp; q < ra.R; q += GP) {
       const size_t g = size_t(t) * ra.R + q;
-      pair_addnorm_row<false>(ra.resid + g * ra.H, ag_local + g * ra.H, ra.sum_out + g * ra.H,
-                              ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0,
-                              pair, half, pair_ss);
+      // reduced row g lives in its owner's `red` buffer (pulled over NVLink)
+      const int owner = q / ra.Rk;
+      const __nv_bfloat16 *red_row =
+          reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[owner] + ra.red_off) + g * ra.H;
+      pair_addnorm_row<1>(ra.resid + g * ra.H, red_row, 0, 0, ra.sum_out + g * ra.H, ra.gamma,
+                          ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair, half,
+                          pair_ss);
     }
+    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
   }
+  if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
 }
 
 template <int BN, int KR>
@@ -375,7 +449,7 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
                       const __grid_constant__ CUtensorMap tb, TileSched ts,
                       const __grid_constant__ RelayArgs ra) {
   extern __shared__ uint8_t smem_raw[];
-  const GemmSmemView<BN> s = GemmSmemView<BN>::carve(smem_raw);
+  const GemmSmemView<BN, 1> s = GemmSmemView<BN, 1>::carve(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -385,25 +459,26 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int i = 0; i < kMaxRanks; ++i) g_peer_base[i] = ra.peer_base[i];
+    trace_mark(ra, 0);
   }
-  gemm_setup<BN>(s, 128);  // ends with __syncthreads
+  gemm_setup<BN, 1>(s, 128);  // ends with __syncthreads
   if (warp == 0) {
-    if (lane == 0) gemm_producer<BN>(s, &ta, &tb, ts, ra.K, ra.status);
+    if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, ts, ra.K, ra.status);
   } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN>(s, ts, ra.K, ra.status);
+    if (lane == 0) gemm_mma<BN, 1>(s, ts, ra.K, ra.status);
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN>(s, ts, ra);
   } else {
     relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch);
   }
-  gemm_teardown<BN>(s);
+  gemm_teardown<BN, 1>(s);
 }
 
 // ------------------------------------------------------------------ host side
 template <int BN, int KR>
 static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, long ldb,
                          TileSched ts, const RelayArgs &ra, int grid, cudaStream_t stream) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, 1>;
   auto kern = relay_down_kernel<BN, KR>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
@@ -466,6 +541,12 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
 // receives one rs increment per (n block, 128-row block touching its slice)
 // from every source, and one ag increment per reduced 256-column unit of each
 // owner's slice.
+// Direct all-pull: every rank receives one rs increment per (n block, 128-row
+// block of the tile) from every source.
+uint32_t relay_direct_expect(int S, int H, int T, int bn) {
+  return uint32_t(((H + bn - 1) / bn) * ((S / T) / kBM));
+}
+
 void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
                         uint32_t *ag_expect, int *nseg) {
   const int R = S / T, Rk = R / k;

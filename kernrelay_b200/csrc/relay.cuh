@@ -1,5 +1,5 @@
-// Shared definitions of the tp_split relay: symmetric buffer layout and the
-// argument block of the fused down-GEMM + reduce + all-gather + Add+RMSNorm kernel.
+// Shared definitions of the tp_split relay: row ownership, the symmetric buffer
+// layout and the argument block of the fused down-GEMM + reduce + Add+RMSNorm kernel.
 #pragma once
 
 #include <stdint.h>
@@ -18,8 +18,8 @@ constexpr int kMaxRanks = 8;
 
 // Row ownership of the tp_split relay: global row g of the S rows lies in row
 // tile rt = g / R; within the tile the rows are cut into k contiguous owner
-// slices of Rk = R / k rows.  Used by the device epilogue (where to push a
-// partial row) and by the host (expected counter increments).
+// slices of Rk = R / k rows.  Used by the device epilogue (which owners a tile's
+// release goes to) and by the host (expected counter increments).
 struct RowRoute {
   int tile, owner, local;
 };
@@ -32,24 +32,26 @@ KRB_RELAY_HD RowRoute relay_route(int g, int R, int Rk) {
   return r;
 }
 
-// Per-rank symmetric region (one allocation, mapped by every peer):
-//   rs_buf  [T][k][Rk][H] bf16   partial rows pushed by each source rank for the
-//                                 rows this rank owns (owner slice of each tile)
-//   ag_buf  [S][H] bf16           reduced rows pushed by every owner (all-gather)
-//   flags   rs_cnt[T][k], ag_cnt[T][k] u32 monotone counters, then the local
-//           run epoch counter; each counter on its own 128-byte line.
+// Per-rank symmetric region (one allocation, mapped by every peer).  All writes
+// into a region are made by its own rank; peers only READ it (pull protocol), so
+// every system-scope release covers local stores only.
+//   part   [S][H] bf16   this rank's partial down_proj output (GEMM epilogue)
+//   red    [S][H] bf16   reduced rows (sum over ranks) of the rows this rank owns
+//   flags  rs_cnt[T][k]: "source src released tile t" (incremented by the sources),
+//          ag_cnt[T][k]: "owner j released its reduced rows of tile t" (incremented
+//          by the owners), then the local run epoch; one 128-byte line each.
 struct SymLayout {
-  size_t rs_off, ag_off, flag_off, bytes;
+  size_t part_off, red_off, flag_off, bytes;
   static constexpr size_t kLine = 128;
   int T, k;
   static SymLayout make(int S, int H, int T, int k) {
     SymLayout L;
     L.T = T;
     L.k = k;
-    const size_t rows_bytes = size_t(S) * size_t(H) * 2;
-    L.rs_off = 0;
-    L.ag_off = (rows_bytes + 4095) & ~size_t(4095);
-    L.flag_off = L.ag_off + ((rows_bytes + 4095) & ~size_t(4095));
+    const size_t rows_bytes = (size_t(S) * size_t(H) * 2 + 4095) & ~size_t(4095);
+    L.part_off = 0;
+    L.red_off = rows_bytes;
+    L.flag_off = 2 * rows_bytes;
     L.bytes = L.flag_off + (2 * size_t(T) * size_t(k) + 2) * kLine;
     return L;
   }
@@ -68,9 +70,13 @@ struct RelayArgs {
   // peers' symmetric regions as seen from this GPU (index = peer rank)
   uint8_t *peer_base[kMaxRanks];
   uint8_t *local_base;
-  size_t rs_off, ag_off, flag_off;
+  size_t part_off, red_off, flag_off;
   uint32_t rs_expect;   // increments per (tile, source) per layer on the owner
   uint32_t ag_expect;   // increments per (tile, owner) per layer on every rank
+  // 1: direct all-pull (every rank sums all k partials of every row inside its
+  // Add+RMSNorm; one synchronisation per tile, (k-1) tiles over NVLink per rank);
+  // 0: reduce-scatter + all-gather (2(k-1)/k tiles over NVLink, two synchronisations)
+  int direct;
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;
   const float *resid;          // h1 [S, H] fp32 residual stream
@@ -81,6 +87,13 @@ struct RelayArgs {
   int do_norm;
   uint64_t timeout_ns;
   uint32_t *status;
+  // optional phase trace (globaltimer ns), kTraceSlots per CTA; null = off
+  unsigned long long *trace;
 };
+
+// trace slots per CTA: 0 start, 1 GEMM epilogue done, 2 relay end,
+// then per row tile t: 3+4t partials arrived, 4+4t reduced + released,
+// 5+4t reduced rows of all owners arrived, 6+4t add+norm done
+constexpr int kTraceSlots = 3 + 4 * 8;
 
 }  // namespace krb
