@@ -109,6 +109,24 @@ int krb_relay_down_single(const void *act, const void *w_down, const void *resid
                           const void *gamma, void *sum_out, void *x_out, int S, int H, int K,
                           int tiles, float eps, int bn, uint32_t *status, void *stream);
 
+/* Allocation-free form of krb_relay_down_single (same arguments, same results; no
+ * counterpart in the reference).  For callers that must not allocate device memory
+ * inside the call: a serving engine that reserved nearly all of HBM up front for
+ * its own pools, or a caller with work in flight on other streams, which the
+ * implicit device synchronisation of cudaFree would stall.  The relay's flag
+ * counters and run epoch live in a static device array of 32 KiB per device
+ * ((2 * tiles + 2) * 128 bytes are used, so tiles <= 127; more returns an error).
+ * The call zeroes them on `stream`, launches, and returns without synchronising.
+ * The first call on a device does its set-up (symbol lookup, kernel attributes)
+ * and should come before any stream capture on that device.  Calls that overlap
+ * in time on one device (different streams or threads) share the scratch and
+ * race; calls in order on one stream are safe.  k = 1 only, like
+ * krb_relay_down_single. */
+int krb_relay_down_single_noalloc(const void *act, const void *w_down, const void *resid,
+                                  const void *gamma, void *sum_out, void *x_out, int S, int H,
+                                  int K, int tiles, float eps, int bn, uint32_t *status,
+                                  void *stream);
+
 /* Failure-detection probe: runs the relay kernel as rank 0 of a two-rank job
  * whose peer never participates (its region is a second local allocation that
  * nobody signals).  Rank 0's bounded waits expire after timeout_ms; the kernel

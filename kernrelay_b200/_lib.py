@@ -64,6 +64,9 @@ SIGNATURES = [
     ("krb_relay_down_single", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_int, c_int, c_int, c_int, c_float, c_int, c_void_p,
                                       c_void_p]),
+    ("krb_relay_down_single_noalloc", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                              c_void_p, c_int, c_int, c_int, c_int, c_float,
+                                              c_int, c_void_p, c_void_p]),
     ("krb_relay_timeout_probe", c_int, [c_int, c_int, c_int, c_int, c_float, c_u32p]),
     ("krb_relay_plan", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_char_p, c_size_t]),
     ("krb_engine_create", c_int, [c_char_p, c_char_p, c_int, c_int, c_int, c_int, c_int,
@@ -245,6 +248,25 @@ def relay_down_single(act, w_down, resid, gamma, tiles, eps, bn=0, status=None, 
     check(lib().krb_relay_down_single(_ptr(act), _ptr(w_down), _ptr(resid), _ptr(gamma), _ptr(s),
                                       _ptr(x), S, H, K, tiles, eps, bn, _ptr(status),
                                       _stream(stream)), "relay_down_single")
+    return s, x
+
+
+def relay_down_single_noalloc(act, w_down, resid, gamma, tiles, eps, bn=0, status=None,
+                              stream=None, out=None):
+    """krb_relay_down_single_noalloc: same results as relay_down_single, no device
+    allocation inside the library call (asynchronous on `stream`).  `out` may
+    pass preallocated (sum fp32 [S,H], x bf16 [S,H])."""
+    import torch
+    S, K = act.shape
+    H = w_down.shape[0]
+    if out is None:
+        out = (torch.empty((S, H), dtype=torch.float32, device=act.device),
+               torch.empty((S, H), dtype=torch.bfloat16, device=act.device))
+    s, x = out
+    check(lib().krb_relay_down_single_noalloc(_ptr(act), _ptr(w_down), _ptr(resid), _ptr(gamma),
+                                              _ptr(s), _ptr(x), S, H, K, tiles, eps, bn,
+                                              _ptr(status), _stream(stream)),
+          "relay_down_single_noalloc")
     return s, x
 
 

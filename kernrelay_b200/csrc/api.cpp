@@ -591,6 +591,62 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
   }
 }
 
+// Allocation-free form of krb_relay_down_single: the relay's counters live in a
+// static device array (relay.cu), looked up once per device; nothing is allocated
+// or freed and the stream is not synchronised.
+KRB_EXPORT int krb_relay_down_single_noalloc(const void *act, const void *w_down,
+                                             const void *resid, const void *gamma, void *sum_out,
+                                             void *x_out, int S, int H, int K, int tiles,
+                                             float eps, int bn, uint32_t *status, void *stream) {
+  try {
+    if (tiles < 1 || S % tiles) throw std::runtime_error("relay: S % tiles != 0");
+    const krb::SymLayout L = krb::SymLayout::flags_only(tiles);
+    if (L.bytes > krb::kRelayNoAllocScratchBytes)
+      throw std::runtime_error("relay (no-alloc): " + std::to_string(tiles) + " row tiles need " +
+                               std::to_string(L.bytes) + " bytes of scratch; the static scratch "
+                               "holds " + std::to_string(krb::kRelayNoAllocScratchBytes) +
+                               " bytes (at most 127 row tiles)");
+    const int dev_bn = bn > 0 ? bn : 256;
+    cudaStream_t s = as_stream(stream);
+    uint8_t *scratch = krb::relay_noalloc_scratch();
+    // the counters and the epoch must start at zero; epoch = 1 for this run
+    KRB_CUDA(cudaMemsetAsync(scratch, 0, L.bytes, s));
+    krb::bump_epoch(reinterpret_cast<uint32_t *>(scratch + L.epoch()), s);
+    krb::RelayArgs ra{};
+    ra.S = S;
+    ra.H = H;
+    ra.K = K;
+    ra.T = tiles;
+    ra.k = 1;
+    ra.rank = 0;
+    ra.R = S / tiles;
+    ra.Rk = ra.R;
+    krb::relay_expectations(S, H, tiles, 1, 0, dev_bn, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.peer_base[0] = scratch;
+    ra.local_base = scratch;
+    ra.part_off = L.part_off;
+    ra.red_off = L.red_off;
+    ra.flag_off = L.flag_off;
+    ra.epoch = reinterpret_cast<const uint32_t *>(scratch + L.epoch());
+    ra.layer = 0;
+    ra.L = 1;
+    ra.resid = static_cast<const float *>(resid);
+    ra.gamma = static_cast<const bf *>(gamma);
+    ra.sum_out = static_cast<float *>(sum_out);
+    ra.x_out = static_cast<bf *>(x_out);
+    ra.eps = eps;
+    ra.do_norm = 1;
+    ra.timeout_ns = 2000000000ull;
+    ra.status = status;
+    ra.trace = nullptr;
+    krb::relay_down_layer(static_cast<const bf *>(act), K, static_cast<const bf *>(w_down), K, dev_bn,
+                          ra, s);
+    return 0;
+  } catch (const std::exception &e) {
+    return fail(e);
+  }
+}
+
 // Failure-detection probe: rank 0 of a two-rank relay whose peer never runs.
 // The "peer" region is a second local allocation nobody signals, so rank 0's
 // bounded waits for the peer's partials must expire after `timeout_ms`, set

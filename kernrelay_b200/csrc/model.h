@@ -218,6 +218,9 @@ void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_
                          cudaStream_t stream);
 void fill_const_device(__nv_bfloat16 *dst, size_t n, float value, cudaStream_t stream);
 void bump_epoch(uint32_t *epoch, cudaStream_t stream);
+// this device's static relay scratch (kRelayNoAllocScratchBytes); the first call
+// per device looks the symbol up
+uint8_t *relay_noalloc_scratch();
 void bf16_row_to_f32(const __nv_bfloat16 *src, float *dst, int n, cudaStream_t stream);
 
 }  // namespace krb

@@ -37,6 +37,8 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <mutex>
+#include <string>
 #include <type_traits>
 
 #include "common.h"
@@ -541,6 +543,32 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
 // receives one rs increment per (n block, 128-row block touching its slice)
 // from every source, and one ag increment per reduced 256-column unit of each
 // owner's slice.
+// ------------------------------------------------- allocation-free relay scratch
+// Scratch of krb_relay_down_single_noalloc: the flag counters and the run epoch
+// of a one-device relay (k = 1 needs no partial or reduced-row buffers: the fp32
+// partial tile goes straight into sum_out).  A module-scope device array exists
+// once per device, so concurrent calls on one device share it.
+static __device__ __align__(256) uint8_t g_relay_noalloc_scratch[kRelayNoAllocScratchBytes];
+
+uint8_t *relay_noalloc_scratch() {
+  static std::mutex mu;
+  static uint8_t *addr[64] = {};
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) throw CudaError("relay scratch: device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    // once per device, with that device current: look up this device's copy
+    void *p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_relay_noalloc_scratch);
+    if (rc != cudaSuccess || !p)
+      throw CudaError(std::string("cudaGetSymbolAddress(relay scratch) failed: ") +
+                      cudaGetErrorString(rc));
+    addr[dev] = static_cast<uint8_t *>(p);
+  }
+  return addr[dev];
+}
+
 // Direct all-pull: every rank receives one rs increment per (n block, 128-row
 // block of the tile) from every source.
 uint32_t relay_direct_expect(int S, int H, int T, int bn) {

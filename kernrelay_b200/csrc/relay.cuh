@@ -55,12 +55,29 @@ struct SymLayout {
     L.bytes = L.flag_off + (2 * size_t(T) * size_t(k) + 2) * kLine;
     return L;
   }
+  // counters and epoch only, at offset 0 (one-device relay: k = 1, where the
+  // partial rows go straight to sum_out and no reduced rows exist)
+  static SymLayout flags_only(int T) {
+    SymLayout L;
+    L.T = T;
+    L.k = 1;
+    L.part_off = 0;
+    L.red_off = 0;
+    L.flag_off = 0;
+    L.bytes = (2 * size_t(T) + 2) * kLine;
+    return L;
+  }
   size_t rs_cnt(int t, int src) const { return flag_off + (size_t(t) * k + src) * kLine; }
   size_t ag_cnt(int t, int src) const {
     return flag_off + (size_t(T) * k + size_t(t) * k + src) * kLine;
   }
   size_t epoch() const { return flag_off + 2 * size_t(T) * k * kLine; }
 };
+
+// Size of the static device scratch behind krb_relay_down_single_noalloc: one
+// 128-byte counter line per row tile plus the epoch lines of the flags-only
+// layout, (2 * tiles + 2) * 128 bytes, so at most 127 row tiles.
+constexpr size_t kRelayNoAllocScratchBytes = 32768;
 
 struct RelayArgs {
   int S, H, K;          // down GEMM: M = S rows, N = H, K = I/k
