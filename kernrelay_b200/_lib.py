@@ -395,14 +395,17 @@ class Engine:
         check(lib().krb_engine_last_logits(self.h, out.ctypes.data_as(c_void_p), n), "last_logits")
         return out
 
+    TRACE_SLOTS = 48  # kTraceSlots in csrc/relay.cuh
+
     def relay_trace(self):
-        """[grid, 35] globaltimer stamps of the last relay launch (KRB_RELAY_TRACE=1)."""
+        """[grid, 48] globaltimer stamps of the last relay launch (KRB_RELAY_TRACE=1);
+        slot meanings in csrc/relay.cuh (kTraceSlots)."""
         import numpy as np
-        out = np.zeros(4096 * 35, dtype=np.uint64)
+        out = np.zeros(4096 * self.TRACE_SLOTS, dtype=np.uint64)
         n = c_size_t()
         check(lib().krb_engine_relay_trace(self.h, out.ctypes.data_as(c_void_p), out.size,
                                            ctypes.byref(n)), "relay_trace")
-        return out[: n.value].reshape(-1, 35) if n.value else None
+        return out[: n.value].reshape(-1, self.TRACE_SLOTS) if n.value else None
 
     def layer_dump(self, on=True):
         check(lib().krb_engine_layer_dump(self.h, 1 if on else 0), "layer_dump")

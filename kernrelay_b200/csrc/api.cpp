@@ -684,6 +684,7 @@ KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float tim
     ra.R = S / tiles;
     ra.Rk = ra.R / k;
     krb::relay_expectations(S, H, tiles, k, 0, 256, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.done_expect = krb::relay_done_expect(S, H, tiles, 256);
     ra.peer_base[0] = static_cast<uint8_t *>(mine);
     ra.peer_base[1] = static_cast<uint8_t *>(ghost);
     ra.local_base = static_cast<uint8_t *>(mine);
@@ -730,7 +731,7 @@ KRB_EXPORT int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, 
     std::ostringstream os;
     os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"num_n\":" << (H + bn - 1) / bn
        << ",\"rs_expect\":" << rs << ",\"ag_expect\":" << ag << ",\"nseg\":" << nseg
-       << ",\"direct_expect\":" << krb::relay_direct_expect(S, H, tiles, bn)
+       << ",\"done_expect\":" << krb::relay_done_expect(S, H, tiles, bn)
        << ",\"blocks\":[";
     for (int b = 0; b < S / 128; ++b) {
       const krb::RowRoute f = krb::relay_route(b * 128, R, Rk);

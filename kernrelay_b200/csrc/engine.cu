@@ -187,7 +187,7 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
       else if (!std::strcmp(e, "rsag")) relay_direct_ = 0;
       else throw std::runtime_error("KRB_RELAY must be direct or rsag");
     }
-    if (relay_direct_) rs_expect_ = relay_direct_expect(S, c.H, T, bn_down_);
+    if (relay_direct_ && k > 4) throw std::runtime_error("direct relay supports up to 4 ranks");
     if (const char *e = std::getenv("KRB_RELAY_TRACE"))
       if (std::atoi(e) > 0) {
         const size_t n = size_t(sm_count(opts_.device)) * kTraceSlots;
@@ -532,6 +532,7 @@ void Engine::layer(int l, StageTimes *st) {
     ra.flag_off = sym_layout_.flag_off;
     ra.rs_expect = rs_expect_;
     ra.ag_expect = ag_expect_;
+    ra.done_expect = relay_done_expect(S, H, opts_.tiles, bn_down_);
     ra.direct = relay_direct_;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch());
     ra.layer = l;

@@ -209,7 +209,7 @@ class Engine {
 // relay launcher (relay.cu)
 void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w_down, long ldb,
                       int bn, const RelayArgs &ra, cudaStream_t stream);
-uint32_t relay_direct_expect(int S, int H, int T, int bn);
+uint32_t relay_done_expect(int S, int H, int T, int bn);
 void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
                         uint32_t *ag_expect, int *nseg);
 

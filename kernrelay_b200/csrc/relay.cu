@@ -28,8 +28,12 @@
 //                rsag 2(k-1)/k tiles; equal at k = 2, where direct saves the second
 //                system-scope synchronisation (~17 us per tile measured).
 // Every region is written only by its own rank, so every system-scope fence
-// covers local stores only (a fence after remote stores costs ~5-12 us on B200
-// while the link drains; after local stores ~2 us); all NVLink traffic is loads.
+// covers local stores only; all NVLink traffic is loads.  Releases are two-level:
+// GPU-scope adds into local completion counters (~1 us), and one signal thread
+// per (row tile, counter) and GPU that fences at system scope and forwards the
+// tile to every rank.  Measured on B200 under NVLink load: a system-scope fence
+// costs 12 us (k = 2) to 40 us (k = 4) when every CTA issues one, 2.5-4.5 us
+// when only the 2T signal threads do.
 // No kernel waits on another kernel of the same GPU: the waits target other CTAs
 // of this co-resident cooperative grid and the same kernel on the peer GPUs.
 // Counters are monotone; targets derive from the run epoch and the layer, so
@@ -49,7 +53,8 @@ namespace krb {
 
 constexpr int kRelayWarp0 = 6;                      // warps 0..5: GEMM roles
 constexpr int kRelayWarps = 8;                      // consumer warps per CTA
-constexpr int kRelayThreads = (kRelayWarp0 + kRelayWarps) * 32;
+constexpr int kSignalWarp = kRelayWarp0 + kRelayWarps;  // warp 14: system-scope signals
+constexpr int kRelayThreads = (kSignalWarp + 1) * 32;
 
 __device__ __forceinline__ uint32_t *flag_ptr(uint8_t *base, size_t off) {
   return reinterpret_cast<uint32_t *>(base + off);
@@ -106,6 +111,7 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
   const uint32_t tmem = *s.tmem_slot;
   __nv_bfloat16 *part = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.part_off);
   float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
+  uint64_t fence_ns = 0, fence_cnt = 0, fence_max = 0;  // trace only
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
     int mb, nb;
@@ -149,20 +155,32 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
     mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
     named_bar_sync(1, 128);       // all four epilogue warps' stores are issued
     if (warp == 2 && lane == 0) {
-      fence_sys();                // cumulative: orders those local stores before the release
-      // one release per owner whose slice this 128-row block touches (direct
-      // all-pull: per rank, since every rank reads every row)
-      const RowRoute first = relay_route(mb * kBM, ra.R, ra.Rk);
-      const RowRoute last = relay_route(mb * kBM + kBM - 1, ra.R, ra.Rk);
-      const int j0 = ra.direct ? 0 : first.owner;
-      const int j1 = ra.direct ? ra.k - 1 : last.owner;
-      for (int j = j0; j <= j1; ++j)
-        red_add_release_sys(
-            flag_ptr(g_peer_base[j], ra.flag_off + (size_t(first.tile) * ra.k + ra.rank) * 128),
-            1u);
+      const uint64_t f0 = ra.trace ? globaltimer_ns() : 0;
+      // GPU-scope release, cumulative over the four warps' stores that the named
+      // barrier ordered before it.  k = 1: straight to the consumer's counter;
+      // k > 1: into the local completion counter that the signal warp forwards.
+      const int t_row = (mb * kBM) / ra.R;
+      const size_t line = ra.k == 1
+                              ? ra.flag_off + size_t(t_row) * 128
+                              : ra.flag_off + (2 * size_t(ra.T) * ra.k + 2 + t_row) * 128;
+      red_add_release_gpu(flag_ptr(ra.local_base, line), 1u);
+      if (ra.trace) {
+        const uint64_t df = globaltimer_ns() - f0;
+        fence_ns += df;
+        fence_max = df > fence_max ? df : fence_max;
+        ++fence_cnt;
+      }
     }
   }
-  if (warp == 2 && lane == 0) trace_mark(ra, 1);
+  if (warp == 2 && lane == 0) {
+    trace_mark(ra, 1);
+    if (ra.trace) {
+      unsigned long long *tr = ra.trace + size_t(blockIdx.x) * kTraceSlots;
+      tr[43] = fence_ns;
+      tr[44] = fence_cnt;
+      tr[45] = fence_max;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- relay warps
@@ -332,27 +350,29 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     return;
   }
 
-  if (ra.direct) {
-    // direct all-pull: once every rank released tile t, each pair of warps sums
-    // the k partial rows (local + NVLink loads) inside its Add+RMSNorm
-    for (int t = 0; t < ra.T; ++t) {
-      const bool ok =
-          wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
-      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
-      if (!ok) {
-        timeout = 0;
-        continue;
+  if constexpr (KR <= 4) {  // direct all-pull is offered up to 4 ranks
+    if (ra.direct) {
+      // direct all-pull: once every rank released tile t, each pair of warps sums
+      // the k partial rows (local + NVLink loads) inside its Add+RMSNorm
+      for (int t = 0; t < ra.T; ++t) {
+        const bool ok =
+            wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
+        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
+        if (!ok) {
+          timeout = 0;
+          continue;
+        }
+        for (int q = gp; q < ra.R; q += GP) {
+          const size_t g = size_t(t) * ra.R + q;
+          pair_addnorm_row<KR>(ra.resid + g * ra.H, nullptr, ra.part_off, g * ra.H,
+                               ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h,
+                               ra.eps, ra.do_norm != 0, pair, half, pair_ss);
+        }
+        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
       }
-      for (int q = gp; q < ra.R; q += GP) {
-        const size_t g = size_t(t) * ra.R + q;
-        pair_addnorm_row<KR>(ra.resid + g * ra.H, nullptr, ra.part_off, g * ra.H,
-                             ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h,
-                             ra.eps, ra.do_norm != 0, pair, half, pair_ss);
-      }
-      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
+      return;
     }
-    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
-    return;
   }
 
   // reduce-scatter step of tile t: wait for every source's partial of my slice,
@@ -395,24 +415,15 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
         }
       }
     }
-    // release of my reduced rows: one signal per CTA and rank, issued by one thread
-    // after the CTA barrier (its system-scope fence is cumulative over the other
-    // relay threads' local stores that the barrier ordered before it)
+    // release of my reduced rows: one GPU-scope add per CTA to the local ag_done[t]
+    // by one thread after the CTA barrier (cumulative over the relay threads'
+    // stores); the signal warp forwards the completed tile to every rank
     named_bar_sync(2, kRelayWarps * 32);
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 4 + 4 * t);
     if (threadIdx.x == kRelayWarp0 * 32 && rs_ok) {
-      fence_sys();
-      uint32_t cta_units = 0;
-      for (int w = 0; w < kRelayWarps; ++w) {
-        const int g0 = (blockIdx.x * kRelayWarps + w) * kRsBatch;
-        for (int b = 0; b < kRsBatch; ++b)
-          if (g0 + b < units) cta_units += uint32_t((units - 1 - (g0 + b)) / (GW * kRsBatch) + 1);
-      }
-      if (cta_units)
-        for (int p = 0; p < KR; ++p)
-          red_add_release_sys(
-              flag_ptr(g_peer_base[p], ag_cnt_base + (size_t(t) * KR + ra.rank) * 128),
-              cta_units);
+      red_add_release_gpu(
+          flag_ptr(ra.local_base, ra.flag_off + (2 * size_t(ra.T) * KR + 2 + ra.T + t) * 128), 1u);
+      if (t < 8) trace_mark(ra, 35 + t);
     }
     if (!rs_ok) timeout = 0;
     return rs_ok;
@@ -445,6 +456,42 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
   if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
 }
 
+// ---------------------------------------------------------------- signal warp
+// k > 1: the system-scope half of the two-level release.  Job j of this GPU (one
+// per CTA j < njobs) waits until the local completion counter of its row tile is
+// complete (acquire), then fences at system scope -- cumulative over every store
+// those GPU-scope releases covered -- and adds 1 to the tile's counter on every
+// rank.  Jobs 0..T-1 forward rs_done[t] to rs_cnt[t][rank]; jobs T..2T-1 (rsag)
+// forward ag_done[t] to ag_cnt[t][rank].  Only 2T threads per GPU pay for a
+// system-scope fence, off the GEMM epilogue and the relay warps.
+__device__ __forceinline__ void relay_signal(const RelayArgs &ra) {
+  const int j = blockIdx.x;
+  const int njobs = ra.direct ? ra.T : 2 * ra.T;
+  if (ra.k == 1 || j >= njobs) return;
+  uint64_t timeout = ra.timeout_ns;
+  if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) timeout = 0;
+  const uint32_t seq = (*ra.epoch - 1u) * uint32_t(ra.L) + uint32_t(ra.layer) + 1u;
+  const bool ag = j >= ra.T;
+  const int t = ag ? j - ra.T : j;
+  const size_t tk = 2 * size_t(ra.T) * ra.k;
+  const size_t done_line = ra.flag_off + (tk + 2 + (ag ? ra.T : 0) + t) * 128;
+  const uint32_t target = seq * (ag ? uint32_t(gridDim.x) : ra.done_expect);
+  if (!wait_counter_geq(flag_ptr(ra.local_base, done_line), target, timeout)) {
+    report_status(ra.status, kStatusLocalWait);
+    return;
+  }
+  const uint64_t f0 = ra.trace ? globaltimer_ns() : 0;
+  fence_sys();
+  const size_t cnt = ra.flag_off + ((ag ? size_t(ra.T) * ra.k : 0) + size_t(t) * ra.k + ra.rank) * 128;
+  for (int p = 0; p < ra.k; ++p) red_add_relaxed_sys(flag_ptr(g_peer_base[p], cnt), 1u);
+  if (ra.trace) {
+    unsigned long long *tr = ra.trace + size_t(blockIdx.x) * kTraceSlots;
+    const uint64_t now = globaltimer_ns();
+    tr[46] = now;
+    tr[47] = now - f0;
+  }
+}
+
 template <int BN, int KR>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
@@ -470,8 +517,10 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
     if (lane == 0) gemm_mma<BN, 1>(s, ts, ra.K, ra.status);
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN>(s, ts, ra);
-  } else {
+  } else if (warp < kSignalWarp) {
     relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch);
+  } else if (lane == 0) {
+    relay_signal(ra);
   }
   gemm_teardown<BN, 1>(s);
 }
@@ -512,6 +561,7 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   if (ra.S % kBM) throw CudaError("relay: seq must be a multiple of 128");
   if (ra.R % kBM) throw CudaError("relay: rows per tile must be a multiple of 128");
   if (ra.H % 8) throw CudaError("relay: hidden must be a multiple of 8");
+  if (ra.H > 4096) throw CudaError("relay: hidden must be at most 4096");
   if (ra.k < 1 || ra.k > kMaxRanks || ra.R % ra.k) throw CudaError("relay: bad rank count");
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
@@ -521,6 +571,7 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   ts.num_n = 0;
   const CUtensorMap tma = make_tmap_2d_bf16(act, ra.S, ra.K, lda, kBM, kBK);
   const int grid = sm_count(dev);
+  if (ra.k > 1 && 2 * ra.T > grid) throw CudaError("relay: more row tiles than signal jobs");
   auto by_ranks = [&](auto bn_tag) {
     constexpr int B = decltype(bn_tag)::value;
     switch (ra.k) {
@@ -569,25 +620,22 @@ uint8_t *relay_noalloc_scratch() {
   return addr[dev];
 }
 
-// Direct all-pull: every rank receives one rs increment per (n block, 128-row
-// block of the tile) from every source.
-uint32_t relay_direct_expect(int S, int H, int T, int bn) {
+// GEMM tiles per row tile: (n blocks) x (128-row blocks of the tile).
+uint32_t relay_done_expect(int S, int H, int T, int bn) {
   return uint32_t(((H + bn - 1) / bn) * ((S / T) / kBM));
 }
 
 void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
                         uint32_t *ag_expect, int *nseg) {
-  const int R = S / T, Rk = R / k;
-  const int num_n = (H + bn - 1) / bn;
-  int touching = 0;
-  for (int b = 0; b < R / kBM; ++b) {
-    const RowRoute first = relay_route(b * kBM, R, Rk);
-    const RowRoute last = relay_route(b * kBM + kBM - 1, R, Rk);
-    if (first.owner <= rank && rank <= last.owner) ++touching;
-  }
-  *rs_expect = uint32_t(num_n * touching);
+  (void)rank;
   *nseg = (H + 255) / 256;
-  *ag_expect = uint32_t(Rk * *nseg);
+  if (k == 1) {
+    *rs_expect = relay_done_expect(S, H, T, bn);  // every GEMM tile releases directly
+    *ag_expect = 0;                               // no all-gather
+  } else {
+    *rs_expect = 1;  // one forwarded signal per (tile, source)
+    *ag_expect = 1;  // one forwarded signal per (tile, owner)
+  }
 }
 
 }  // namespace krb

@@ -39,7 +39,10 @@ KRB_RELAY_HD RowRoute relay_route(int g, int R, int Rk) {
 //   red    [S][H] bf16   reduced rows (sum over ranks) of the rows this rank owns
 //   flags  rs_cnt[T][k]: "source src released tile t" (incremented by the sources),
 //          ag_cnt[T][k]: "owner j released its reduced rows of tile t" (incremented
-//          by the owners), then the local run epoch; one 128-byte line each.
+//          by the owners), the local run epoch (+1 spare line), then the local
+//          completion counters rs_done[T] (GEMM tiles of row tile t stored) and
+//          ag_done[T] (CTAs that stored their reduced rows of tile t); one
+//          128-byte line each.
 struct SymLayout {
   size_t part_off, red_off, flag_off, bytes;
   static constexpr size_t kLine = 128;
@@ -52,7 +55,7 @@ struct SymLayout {
     L.part_off = 0;
     L.red_off = rows_bytes;
     L.flag_off = 2 * rows_bytes;
-    L.bytes = L.flag_off + (2 * size_t(T) * size_t(k) + 2) * kLine;
+    L.bytes = L.flag_off + (2 * size_t(T) * size_t(k) + 2 + 2 * size_t(T)) * kLine;
     return L;
   }
   // counters and epoch only, at offset 0 (one-device relay: k = 1, where the
@@ -72,6 +75,8 @@ struct SymLayout {
     return flag_off + (size_t(T) * k + size_t(t) * k + src) * kLine;
   }
   size_t epoch() const { return flag_off + 2 * size_t(T) * k * kLine; }
+  size_t rs_done(int t) const { return flag_off + (2 * size_t(T) * k + 2 + t) * kLine; }
+  size_t ag_done(int t) const { return flag_off + (2 * size_t(T) * k + 2 + T + t) * kLine; }
 };
 
 // Size of the static device scratch behind krb_relay_down_single_noalloc: one
@@ -88,8 +93,16 @@ struct RelayArgs {
   uint8_t *peer_base[kMaxRanks];
   uint8_t *local_base;
   size_t part_off, red_off, flag_off;
-  uint32_t rs_expect;   // increments per (tile, source) per layer on the owner
+  // Releases, per layer.  k = 1: every GEMM tile's epilogue adds 1 to rs_cnt[t][0]
+  // (rs_expect = GEMM tiles per row tile).  k > 1, two levels: each GEMM tile's
+  // epilogue adds 1 to the local rs_done[t] at GPU scope (done_expect per row
+  // tile); once it is complete, one signal thread per GPU fences at system scope
+  // and adds 1 to rs_cnt[t][rank] on every rank (rs_expect = 1); likewise every
+  // CTA adds 1 to ag_done[t] after storing its reduced rows (grid per row tile)
+  // and one signal thread forwards 1 to ag_cnt[t][rank] (ag_expect = 1).
+  uint32_t rs_expect;   // increments per (tile, source) per layer on a consumer
   uint32_t ag_expect;   // increments per (tile, owner) per layer on every rank
+  uint32_t done_expect; // GEMM tiles per row tile (k > 1: local rs_done target)
   // 1: direct all-pull (every rank sums all k partials of every row inside its
   // Add+RMSNorm; one synchronisation per tile, (k-1) tiles over NVLink per rank);
   // 0: reduce-scatter + all-gather (2(k-1)/k tiles over NVLink, two synchronisations)
@@ -109,8 +122,11 @@ struct RelayArgs {
 };
 
 // trace slots per CTA: 0 start, 1 GEMM epilogue done, 2 relay end,
-// then per row tile t: 3+4t partials arrived, 4+4t reduced + released,
-// 5+4t reduced rows of all owners arrived, 6+4t add+norm done
-constexpr int kTraceSlots = 3 + 4 * 8;
+// then per row tile t < 8: 3+4t partials arrived, 4+4t reduced rows stored,
+// 5+4t reduced rows of all owners arrived, 6+4t add+norm done;
+// 35+t: reduced rows released (local GPU-scope release);
+// 43/44/45: the epilogue's releases: total ns, count, longest ns;
+// 46: this CTA's signal job forwarded (k > 1), 47: its system-scope fence in ns
+constexpr int kTraceSlots = 48;
 
 }  // namespace krb

@@ -81,20 +81,27 @@ def test_device_count_never_fails(krlib):
                                         (512, 896, 4, 1, 256), (4096, 4096, 4, 8, 256),
                                         (2048, 2560, 2, 4, 128)])
 def test_relay_plan_counts(krlib, S, H, T, k, bn):
-    """Every source's epilogue releases exactly rs_expect increments on each owner per
-    tile, and the owners' reduced units sum to ag_expect (restated from the plan)."""
+    """Every row tile's GEMM tiles (n blocks x its 128-row blocks) complete the local
+    counter the signal warp waits for (done_expect); for k > 1 each source forwards
+    one signal per tile and owner (rs_expect = ag_expect = 1), for k = 1 the GEMM
+    tiles release the consumer directly (rs_expect = done_expect).  Every rank owns
+    a slice of every row tile, so every rank hears from every source."""
     plans = [krlib.relay_plan(S, H, T, k, r, bn) for r in range(k)]
     p0 = plans[0]
     assert p0["R"] == S // T and p0["Rk"] * k == p0["R"]
-    counts = {}
+    per_tile, owners = {}, {}
     for b, (tile, j0, j1) in enumerate(p0["blocks"]):
         assert tile == (b * 128) // p0["R"]
-        for j in range(j0, j1 + 1):
-            counts[(tile, j)] = counts.get((tile, j), 0) + p0["num_n"]
+        per_tile[tile] = per_tile.get(tile, 0) + p0["num_n"]
+        owners.setdefault(tile, set()).update(range(j0, j1 + 1))
+    for t in range(T):
+        assert per_tile[t] == p0["done_expect"], t
+        assert owners[t] == set(range(k)), t
     for j in range(k):
-        for t in range(T):
-            assert counts[(t, j)] == plans[j]["rs_expect"], (t, j)
-        assert plans[j]["ag_expect"] == p0["Rk"] * ((H + 255) // 256)
+        if k == 1:
+            assert plans[j]["rs_expect"] == p0["done_expect"] and plans[j]["ag_expect"] == 0
+        else:
+            assert plans[j]["rs_expect"] == 1 and plans[j]["ag_expect"] == 1
 
 
 def test_relay_plan_rejects_bad_shapes(krlib):

@@ -50,14 +50,23 @@ def _run_all(engines, fn):
 
 
 @pytest.mark.parametrize("k", [2, 4, 8])
-@pytest.mark.parametrize("split", [True, False])
-def test_tp_engines_match_oracle(cuda, krlib, tiny, k, split):
+@pytest.mark.parametrize("variant", ["direct", "rsag", "nccl"])
+def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
+    """variant: the split relay's direct all-pull or reduce-scatter + all-gather
+    form (KRB_RELAY, read at engine creation), or the NCCL tp baseline."""
     if _ngpu() < k:
         pytest.skip(f"needs {k} GPUs")
+    if variant == "direct" and k > 4:
+        pytest.skip("the direct relay is offered up to 4 ranks")
     d, ref, cfg = tiny
+    split = variant != "nccl"
     mode = f"tp{k}_split" if split else f"tp{k}"
+    if split:
+        monkeypatch.setenv("KRB_RELAY", variant)
     engines = [krlib.Engine(d, mode, 512, rank=r, world=k, device=r, tiles=4) for r in range(k)]
     try:
+        if split:
+            assert engines[0].info()["relay"] == variant
         if split:
             krlib.Engine.link(engines)
         else:
