@@ -112,9 +112,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const AttnSmem sm = carve(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nqb = gridDim.x;
-  const int qb = nqb - 1 - blockIdx.x;  // heaviest (longest causal row) first
-  const int h = blockIdx.y;
+  // grid (HQ, q tiles): blocks are dispatched x-fastest, so every head's longest
+  // causal row tile goes first and the shortest last (longest-processing-time
+  // order over the whole grid, not per head)
+  const int nqb = gridDim.y;
+  const int qb = nqb - 1 - blockIdx.y;
+  const int h = blockIdx.x;
   const int kvh = h / group;
   const int q0 = qb * kTileRows;
   const int nkb = min(qb + 1, (S + kTileRows - 1) / kTileRows);
@@ -341,7 +344,7 @@ void attention_tc_bf16(const __nv_bfloat16 *qkv, const __nv_bfloat16 *vt, long l
                                   int(kAttnSmemBytes)));
     configured[dev & 63] = true;
   }
-  dim3 grid((S + kTileRows - 1) / kTileRows, HQ);
+  dim3 grid(HQ, (S + kTileRows - 1) / kTileRows);
   attn_tc_kernel<<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(
       tm_qk, tm_vt, out, static_cast<long>(HQ) * D, S, HQ, HQ / HKV,
       scale * 1.4426950408889634f, status);

@@ -117,27 +117,30 @@ __device__ __forceinline__ void store8(float *p, long v, const float *f) {
   q[1] = make_float4(f[4], f[5], f[6], f[7]);
 }
 
-// One warp per row; NV = max 8-element vectors per lane (H <= NV*256).
-//   s = a (+ b)            a: residual (fp32 or bf16), b: bf16 delta or null
+// One CTA per row, blockDim = 32 * ceil(hv / 128): every lane owns at most kNormVec
+// 8-element vectors, so all of a row's loads are in flight at once (HBM-bound).
+//   s = a (+ b)            a: residual (fp32 or bf16), b: bf16/fp32 delta or null
 //   sum_f <- s (fp32, unrounded)   or   sum_b <- bf16(s) and the norm uses bf16(s)
 //   y = s * rsqrt(mean(s^2) + eps) * gamma  (bf16)
 // With a bf16 sum the norm is taken over the rounded value, as the stored
 // bf16 residual is what later layers see (aclnnAddRmsNorm semantics).
-template <int NV, typename TA, typename TB>
+constexpr int kNormVec = 4;
+
+template <typename TA, typename TB>
 __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restrict__ b,
                                    const uint4 *__restrict__ gamma, uint4 *__restrict__ y,
                                    float *__restrict__ rstd, float *__restrict__ sum_f,
-                                   uint4 *__restrict__ sum_b, int rows, int hv, float inv_h,
-                                   float eps) {
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+                                   uint4 *__restrict__ sum_b, int hv, float inv_h, float eps) {
+  __shared__ float part[32];
+  const int row = blockIdx.x;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  const int warp = threadIdx.x >> 5;
   const long base = static_cast<long>(row) * hv;
-  float x[NV][8];
+  float x[kNormVec][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = lane + i * 32;
+  for (int i = 0; i < kNormVec; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
     if (v < hv) {
       load8(a, base + v, x[i]);
       if (b) {
@@ -146,6 +149,12 @@ __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restric
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[i][e] += t[e];
       }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kNormVec; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < hv) {
       if (sum_b) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[i][e] = bf16_round(x[i][e]);
@@ -157,11 +166,16 @@ __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restric
     }
   }
   ss = warp_sum(ss);
-  const float r = rsqrtf(ss * inv_h + eps);
-  if (rstd && lane == 0) rstd[row] = r;
+  if (lane == 0) part[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) tot += part[w];
+  const float r = rsqrtf(tot * inv_h + eps);
+  if (rstd && threadIdx.x == 0) rstd[row] = r;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int v = lane + i * 32;
+  for (int i = 0; i < kNormVec; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
     if (v < hv) {
       float g[8];
       unpack8(__ldg(gamma + v), g);
@@ -177,23 +191,16 @@ static void launch_add_rmsnorm(const TA *a, const TB *b, const __nv_bfloat16 *ga
                                __nv_bfloat16 *y, float *rstd, float *sum_f, __nv_bfloat16 *sum_b,
                                int rows, int H, float eps, cudaStream_t stream) {
   if (H % 8) throw CudaError("rmsnorm: H % 8 != 0");
+  if (rows <= 0) throw CudaError("rmsnorm: no rows");
   const int hv = H / 8;
-  const int threads = 128;
-  const int blocks = (rows * 32 + threads - 1) / threads;
+  const int warps = (hv + 32 * kNormVec - 1) / (32 * kNormVec);
+  if (warps > 32) throw CudaError("rmsnorm: H too large");
   const auto *g4 = reinterpret_cast<const uint4 *>(gamma);
   auto *y4 = reinterpret_cast<uint4 *>(y);
   auto *s4 = reinterpret_cast<uint4 *>(sum_b);
   const float inv_h = 1.0f / float(H);
-  if (hv <= 4 * 32)
-    add_rmsnorm_kernel<4, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
-  else if (hv <= 8 * 32)
-    add_rmsnorm_kernel<8, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
-  else if (hv <= 16 * 32)
-    add_rmsnorm_kernel<16, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
-  else if (hv <= 32 * 32)
-    add_rmsnorm_kernel<32, TA, TB><<<blocks, threads, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, rows, hv, inv_h, eps);
-  else
-    throw CudaError("rmsnorm: H too large");
+  add_rmsnorm_kernel<TA, TB><<<rows, warps * 32, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, hv,
+                                                              inv_h, eps);
   KRB_CUDA(cudaGetLastError());
 }
 
@@ -235,55 +242,66 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int 
                                     const __nv_bfloat16 *__restrict__ sin_tab,
                                     const __nv_bfloat16 *__restrict__ q_norm,
                                     const __nv_bfloat16 *__restrict__ k_norm, float eps) {
+  // one thread per 8 rotation pairs: elements j..j+7 of the first half and
+  // HALF+j..HALF+j+7 of the second, 16-byte loads and stores; the head's
+  // kLanes = HALF/8 threads are consecutive lanes of one warp
   constexpr int HALF = D / 2;
-  constexpr int PER = HALF / 32;  // pairs per lane
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  constexpr int kLanes = HALF / 8;
+  const long gt = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nh = HQ + HKV;
-  if (gw >= S * nh) return;
-  const int s = gw / nh;
-  const int h = gw - s * nh;
+  const long head = gt / kLanes;
+  const int j = static_cast<int>(gt % kLanes) * 8;
+  if (head >= static_cast<long>(S) * nh) return;  // whole heads only: warp-uniform per head
+  const int s = static_cast<int>(head / nh);
+  const int h = static_cast<int>(head - static_cast<long>(s) * nh);
   __nv_bfloat16 *p = qkv + (static_cast<long>(s) * (HQ + 2 * HKV) + h) * D;
   const __nv_bfloat16 *nw = (h < HQ) ? q_norm : k_norm;
-  float lo[PER], hi[PER];
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    lo[i] = __bfloat162float(p[lane + 32 * i]);
-    hi[i] = __bfloat162float(p[HALF + lane + 32 * i]);
-  }
+  float lo[8], hi[8];
+  unpack8(*reinterpret_cast<const uint4 *>(p + j), lo);
+  unpack8(*reinterpret_cast<const uint4 *>(p + HALF + j), hi);
+  const long trow = static_cast<long>(s) * D;
+  float c0[8], s0[8], c1[8], s1[8];
+  unpack8(__ldg(reinterpret_cast<const uint4 *>(cos_tab + trow + j)), c0);
+  unpack8(__ldg(reinterpret_cast<const uint4 *>(sin_tab + trow + j)), s0);
+  unpack8(__ldg(reinterpret_cast<const uint4 *>(cos_tab + trow + HALF + j)), c1);
+  unpack8(__ldg(reinterpret_cast<const uint4 *>(sin_tab + trow + HALF + j)), s1);
   if (nw) {
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) ss += lo[i] * lo[i] + hi[i] * hi[i];
-    ss = warp_sum(ss);
-    const float r = rsqrtf(ss / float(D) + eps);
+    for (int e = 0; e < 8; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
+    // the head's kLanes lanes (all active or all returned together)
+    const unsigned lane = threadIdx.x & 31;
+    const unsigned mask = ((1u << kLanes) - 1u) << (lane & ~unsigned(kLanes - 1));
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
+    for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(mask, ss, o);
+    const float r = rsqrtf(ss / float(D) + eps);
+    float wl[8], wh[8];
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(nw + j)), wl);
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(nw + HALF + j)), wh);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
       // HF RMSNorm returns bf16 before RoPE: keep that rounding point
-      lo[i] = bf16_round(lo[i] * r * __bfloat162float(nw[lane + 32 * i]));
-      hi[i] = bf16_round(hi[i] * r * __bfloat162float(nw[HALF + lane + 32 * i]));
+      lo[e] = bf16_round(lo[e] * r * wl[e]);
+      hi[e] = bf16_round(hi[e] * r * wh[e]);
     }
   }
-  const __nv_bfloat16 *cr = cos_tab + static_cast<long>(s) * D;
-  const __nv_bfloat16 *sr = sin_tab + static_cast<long>(s) * D;
+  float olo[8], ohi[8];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int j = lane + 32 * i;
-    const float c0 = __bfloat162float(cr[j]), s0 = __bfloat162float(sr[j]);
-    const float c1 = __bfloat162float(cr[HALF + j]), s1 = __bfloat162float(sr[HALF + j]);
-    const float a = lo[i], b = hi[i];
-    p[j] = __float2bfloat16_rn(a * c0 - b * s0);
-    p[HALF + j] = __float2bfloat16_rn(b * c1 + a * s1);
+  for (int e = 0; e < 8; ++e) {
+    olo[e] = lo[e] * c0[e] - hi[e] * s0[e];
+    ohi[e] = hi[e] * c1[e] + lo[e] * s1[e];
   }
+  *reinterpret_cast<uint4 *>(p + j) = pack8(olo);
+  *reinterpret_cast<uint4 *>(p + HALF + j) = pack8(ohi);
 }
 
 void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
                        const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
                        const __nv_bfloat16 *q_norm, const __nv_bfloat16 *k_norm, float eps,
                        cudaStream_t stream) {
-  const long warps = static_cast<long>(S) * (HQ + HKV);
+  const long threads_total = static_cast<long>(S) * (HQ + HKV) * (D / 16);
   const int threads = 256;
-  const long blocks = (warps * 32 + threads - 1) / threads;
+  const long blocks = (threads_total + threads - 1) / threads;
   switch (D) {
     case 64:
       qk_norm_rope_kernel<64><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab, sin_tab,
