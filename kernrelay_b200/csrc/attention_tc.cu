@@ -102,6 +102,19 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 2^x with the MUFU.EX2 instruction (flush-to-zero; the probabilities are rounded
+// to bf16 right after, so its ~2 ulp fp32 error is far below that rounding)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// the running max is only moved (and O rescaled) when a row's max grew by more
+// than 2^8: until then P = 2^(s - m_stale) <= 256 stays exact enough in bf16 and
+// O and the row sum carry the same stale max, so O / l is unchanged
+constexpr float kRescaleLog2 = 8.0f;
+
 }  // namespace
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -238,27 +251,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int c = 0; c < 128; ++c)
           if (key0 + c > row || key0 + c >= S) s[c] = -INFINITY;
       }
-      float mx = m_run;
+      // row max with eight independent chains (scale_log2 > 0 commutes with max)
+      float m8[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c] * scale_log2);
-      const float alpha = exp2f(m_run - mx);  // 0 on the first block
+      for (int e = 0; e < 8; ++e) m8[e] = s[e];
+#pragma unroll
+      for (int c = 8; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
+      const bool grow = mx - m_run > kRescaleLog2;  // true on the first block (m_run = -inf)
+      const float m_use = grow ? mx : m_run;
+      const float alpha = grow ? ex2_approx(m_run - mx) : 1.f;  // 0 on the first block
       uint32_t p[64];
-      float rs = 0.f;
+      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float p0 = exp2f(s[2 * c] * scale_log2 - mx);
-        const float p1 = exp2f(s[2 * c + 1] * scale_log2 - mx);
+        const float p0 = ex2_approx(fmaf(s[2 * c], scale_log2, -m_use));
+        const float p1 = ex2_approx(fmaf(s[2 * c + 1], scale_log2, -m_use));
         p[c] = pack_bf16x2(p0, p1);
-        const float2 f = unpack_bf16x2(p[c]);
-        rs += f.x + f.y;
+        // the row sum uses the rounded probabilities that the PV product sees
+        r8[c & 7] += __uint_as_float(p[c] << 16) + __uint_as_float(p[c] & 0xffff0000u);
       }
+      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       l_run = l_run * alpha + rs;
       if (j > 0) {
         // PV_{j-1} must be complete before O is rescaled and P is overwritten
         ok = mbar_wait(sm.o_done, (j - 1) & 1, kMbarLimitNs);
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, mx > m_run)) {
+        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
@@ -270,7 +291,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
       }
-      m_run = mx;
+      m_run = m_use;
       {
         uint32_t lo[32], hi[32];
 #pragma unroll
