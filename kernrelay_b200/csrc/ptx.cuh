@@ -87,6 +87,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
   }
 }
 
+// ---------------------------------------------------------------- bulk copies
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar`
+// (transaction bytes).  src and dst 16-byte aligned, bytes a multiple of 16.  The
+// source may be a peer GPU's memory (NVLink); plain per-CTA form only.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// orders this thread's later async-proxy (bulk copy) accesses after the
+// generic-proxy accesses it has observed (e.g. data released by another GPU)
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

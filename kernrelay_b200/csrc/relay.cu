@@ -41,6 +41,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -303,9 +304,84 @@ __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void 
 }
 
 
+// Bulk-staged form of pair_addnorm_row: the pair's leader has issued one bulk
+// copy of the row's bf16 delta into shared memory (`stage`, completing on `bar`
+// with parity `phase`); meanwhile the 64 threads load the residual (and, for the
+// direct relay, this rank's own partial row) with ordinary loads.
+//   kLocalPart = false: delta = stage                      (reduced row of the owner)
+//   kLocalPart = true:  delta = local_part + stage          (k = 2: both partials,
+//                       summed first, so every rank forms the same fp32 value)
+// Returns false if the copy did not complete within limit_ns (the row is then
+// left unwritten; the pair still meets at its barriers).
+template <bool kLocalPart>
+__device__ __forceinline__ bool pair_addnorm_row_staged(
+    const float *resid, const __nv_bfloat16 *local_part, const uint4 *stage, uint64_t *bar,
+    uint32_t phase, uint64_t limit_ns, float *sum_out, const __nv_bfloat16 *gamma,
+    __nv_bfloat16 *x_out, int hv, float inv_h, float eps, bool do_norm, int pair, int half,
+    float *pair_ss) {
+  const int lane = threadIdx.x & 31;
+  const int hv0 = (hv + 1) / 2;
+  const int vbeg = half ? hv0 : 0;
+  const int vend = half ? hv : hv0;
+  float h[kHalfVec][8];
+  uint4 lp[kLocalPart ? kHalfVec : 1];
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+      const float4 r0 = __ldcg(reinterpret_cast<const float4 *>(resid) + 2 * v);
+      const float4 r1 = __ldcg(reinterpret_cast<const float4 *>(resid) + 2 * v + 1);
+      h[i][0] = r0.x; h[i][1] = r0.y; h[i][2] = r0.z; h[i][3] = r0.w;
+      h[i][4] = r1.x; h[i][5] = r1.y; h[i][6] = r1.z; h[i][7] = r1.w;
+      if constexpr (kLocalPart) lp[i] = __ldcg(reinterpret_cast<const uint4 *>(local_part) + v);
+    }
+  }
+  const bool ok = mbar_wait(bar, phase, limit_ns);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+      float d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if constexpr (kLocalPart) acc8_bits(d, lp[i]);
+      if (ok) acc8_bits(d, stage[v]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        h[i][e] += d[e];
+        ss += h[i][e] * h[i][e];
+      }
+      if (ok) {
+        reinterpret_cast<float4 *>(sum_out)[2 * v] = make_float4(h[i][0], h[i][1], h[i][2], h[i][3]);
+        reinterpret_cast<float4 *>(sum_out)[2 * v + 1] =
+            make_float4(h[i][4], h[i][5], h[i][6], h[i][7]);
+      }
+    }
+  }
+  ss = warp_allsum(ss);
+  if (lane == 0) pair_ss[pair * 2 + half] = ss;
+  // pair-uniform outcome; also: every thread is done reading `stage`
+  const bool pair_ok = named_bar_and(3 + pair, 64, ok);
+  const float tot = pair_ss[pair * 2] + pair_ss[pair * 2 + 1];
+  named_bar_sync(3 + pair, 64);
+  if (!do_norm || !pair_ok) return pair_ok;
+  const float r = rsqrtf(tot * inv_h + eps);
+#pragma unroll
+  for (int i = 0; i < kHalfVec; ++i) {
+    const int v = vbeg + lane + 32 * i;
+    if (v < vend) {
+      float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      acc8_bits(g, __ldg(reinterpret_cast<const uint4 *>(gamma) + v));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[i][e] = h[i][e] * r * g[e];
+      reinterpret_cast<uint4 *>(x_out)[v] = pack8f(h[i]);
+    }
+  }
+  return pair_ok;
+}
+
 template <int KR>  // number of ranks (compile-time so the partial registers fit)
 __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int *flag_smem,
-                                               float *pair_ss) {
+                                               float *pair_ss, uint8_t *stage_base) {
   // reduce-scatter units in flight per warp: KR partial vectors each
   constexpr int kRsBatch = KR <= 2 ? 4 : (KR == 4 ? 2 : 1);
   const int lane = threadIdx.x & 31;
@@ -326,6 +402,24 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
   // after any earlier failure (status word set) do not wait again: give up fast
   uint64_t timeout = ra.timeout_ns;
   if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) timeout = 0;
+  // bulk staging (ra.bulk): one H-element bf16 row buffer and one mbarrier per pair;
+  // the pair's leader issues the copies, all 64 threads wait on the mbarrier
+  const bool leader = half == 0 && lane == 0;
+  uint8_t *pbuf = ra.bulk ? stage_base + size_t(pair) * ra.H * 2 : nullptr;
+  uint64_t *pbar =
+      ra.bulk ? reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) * ra.H * 2) + pair
+              : nullptr;
+  uint32_t phase = 0;
+  bool stuck = false;  // a copy did not complete in time: no new copies, drain at exit
+  auto stage_fail = [&]() {
+    if (!stuck) report_status(ra.status, kStatusRsWait);
+    stuck = true;
+    timeout = 0;
+  };
+  auto drain = [&]() {
+    // no bulk copy may still be writing this CTA's shared memory when it exits
+    if (ra.bulk && stuck && leader) mbar_wait(pbar, phase, ra.timeout_ns);
+  };
 
   if constexpr (KR == 1) {
     // single rank: the fp32 partial rows of tile t sit in sum_out once the tile's
@@ -348,6 +442,46 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     }
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
     return;
+  }
+
+  if constexpr (KR == 2) {
+    if (ra.direct && ra.bulk) {
+      // direct all-pull with bulk staging: the peer's partial row arrives by one
+      // bulk copy while the pair loads the residual and this rank's partial
+      const int peer = 1 - ra.rank;
+      const __nv_bfloat16 *mine = reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.part_off);
+      const uint8_t *theirs = g_peer_base[peer] + ra.part_off;
+      for (int t = 0; t < ra.T; ++t) {
+        const bool ok =
+            wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
+        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
+        if (!ok || stuck) {
+          timeout = 0;
+          continue;
+        }
+        if (leader) fence_proxy_async_global();
+        for (int q = gp; q < ra.R; q += GP) {
+          const size_t g = size_t(t) * ra.R + q;
+          if (leader) {
+            mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
+            bulk_load(pbuf, theirs + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
+          }
+          const bool rok = pair_addnorm_row_staged<true>(
+              ra.resid + g * ra.H, mine + g * ra.H, reinterpret_cast<const uint4 *>(pbuf), pbar,
+              phase, ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv,
+              inv_h, ra.eps, ra.do_norm != 0, pair, half, pair_ss);
+          if (!rok) {
+            stage_fail();
+            break;
+          }
+          phase ^= 1;
+        }
+        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+      }
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
+      drain();
+      return;
+    }
   }
 
   if constexpr (KR <= 4) {  // direct all-pull is offered up to 4 ranks
@@ -381,7 +515,46 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     const bool rs_ok =
         wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
-    if (rs_ok) {
+    if (rs_ok && ra.bulk && !stuck) {
+      // unit = (owned row i, column segment seg of W = H/k columns): the leader
+      // stages the k sources' segments (k bulk copies, source order) in the pair
+      // buffer; the pair sums them in fp32 in that order and stores the bf16 row
+      __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
+      const int W = ra.H / KR;
+      const uint32_t seg_bytes = uint32_t(W) * 2;
+      const int wv = W / 8;
+      const int tid = half * 32 + lane;
+      const int nunits = ra.Rk * KR;
+      if (leader) fence_proxy_async_global();
+      for (int u = gp; u < nunits; u += GP) {
+        const int i = u / KR, seg = u - i * KR;
+        const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
+        const size_t off = (g * ra.H + size_t(seg) * W) * 2;
+        if (leader) {
+          mbar_arrive_expect_tx(pbar, seg_bytes * KR);
+#pragma unroll
+          for (int src = 0; src < KR; ++src)
+            bulk_load(pbuf + src * seg_bytes, g_peer_base[src] + ra.part_off + off, seg_bytes, pbar);
+        }
+        const bool uok = mbar_wait(pbar, phase, ra.timeout_ns);
+        if (uok) {
+          const uint4 *sv = reinterpret_cast<const uint4 *>(pbuf);
+          for (int v = tid; v < wv; v += 64) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int src = 0; src < KR; ++src) acc8_bits(acc, sv[src * wv + v]);
+            reinterpret_cast<uint4 *>(red + g * ra.H + size_t(seg) * W)[v] = pack8f(acc);
+          }
+        }
+        // pair-uniform outcome, and every thread is done reading the buffer
+        const bool all_ok = named_bar_and(3 + pair, 64, uok);
+        if (!all_ok) {
+          stage_fail();
+          break;
+        }
+        phase ^= 1;
+      }
+    } else if (rs_ok) {
       __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
       for (int u0 = gw * kRsBatch; u0 < units; u0 += GW * kRsBatch) {
         uint4 part[kRsBatch][KR];
@@ -420,7 +593,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     // stores); the signal warp forwards the completed tile to every rank
     named_bar_sync(2, kRelayWarps * 32);
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 4 + 4 * t);
-    if (threadIdx.x == kRelayWarp0 * 32 && rs_ok) {
+    if (threadIdx.x == kRelayWarp0 * 32 && rs_ok && !stuck) {
       red_add_release_gpu(
           flag_ptr(ra.local_base, ra.flag_off + (2 * size_t(ra.T) * KR + 2 + ra.T + t) * 128), 1u);
       if (t < 8) trace_mark(ra, 35 + t);
@@ -441,6 +614,29 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 5 + 4 * t);
     if (!rs_ok || !ag_ok) timeout = 0;
     if (!ag_ok) continue;
+    if (ra.bulk) {
+      if (stuck) continue;
+      if (leader) fence_proxy_async_global();
+      for (int q = gp; q < ra.R; q += GP) {
+        const size_t g = size_t(t) * ra.R + q;
+        const int owner = q / ra.Rk;
+        if (leader) {
+          mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
+          bulk_load(pbuf, g_peer_base[owner] + ra.red_off + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
+        }
+        const bool rok = pair_addnorm_row_staged<false>(
+            ra.resid + g * ra.H, nullptr, reinterpret_cast<const uint4 *>(pbuf), pbar, phase,
+            ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps,
+            ra.do_norm != 0, pair, half, pair_ss);
+        if (!rok) {
+          stage_fail();
+          break;
+        }
+        phase ^= 1;
+      }
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+      continue;
+    }
     for (int q = gp; q < ra.R; q += GP) {
       const size_t g = size_t(t) * ra.R + q;
       // reduced row g lives in its owner's `red` buffer (pulled over NVLink)
@@ -454,6 +650,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
   }
   if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
+  drain();
 }
 
 // ---------------------------------------------------------------- signal warp
@@ -505,12 +702,19 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
   }
+  // relay staging: kRelayWarps/2 pair buffers of H bf16, then their mbarriers
+  using C = GemmCfg<BN, 1>;
+  uint8_t *stage_base = s.tiles + ((C::kTileBytes + C::kEpiBytes + C::kBarBytes + 127) & ~127u);
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int i = 0; i < kMaxRanks; ++i) g_peer_base[i] = ra.peer_base[i];
     trace_mark(ra, 0);
+    if (ra.bulk) {
+      uint64_t *bars = reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) * ra.H * 2);
+      for (int i = 0; i < kRelayWarps / 2; ++i) mbar_init(&bars[i], 1);
+    }
   }
-  gemm_setup<BN, 1>(s, 128);  // ends with __syncthreads
+  gemm_setup<BN, 1>(s, 128);  // its barrier-init fence and __syncthreads cover the above
   if (warp == 0) {
     if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, ts, ra.K, ra.status);
   } else if (warp == 1) {
@@ -518,7 +722,7 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN>(s, ts, ra);
   } else if (warp < kSignalWarp) {
-    relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch);
+    relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch, stage_base);
   } else if (lane == 0) {
     relay_signal(ra);
   }
@@ -526,19 +730,49 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
+
+// dynamic shared memory of the relay kernel: the GEMM pipeline, plus (bulk) the
+// pair row buffers and their mbarriers behind it
+template <int BN>
+static size_t relay_smem_bytes(int H, bool bulk) {
+  using C = GemmCfg<BN, 1>;
+  if (!bulk) return C::kSmemBytes;
+  return C::kSmemBytes + 128 + size_t(kRelayWarps / 2) * H * 2 + (kRelayWarps / 2) * 8;
+}
+
+// Bulk staging needs the row buffers to fit next to the GEMM pipeline (within the
+// opt-in dynamic shared memory left beside the kernel's static shared memory) and
+// every copy to be 16-byte aligned: rows (H bf16) and, for the reduce-scatter
+// units, segments of H/k columns.
+template <int BN>
+static bool relay_bulk_fits(int H, int k, size_t dyn_limit) {
+  if (relay_smem_bytes<BN>(H, true) > dyn_limit) return false;
+  if ((H * 2) % 16) return false;
+  if (k > 1 && (H % k || (H / k) % 8)) return false;
+  return true;
+}
+
 template <int BN, int KR>
 static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, long ldb,
-                         TileSched ts, const RelayArgs &ra, int grid, cudaStream_t stream) {
-  using C = GemmCfg<BN, 1>;
+                         TileSched ts, const RelayArgs &ra_in, bool want_bulk, int grid,
+                         cudaStream_t stream) {
   auto kern = relay_down_kernel<BN, KR>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
-  static bool configured[64] = {false};
-  if (!configured[dev & 63]) {
-    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(C::kSmemBytes)));
-    configured[dev & 63] = true;
+  static size_t dyn_limit[64] = {0};
+  if (!dyn_limit[dev & 63]) {
+    int optin = 0;
+    KRB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    cudaFuncAttributes fa{};
+    KRB_CUDA(cudaFuncGetAttributes(&fa, kern));
+    const size_t lim = size_t(optin) - fa.sharedSizeBytes;
+    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(lim)));
+    dyn_limit[dev & 63] = lim;
   }
+  RelayArgs ra = ra_in;
+  ra.bulk = (want_bulk && relay_bulk_fits<BN>(ra.H, ra.k, dyn_limit[dev & 63])) ? 1 : 0;
+  const size_t smem = relay_smem_bytes<BN>(ra.H, ra.bulk != 0);
+  if (smem > dyn_limit[dev & 63]) throw CudaError("relay: shared memory budget exceeded");
   const CUtensorMap tmb = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, BN, kBK);
   ts.num_n = (ra.H + BN - 1) / BN;
   // cooperative: every CTA must be co-resident, because the relay warps wait
@@ -546,7 +780,7 @@ static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, lo
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kRelayThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
@@ -574,11 +808,18 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   if (ra.k > 1 && 2 * ra.T > grid) throw CudaError("relay: more row tiles than signal jobs");
   auto by_ranks = [&](auto bn_tag) {
     constexpr int B = decltype(bn_tag)::value;
+    // bulk staging serves the exchange paths: reduce-scatter + all-gather, and the
+    // direct relay at k = 2 (one remote row per row); KRB_RELAY_BULK=0 turns it off
+    static const bool bulk_env = [] {
+      const char *e = std::getenv("KRB_RELAY_BULK");
+      return !(e && e[0] == '0');
+    }();
+    const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
     switch (ra.k) {
-      case 1: launch_relay<B, 1>(tma, w_down, ldb, ts, ra, grid, stream); break;
-      case 2: launch_relay<B, 2>(tma, w_down, ldb, ts, ra, grid, stream); break;
-      case 4: launch_relay<B, 4>(tma, w_down, ldb, ts, ra, grid, stream); break;
-      case 8: launch_relay<B, 8>(tma, w_down, ldb, ts, ra, grid, stream); break;
+      case 1: launch_relay<B, 1>(tma, w_down, ldb, ts, ra, false, grid, stream); break;
+      case 2: launch_relay<B, 2>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+      case 4: launch_relay<B, 4>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+      case 8: launch_relay<B, 8>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
       default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
     }
   };

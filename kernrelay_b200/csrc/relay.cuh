@@ -107,6 +107,9 @@ struct RelayArgs {
   // Add+RMSNorm; one synchronisation per tile, (k-1) tiles over NVLink per rank);
   // 0: reduce-scatter + all-gather (2(k-1)/k tiles over NVLink, two synchronisations)
   int direct;
+  // 1: the relay warps stage remote rows in shared memory with bulk copies (set
+  // by the launcher when the shared-memory budget and the alignment allow it)
+  int bulk;
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;
   const float *resid;          // h1 [S, H] fp32 residual stream
