@@ -113,6 +113,25 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, to share the softmax's exponentials with the MUFU unit:
+// Cody-Waite style range reduction x = n + f, n = round(x) (by the 1.5*2^23
+// shift), f in [-1/2, 1/2], and a cubic for 2^f fitted here by weighted least
+// squares for relative error on Chebyshev nodes (max relative error 2.2e-4,
+// a tenth of the bf16 rounding the probabilities get next); n is added to the
+// exponent field.  x < -125 gives exactly 0 (masked scores are -inf).
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -125.0f);
+  const float t = xc + 12582912.0f;  // 1.5 * 2^23: round(xc) in the low mantissa bits
+  const float n = t - 12582912.0f;
+  const float f = xc - n;
+  const float p = fmaf(fmaf(fmaf(0.05286743491888046f, f, 0.2421518862247467f), f,
+                            0.6935867667198181f),
+                       f, 0.9999627470970154f);
+  const int e = (__float_as_int(t) - __float_as_int(12582912.0f)) << 23;
+  const float r = __int_as_float(__float_as_int(p) + e);
+  return x < -125.0f ? 0.0f : r;
+}
+
 // the running max is only moved (and O rescaled) when a row's max grew by more
 // than 2^8: until then P = 2^(s - m_stale) <= 256 stays exact enough in bf16 and
 // O and the row sum carry the same stale max, so O / l is unchanged
@@ -222,8 +241,10 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
         s0 = ((key > row) | (key >= S)) ? -INFINITY : s0;
         s1 = ((key + 1 > row) | (key + 1 >= S)) ? -INFINITY : s1;
       }
-      const float p0 = ex2_approx(fmaf(s0, scale_log2, -m_use));
-      const float p1 = ex2_approx(fmaf(s1, scale_log2, -m_use));
+      // half of the pairs on MUFU.EX2, half on the FMA pipe (balances the two units)
+      const float a0 = fmaf(s0, scale_log2, -m_use), a1 = fmaf(s1, scale_log2, -m_use);
+      const float p0 = (e & 1) ? exp2_poly(a0) : ex2_approx(a0);
+      const float p1 = (e & 1) ? exp2_poly(a1) : ex2_approx(a1);
       pk[e] = pack_bf16x2(p0, p1);
       // the row sum uses the rounded probabilities that the PV product sees
       r8[e & 7] += __uint_as_float(pk[e] << 16) + __uint_as_float(pk[e] & 0xffff0000u);
@@ -320,36 +341,54 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       // ---------------- MMA issuer
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
-      bool ok = mbar_wait(sm.q_full, 0, kMbarLimitNs);
+      // descriptors of every smem tile, computed once; k-step kk of a tile is the
+      // base descriptor plus the step's byte offset >> 4 in the start-address field
+      // (all offsets stay inside the 14-bit field: shared memory < 256 KB)
+      const uint64_t dq0 = tile_desc(sm.q, 0), dq1 = tile_desc(sm.q + kTileBytes, 0);
+      const uint64_t dk0 = tile_desc(sm.q + 2 * kTileBytes, 0), dk1 = tile_desc(sm.q + 3 * kTileBytes, 0);
+      const uint64_t dv0 = tile_desc(sm.q + 4 * kTileBytes, 0), dv1 = tile_desc(sm.q + 5 * kTileBytes, 0);
+      auto kstep = [](int kk) -> uint64_t {
+        return static_cast<uint64_t>(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+      };
+      // issue order per key block j: PV(A,j), QK(A,j+1), PV(B,j), QK(B,j+1) -- tile
+      // A's next scores are computed while tile B's softmax runs and vice versa
+      // (ping-pong).  QK(x,j+1) overwrites the TMEM columns that hold P_x(j), so it
+      // waits until PV(x,j) has completed.
+      auto issue_qk = [&](int x, int jj) {
+        tc_fence_after();
+        const uint32_t sacc = tmem + 256 * x;
+        const uint64_t qd = x ? dq1 : dq0, kd = (jj & 1) ? dk1 : dk0;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_bf16(sacc, qd + kstep(kk), kd + kstep(kk), idesc_s, kk > 0);
+        umma_commit(&sm.s_full[x]);
+      };
+      bool ok = mbar_wait(sm.q_full, 0, kMbarLimitNs) &&
+                mbar_wait(&sm.kv_full[0], 0, kMbarLimitNs);
+      if (ok) {
+        issue_qk(0, 0);
+        if (nB > 0) issue_qk(1, 0);
+      }
       for (int j = 0; j < nkb && ok; ++j) {
         const int st = j & 1;
-        ok = mbar_wait(&sm.kv_full[st], (j >> 1) & 1, kMbarLimitNs);
-        if (!ok) break;
-        const uint8_t *kst = sm.q + (2 + st) * kTileBytes;
-        const uint8_t *vst = sm.q + (4 + st) * kTileBytes;
+        if (j + 1 < nkb) ok = mbar_wait(&sm.kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, kMbarLimitNs);
         for (int x = 0; x < 2 && ok; ++x) {
-          if (j >= (x ? nB : nA)) continue;
-          // S_x is free once PV(x, j-1) has read P_x
-          if (j > 0) ok = mbar_wait(&sm.o_done[x], (j - 1) & 1, kMbarLimitNs);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t sacc = tmem + 256 * x;
-          const uint8_t *qx = sm.q + x * kTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_bf16(sacc, tile_desc(qx, kk), tile_desc(kst, kk), idesc_s, kk > 0);
-          umma_commit(&sm.s_full[x]);
-        }
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (j >= (x ? nB : nA)) continue;
+          const int nx = x ? nB : nA;
+          if (j >= nx) continue;
           ok = mbar_wait(&sm.p_ready[x], j & 1, kMbarLimitNs);
           if (!ok) break;
           tc_fence_after();
+          const uint64_t vd = st ? dv1 : dv0;
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_bf16_ts(tmem + 256 * x + 128, tmem + 256 * x + kk * 8, tile_desc(vst, kk), idesc_o,
+            umma_bf16_ts(tmem + 256 * x + 128, tmem + 256 * x + kk * 8, vd + kstep(kk), idesc_o,
                          (j > 0 || kk > 0));
           umma_commit(&sm.o_done[x]);
+          if (j + 1 < nx) {
+            ok = mbar_wait(&sm.o_done[x], j & 1, kMbarLimitNs);
+            if (!ok) break;
+            issue_qk(x, j + 1);
+          }
         }
         if (ok) umma_commit(&sm.kv_empty[st]);
       }
