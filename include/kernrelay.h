@@ -41,8 +41,13 @@ int kr_plan_run(const char *schedule_json, int iters, int warmup, const char *de
 int kr_qwen_run(const char *model_dir, const char *mode, int seq, int device, int warmup,
                 int iters, char *out, size_t out_cap);
 
-/* Two-stage pipeline-parallel prefill (PP=2).  mode: "pp" | "pp_serial".
- * Replaces kr_qwen_pp_run (include/kernrelay.h:45-47). */
+/* Two-stage pipeline-parallel prefill (PP=2).  mode: "pp" | "pp1" (requests overlap
+ * across the stages) | "pp_serial" | "pp1_serial" (stage 0 starts request r after
+ * stage 1 finished r-1).  Stage 0 on dev0 runs layers [0, L/2), stage 1 on dev1
+ * layers [L/2, L) and the logits; requests 1..8.  Result JSON: mode (pp_pipeline |
+ * pp_serial), seq, requests, devices, layers, wall_best_us, wall_typical_us,
+ * wall_samples_us, stages[2] (stage 1 carries argmax / maxdiff).
+ * Replaces kr_qwen_pp_run (include/kernrelay.h:45-47, qwen_main.cpp:1993-2146). */
 int kr_qwen_pp_run(const char *model_dir, const char *mode, int seq, int dev0, int dev1,
                    int requests, int warmup, int iters, char *out, size_t out_cap);
 

@@ -200,18 +200,140 @@ KRB_EXPORT int kr_qwen_run(const char *model_dir, const char *mode, int seq, int
   }
 }
 
+// PP=2 layer pipeline (qwen_main.cpp:1359-1528 BuildPP, 1993-2146 RunQwenPP):
+// stage 0 on dev0 runs embed + layers [0, L/2), stage 1 on dev1 layers [L/2, L) +
+// final norm + lm_head.  Per request r the stage-0 residual stream (fp32 [S, H])
+// crosses NVLink by one peer copy into stage 1's receive buffer r; a cross-device
+// event orders stage 1 after the copy (the reference's HcclSend/HcclRecv).
+// "pp"/"pp1": all requests are enqueued back to back, so stage 0 computes request
+// r+1 while stage 1 computes request r; "pp_serial"/"pp1_serial": stage 0 starts
+// request r only after stage 1 finished request r-1 (the no-overlap baseline).
+// Both stages are driven from this thread (stage 0 then stage 1 per request), so
+// every cross-device wait refers to the current iteration's record.
 KRB_EXPORT int kr_qwen_pp_run(const char *model_dir, const char *mode, int seq, int dev0,
                               int dev1, int requests, int warmup, int iters, char *out,
                               size_t out_cap) {
-  (void)model_dir;
-  (void)mode;
-  (void)seq;
-  (void)dev0;
-  (void)dev1;
-  (void)requests;
-  (void)warmup;
-  (void)iters;
-  return write_error("pp modes are not built in the B200 library", out, out_cap);
+  std::vector<void *> recv;
+  std::vector<cudaEvent_t> ev_sent, ev_done;
+  std::unique_ptr<krb::Engine> eng[2];
+  auto cleanup = [&] {
+    for (auto &e : ev_sent) if (e) cudaEventDestroy(e);
+    for (auto &e : ev_done) if (e) cudaEventDestroy(e);
+    if (!recv.empty()) {
+      cudaSetDevice(dev1);
+      for (void *p : recv) if (p) cudaFree(p);
+    }
+    recv.clear();
+    ev_sent.clear();
+    ev_done.clear();
+    eng[0].reset();
+    eng[1].reset();
+  };
+  try {
+    if (!model_dir || !*model_dir) throw std::runtime_error("model path required");
+    const std::string mname = mode ? mode : "pp";
+    const krb::Mode m = krb::Mode::parse(mname);
+    if (!m.pp) throw std::runtime_error("kr_qwen_pp_run needs a pp mode (pp, pp_serial, pp1, pp1_serial)");
+    if (dev1 < 0 || dev1 == dev0) throw std::runtime_error("--device2 must be a different device");
+    if (requests < 1 || requests > 8) throw std::runtime_error("--requests must be in 1..8");
+    int ndev = 0;
+    KRB_CUDA(cudaGetDeviceCount(&ndev));
+    if (dev0 < 0 || dev0 >= ndev || dev1 >= ndev) throw std::runtime_error("device not present");
+    const int devs[2] = {dev0, dev1};
+    for (int i = 0; i < 2; ++i) {
+      int can = 0;
+      KRB_CUDA(cudaDeviceCanAccessPeer(&can, devs[i], devs[1 - i]));
+      if (!can) throw std::runtime_error("no peer access between the two devices");
+      KRB_CUDA(cudaSetDevice(devs[i]));
+      cudaError_t r = cudaDeviceEnablePeerAccess(devs[1 - i], 0);
+      if (r == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else KRB_CUDA(r);
+    }
+    {
+      std::string errs[2];
+      std::vector<std::thread> th;
+      for (int st = 0; st < 2; ++st)
+        th.emplace_back([&, st] {
+          try {
+            krb::EngineOpts o;
+            o.model_dir = model_dir;
+            o.mode = mname;
+            o.seq = seq;
+            o.device = devs[st];
+            o.pp_stage = st;
+            o.pp_stages = 2;
+            eng[st] = std::make_unique<krb::Engine>(o);
+          } catch (const std::exception &ex) {
+            errs[st] = ex.what();
+          }
+        });
+      for (auto &t : th) t.join();
+      for (int st = 0; st < 2; ++st)
+        if (!errs[st].empty()) throw std::runtime_error("stage" + std::to_string(st) + ": " + errs[st]);
+    }
+    const size_t bytes = size_t(seq) * eng[0]->cfg().H * 4;
+    recv.assign(requests, nullptr);
+    ev_sent.assign(requests, nullptr);
+    ev_done.assign(requests, nullptr);
+    KRB_CUDA(cudaSetDevice(dev1));
+    for (int r = 0; r < requests; ++r) {
+      KRB_CUDA(cudaMalloc(&recv[r], bytes));
+      KRB_CUDA(cudaEventCreateWithFlags(&ev_done[r], cudaEventDisableTiming));
+    }
+    KRB_CUDA(cudaSetDevice(dev0));
+    for (int r = 0; r < requests; ++r)
+      KRB_CUDA(cudaEventCreateWithFlags(&ev_sent[r], cudaEventDisableTiming));
+    krb::Engine &s0 = *eng[0];
+    krb::Engine &s1 = *eng[1];
+    auto iteration = [&] {
+      for (int r = 0; r < requests; ++r) {
+        KRB_CUDA(cudaSetDevice(dev0));
+        if (!m.pp_pipeline && r > 0) KRB_CUDA(cudaStreamWaitEvent(s0.stream(), ev_done[r - 1], 0));
+        s0.enqueue_stage(nullptr);
+        KRB_CUDA(cudaMemcpyPeerAsync(recv[r], dev1, s0.residual_out(), dev0, bytes, s0.stream()));
+        KRB_CUDA(cudaEventRecord(ev_sent[r], s0.stream()));
+        KRB_CUDA(cudaSetDevice(dev1));
+        KRB_CUDA(cudaStreamWaitEvent(s1.stream(), ev_sent[r], 0));
+        s1.enqueue_stage(static_cast<const float *>(recv[r]));
+        KRB_CUDA(cudaEventRecord(ev_done[r], s1.stream()));
+      }
+      s0.sync();
+      s1.sync();
+    };
+    // first run (correctness, outside the timing), warm-up, timed iterations
+    iteration();
+    krb::Engine::Verdict v = s1.verify();
+    for (int w = 0; w < warmup; ++w) iteration();
+    std::vector<double> wall;
+    for (int i = 0; i < std::max(1, iters); ++i) {
+      const auto t0 = Clock::now();
+      iteration();
+      wall.push_back(us_between(t0, Clock::now()));
+    }
+    v = s1.verify();
+    uint32_t st0 = s0.read_status(), st1 = s1.read_status();
+    if (st0 || st1)
+      throw std::runtime_error("device status " + std::to_string(st0) + "/" + std::to_string(st1));
+    const krb::Engine::Verdict none;
+    const std::string j0 = stage_json(s0, "pp_stage0", warmup, iters, wall, {}, none, st0, 0);
+    const std::string j1 = stage_json(s1, "pp_stage1", warmup, iters, wall, {}, v, st1, 0);
+    double best, typ;
+    stats(wall, &best, &typ);
+    std::ostringstream os;
+    os << "{\"mode\":\"" << (m.pp_pipeline ? "pp_pipeline" : "pp_serial") << "\",\"seq\":" << seq
+       << ",\"requests\":" << requests << ",\"devices\":[" << dev0 << "," << dev1 << "]"
+       << ",\"layers\":[[" << s0.layer_begin() << "," << s0.layer_end() << "],["
+       << s1.layer_begin() << "," << s1.layer_end() << "]]"
+       << ",\"wall_best_us\":" << fmt(best) << ",\"wall_typical_us\":" << fmt(typ)
+       << ",\"wall_samples_us\":" << samples_json(wall) << ",\"stages\":[" << j0 << "," << j1
+       << "]}";
+    cleanup();
+    return write_out(os.str(), out, out_cap);
+  } catch (const std::exception &ex) {
+    cudaDeviceSynchronize();
+    cleanup();
+    return write_error(ex.what(), out, out_cap);
+  }
 }
 
 namespace {

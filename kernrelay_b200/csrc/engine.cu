@@ -99,6 +99,11 @@ Mode Mode::parse(const std::string &name) {
   } else if (name == "relay_flag_graph") {
     m.split = true;
     m.graph = true;
+  } else if (name == "pp" || name == "pp1" || name == "pp_serial" || name == "pp1_serial") {
+    // PP=2 (qwen_main.cpp:1359-1528, 1993-2146): "pp"/"pp1" overlap the requests
+    // across the stages, "pp_serial"/"pp1_serial" run them one after another
+    m.pp = true;
+    m.pp_pipeline = name == "pp" || name == "pp1";
   } else if (name.rfind("tp", 0) == 0) {
     // tp{k}[_split][_graph]; "tp" alone means k=2 as in the reference's tp2
     std::string rest = name.substr(2);
@@ -157,6 +162,15 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
     flag_timeout_ns_ = uint64_t(std::max(1.0, std::atof(e)) * 1e6);
   Iloc_ = c.I / opts_.world;
   nqkv_ = (c.HQ + 2 * c.HKV) * c.D;
+  layer_begin_ = 0;
+  layer_end_ = c.L;
+  if (mode_.pp) {
+    // stage s of n runs layers [s*L/n, (s+1)*L/n) (qwen_main.cpp:746-747)
+    if (opts_.pp_stages < 2 || opts_.pp_stage < 0 || opts_.pp_stage >= opts_.pp_stages)
+      throw std::runtime_error("pp: bad stage");
+    layer_begin_ = opts_.pp_stage * c.L / opts_.pp_stages;
+    layer_end_ = (opts_.pp_stage + 1) * c.L / opts_.pp_stages;
+  }
   const int sms = sm_count(opts_.device);
   bn_gu_ = pick_bn_silu(opts_.seq, Iloc_, sms);
   const int half = bn_gu_ / 2;
@@ -279,6 +293,13 @@ void Engine::load_weights() {
   for (int l = 0; l < c.L; ++l) {
     const std::string p = layer_prefix(l);
     LayerW &w = lw_[l];
+    if (l < layer_begin_ || l >= layer_end_) {
+      // another pipeline stage's layer: only its input norm (the last layer of a
+      // stage normalises with the next layer's ln1)
+      w.ln1 = A(H);
+      copy_into(p + "input_layernorm.weight", w.ln1);
+      continue;
+    }
     // fused QKV [nq + 2 nkv, H] K-major from q/k/v weight_t [H, n]
     w.wqkv = A(size_t(nqkv_) * H);
     const std::string roles[3] = {"q_proj", "k_proj", "v_proj"};
@@ -334,8 +355,9 @@ void Engine::load_weights() {
   }
   embed_ = A(size_t(c.V) * H);
   copy_into("embed.weight", embed_);
-  // rank != 0 produces no logits: no lm_head / final norm (reference :1206-1208)
-  if (r == 0) {
+  // only the logits engine (TP rank 0 of the last stage) keeps lm_head / final norm
+  // (reference :1206-1208)
+  if (has_logits()) {
     final_norm_ = A(H);
     copy_into("final_norm.weight", final_norm_);
     const TensorSpec &lm = m_.at("lm_head.weight_t");
@@ -378,7 +400,7 @@ void Engine::alloc_activations() {
   hf_ = F(S * H);
   delta_ = F(S * H);
   xf_ = A(S * H);
-  if (opts_.rank == 0) logits_ = A(size_t(lm_rows_) * size_t(c.V));
+  if (has_logits()) logits_ = A(size_t(lm_rows_) * size_t(c.V));
   last_f32_ = static_cast<float *>(alloc(size_t(c.V) * 4));
   // tcgen05 attention for head_dim 128 (KRB_ATTN=mma selects the mma.sync kernel)
   const char *ae = std::getenv("KRB_ATTN");
@@ -584,7 +606,7 @@ void Engine::layer(int l, StageTimes *st) {
 }
 
 void Engine::epilogue(StageTimes *st) {
-  if (opts_.rank != 0) return;
+  if (!has_logits()) return;
   const ModelCfg &c = m_.cfg;
   StageRec rec(stream_, st, g_events);
   ++launches_;
@@ -595,12 +617,24 @@ void Engine::epilogue(StageTimes *st) {
   rec.end();
 }
 
-void Engine::enqueue() {
+void Engine::enqueue() { enqueue_stage(nullptr); }
+
+void Engine::enqueue_stage(const float *h_in) {
   KRB_CUDA(cudaSetDevice(opts_.device));
   launches_ = 0;
-  prologue(nullptr);
   const size_t SH = size_t(opts_.seq) * m_.cfg.H;
-  for (int l = 0; l < m_.cfg.L; ++l) {
+  if (layer_begin_ == 0) {
+    prologue(nullptr);
+  } else {
+    // later pipeline stage: the previous stage's residual stream, then this stage's
+    // first input norm (qwen_main.cpp:1459-1465)
+    if (!h_in) throw std::runtime_error("pp: stage input missing");
+    KRB_CUDA(cudaMemcpyAsync(h0_, h_in, SH * 4, cudaMemcpyDeviceToDevice, stream_));
+    add_rmsnorm_res_f32(h0_, static_cast<const float *>(nullptr), lw_[layer_begin_].ln1, x_,
+                        nullptr, opts_.seq, m_.cfg.H, float(m_.cfg.eps), stream_);
+    launches_ += 1;
+  }
+  for (int l = layer_begin_; l < layer_end_; ++l) {
     layer(l, nullptr);
     if (dump_) {
       const bool last = (l + 1 == m_.cfg.L);
@@ -636,7 +670,7 @@ void Engine::enqueue_host(const int64_t *ids_host, float *last_logits_host) {
   KRB_CUDA(cudaSetDevice(opts_.device));
   KRB_CUDA(cudaMemcpyAsync(ids_, ids_host, size_t(opts_.seq) * 8, cudaMemcpyHostToDevice, stream_));
   run();
-  if (opts_.rank == 0 && last_logits_host) {
+  if (has_logits() && last_logits_host) {
     const ModelCfg &c = m_.cfg;
     bf16_row_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
     KRB_CUDA(cudaMemcpyAsync(last_logits_host, last_f32_, size_t(c.V) * 4, cudaMemcpyDeviceToHost,
@@ -684,6 +718,7 @@ uint32_t Engine::read_status() {
 }
 
 StageTimes Engine::instrumented_run() {
+  if (mode_.pp) throw std::runtime_error("stage times are not available in pp modes");
   KRB_CUDA(cudaSetDevice(opts_.device));
   std::vector<std::pair<double *, std::pair<cudaEvent_t, cudaEvent_t>>> events;
   g_events = &events;
@@ -721,7 +756,7 @@ StageTimes Engine::instrumented_run() {
 std::vector<float> Engine::last_logits() {
   const ModelCfg &c = m_.cfg;
   std::vector<float> out;
-  if (opts_.rank != 0) return out;
+  if (!has_logits()) return out;
   KRB_CUDA(cudaSetDevice(opts_.device));
   bf16_row_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
   out.resize(c.V);
@@ -745,7 +780,7 @@ std::vector<unsigned long long> Engine::relay_trace() {
 
 Engine::Verdict Engine::verify() {
   Verdict v;
-  if (opts_.rank != 0) return v;
+  if (!has_logits()) return v;
   const std::vector<float> got = last_logits();
   const int V = m_.cfg.V;
   float best = -INFINITY;

@@ -67,6 +67,8 @@ struct Mode {
   bool split = false;   // row-tile relay (fused kernel) instead of GEMM + AllReduce
   bool graph = false;   // capture the prefill into a CUDA graph and replay it
   bool fused = true;    // Add+RMSNorm fused (serial = unfused add then norm)
+  bool pp = false;      // pp*: layer pipeline over two devices (one stage per engine)
+  bool pp_pipeline = false;  // pp / pp1: requests overlap across the stages
   static Mode parse(const std::string &name);
 };
 
@@ -79,6 +81,8 @@ struct EngineOpts {
   int device = 0;
   int tiles = 4;
   int lm_rows = -1;   // -1: all S rows (reference); 1: last row only
+  int pp_stage = 0;   // pp modes: this engine's stage and the number of stages
+  int pp_stages = 1;
 };
 
 // Per-stage device time accumulated by an instrumented run (microseconds).
@@ -131,6 +135,15 @@ class Engine {
   int lm_rows() const { return lm_rows_; }
   // kernels of this library launched by the last enqueue (one prefill)
   int launches() const { return launches_; }
+  // layers [layer_begin, layer_end) run on this engine (all of them except in pp modes)
+  int layer_begin() const { return layer_begin_; }
+  int layer_end() const { return layer_end_; }
+  // this engine produces the logits: TP rank 0 of the last pipeline stage
+  bool has_logits() const { return opts_.rank == 0 && layer_end_ == m_.cfg.L; }
+  // pp: enqueue this stage's part of one prefill; a later stage takes the fp32
+  // residual stream [S, H] of the previous stage from `h_in` (device memory)
+  void enqueue_stage(const float *h_in);
+  const float *residual_out() const { return h0_; }
   const char *relay_kind() const {
     return mode_.split ? (relay_direct_ ? "direct" : "rsag") : "none";
   }
@@ -153,6 +166,7 @@ class Engine {
   EngineOpts opts_;
   Manifest m_;
   Mode mode_;
+  int layer_begin_ = 0, layer_end_ = 0;
   int Iloc_ = 0, nqkv_ = 0, bn_gu_ = 256, bn_down_ = 256, gu_rows_ = 0;
   int lm_rows_ = 0;
   int launches_ = 0;

@@ -66,6 +66,19 @@ def test_run_errors_are_json_without_gpu(krlib, tmp_path):
     assert r["_rc"] == 1 and "error" in r
 
 
+@pytest.mark.parametrize("mode,dev0,dev1,requests,what", [
+    ("pp", 0, 0, 2, "device2"),          # qwen_main.cpp:1995-1997
+    ("pp", 0, 1, 0, "requests"),         # :1998-2000
+    ("pp_serial", 0, 1, 9, "requests"),
+    ("tp2", 0, 1, 2, "pp mode"),
+])
+def test_pp_run_rejects_bad_arguments(krlib, tmp_path, mode, dev0, dev1, requests, what):
+    """kr_qwen_pp_run validates its arguments (as RunQwenPP does) before any device work."""
+    from kernrelay_b200 import libapi
+    r = libapi.qwen_pp_run(tmp_path, mode=mode, seq=64, dev0=dev0, dev1=dev1, requests=requests)
+    assert r["_rc"] == 1 and what in r["error"]
+
+
 def test_small_output_buffer_is_an_error(krlib, tmp_path):
     import ctypes
     buf = ctypes.create_string_buffer(8)

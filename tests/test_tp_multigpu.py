@@ -1,6 +1,7 @@
 """Tensor-parallel prefill on 2+ GPUs (one process, one host thread per rank):
 tp{k} (NCCL AllReduce baseline) and tp{k}_split (fused NVLink relay) against the
-fp32 CPU oracle, per layer, and through the reference's kr_qwen_tp_run ABI."""
+fp32 CPU oracle, per layer, and through the reference's kr_qwen_tp_run ABI; and the
+PP=2 layer pipeline through kr_qwen_pp_run."""
 import threading
 
 import numpy as np
@@ -116,3 +117,22 @@ def test_relay_timeout_is_reported_not_hung(cuda, krlib):
     c = krlib.gemm(a, a)
     torch.cuda.synchronize()
     assert torch.isfinite(c.float()).all()
+
+
+@pytest.mark.parametrize("mode", ["pp", "pp_serial"])
+def test_kr_qwen_pp_run_abi(cuda, tiny, mode):
+    """PP=2: stage 0 layers [0, L/2) on GPU 0, stage 1 [L/2, L) + lm_head on GPU 1;
+    two requests; last-row logits against the oracle (qwen_main.cpp:1993-2146)."""
+    if _ngpu() < 2:
+        pytest.skip("needs 2 GPUs")
+    d, ref, cfg = tiny
+    r = libapi.qwen_pp_run(d, mode=mode, seq=512, dev0=0, dev1=1, requests=2, warmup=1, iters=3)
+    assert r["_rc"] == 0, r
+    assert r["mode"] == ("pp_pipeline" if mode == "pp" else "pp_serial")
+    assert r["requests"] == 2 and r["devices"] == [0, 1]
+    assert r["layers"] == [[0, cfg.L // 2], [cfg.L // 2, cfg.L]]
+    assert len(r["wall_samples_us"]) == 3 and r["wall_best_us"] > 0
+    s1 = r["stages"][1]
+    assert s1["argmax"] == s1["ref_argmax"] == int(np.argmax(ref["logits_last"]))
+    assert s1["maxdiff"] <= 2 * TOL * float(np.abs(ref["logits_last"]).max())
+    assert s1["flag_timeouts"] == 0 and r["stages"][0]["flag_timeouts"] == 0
