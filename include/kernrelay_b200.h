@@ -48,6 +48,16 @@ int krb_synth_normal_host(const char *name, uint64_t seed, double std_, double m
 int krb_gemm_bf16(const void *A, long lda, const void *B, long ldb, void *C, long ldc,
                   const void *bias, int M, int N, int K, int bn, void *stream);
 
+/* Fused QKV projection: C[M,(HQ+2HKV)D] = A . B^T + bias, then per q / k head an
+ * optional RMSNorm over D (q_norm / k_norm; Qwen3) and rotate-half RoPE with the bf16
+ * cos / sin tables [max_pos, D] at position = row, in the GEMM epilogue; v heads get the
+ * bias only.  D in {64, 128}.  Replaces EmitQkv + EmitQkNorm + aclnnApplyRotaryPosEmb
+ * (qwen_main.cpp:1336-1357, 567-582) as one kernel. */
+int krb_gemm_qkv_rope_bf16(const void *A, long lda, const void *B, long ldb, void *C, long ldc,
+                           const void *bias, int M, int K, int HQ, int HKV, int D,
+                           const void *cos_tab, const void *sin_tab, const void *q_norm,
+                           const void *k_norm, float eps, void *stream);
+
 /* out[M,N] = A[M,K] . B[N,K]^T in fp32 (unrounded; row pitch ld) -- the o_proj and
  * single-device down_proj form whose output feeds the fp32 residual stream. */
 int krb_gemm_f32out(const void *A, long lda, const void *B, long ldb, float *out, long ld, int M,

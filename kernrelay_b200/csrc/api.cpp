@@ -568,6 +568,20 @@ KRB_EXPORT int krb_gemm_bf16(const void *A, long lda, const void *B, long ldb, v
   KRB_OP_END
 }
 
+KRB_EXPORT int krb_gemm_qkv_rope_bf16(const void *A, long lda, const void *B, long ldb, void *C,
+                                      long ldc, const void *bias, int M, int K, int HQ, int HKV,
+                                      int D, const void *cos_tab, const void *sin_tab,
+                                      const void *q_norm, const void *k_norm, float eps,
+                                      void *stream) {
+  KRB_OP_BEGIN
+  krb::gemm_qkv_rope_bf16(static_cast<const bf *>(A), lda, static_cast<const bf *>(B), ldb,
+                          static_cast<bf *>(C), ldc, static_cast<const bf *>(bias), M, K, HQ, HKV, D,
+                          static_cast<const bf *>(cos_tab), static_cast<const bf *>(sin_tab),
+                          static_cast<const bf *>(q_norm), static_cast<const bf *>(k_norm), eps,
+                          nullptr, as_stream(stream));
+  KRB_OP_END
+}
+
 KRB_EXPORT int krb_gemm_silu_bf16(const void *A, long lda, const void *Bgu, long ldb, void *act,
                                   long ldact, int M, int n_out, int K, int bn, void *stream) {
   KRB_OP_BEGIN

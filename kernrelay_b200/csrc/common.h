@@ -41,6 +41,16 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
 void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb, float *out,
                  long ld, int M, int N, int K, int bn, uint32_t *status, cudaStream_t stream);
 
+// Fused QKV projection: C[M, (HQ+2HKV)D] = A . B^T + bias, then per q / k head an
+// optional RMSNorm over D (qn / kn, Qwen3) and rotate-half RoPE with the bf16 cos /
+// sin tables [max_pos, D] at position = row; v heads get the bias only.
+void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
+                        __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int K,
+                        int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
+                        const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
+                        const __nv_bfloat16 *kn, float eps, uint32_t *status,
+                        cudaStream_t stream);
+
 // act[M, n_out] = silu(gate) * up, with B rows interleaved in blocks of bn:
 // rows [b*bn, b*bn+bn/2) gate, [b*bn+bn/2, (b+1)*bn) up for outputs [b*bn/2, (b+1)*bn/2).
 void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,

@@ -164,6 +164,9 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
   nqkv_ = (c.HQ + 2 * c.HKV) * c.D;
   layer_begin_ = 0;
   layer_end_ = c.L;
+  // fused modes run RoPE (and QK-norm) in the QKV GEMM epilogue; KRB_FUSE_ROPE=0 keeps
+  // the separate kernel
+  fuse_rope_ = mode_.fused && !(std::getenv("KRB_FUSE_ROPE") && std::getenv("KRB_FUSE_ROPE")[0] == '0');
   if (mode_.pp) {
     // stage s of n runs layers [s*L/n, (s+1)*L/n) (qwen_main.cpp:746-747)
     if (opts_.pp_stages < 2 || opts_.pp_stage < 0 || opts_.pp_stage >= opts_.pp_stages)
@@ -486,15 +489,25 @@ void Engine::layer(int l, StageTimes *st) {
   const float eps = float(c.eps);
   const LayerW &w = lw_[l];
   StageRec rec(stream_, st, g_events);
-  launches_ += 5;  // qkv, rope, attention, o, gate/up (+ add_norm counted there)
+  launches_ += 4;  // qkv, attention, o, gate/up (+ add_norm counted there)
   rec.begin(st ? &st->qkv : nullptr);
-  gemm_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, nqkv_, H, 0, 0, status_,
-            stream_);
-  rec.end();
-  rec.begin(st ? &st->rope : nullptr);
-  qk_norm_rope_bf16(qkv_, S, c.HQ, c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
-                    c.qk_norm ? w.kn : nullptr, eps, stream_);
-  rec.end();
+  if (fuse_rope_) {
+    // QK-norm and RoPE in the QKV GEMM's epilogue (no separate pass over q / k)
+    gemm_qkv_rope_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, H, c.HQ,
+                       c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
+                       c.qk_norm ? w.kn : nullptr, eps, status_, stream_);
+    rec.end();
+  } else {
+    // unfused serial modes: the reference's separate ops (qwen_main.cpp:1336-1357, 567-582)
+    gemm_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, nqkv_, H, 0, 0,
+              status_, stream_);
+    rec.end();
+    rec.begin(st ? &st->rope : nullptr);
+    qk_norm_rope_bf16(qkv_, S, c.HQ, c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
+                      c.qk_norm ? w.kn : nullptr, eps, stream_);
+    ++launches_;
+    rec.end();
+  }
   rec.begin(st ? &st->attn : nullptr);
   if (attn_tc_) {
     attention_vt_bf16(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);

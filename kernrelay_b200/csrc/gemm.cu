@@ -150,7 +150,11 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
-  EpiArgs ea{C, ldc, bias, N, nullptr};
+  EpiArgs ea{};
+  ea.c = C;
+  ea.ldc = ldc;
+  ea.bias = bias;
+  ea.n_out = N;
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   switch (bn) {
     case 256: {
@@ -181,7 +185,10 @@ void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long 
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
-  EpiArgs ea{nullptr, ld, nullptr, N, out};
+  EpiArgs ea{};
+  ea.ldc = ld;
+  ea.n_out = N;
+  ea.out_f32 = out;
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   switch (bn) {
     case 256: {
@@ -204,6 +211,51 @@ void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long 
   }
 }
 
+void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
+                        __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int K,
+                        int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
+                        const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
+                        const __nv_bfloat16 *kn, float eps, uint32_t *status,
+                        cudaStream_t stream) {
+  const int N = (HQ + 2 * HKV) * D;
+  if (M <= 0 || K <= 0 || HQ <= 0 || HKV <= 0) throw CudaError("gemm_qkv_rope: empty shape");
+  if (D != 64 && D != 128) throw CudaError("gemm_qkv_rope: head_dim must be 64 or 128");
+  if (ldc % 8 != 0 || reinterpret_cast<uintptr_t>(C) % 16 ||
+      (bias && reinterpret_cast<uintptr_t>(bias) % 16))
+    throw CudaError("gemm_qkv_rope: C/bias must be 16-byte aligned, ldc % 8 == 0");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  // heads must not straddle tiles: 256 or 128 (multiples of D), fewer waves wins
+  const int sms = sm_count(dev);
+  const long mblk = (M + kBM - 1) / kBM;
+  auto cost = [&](int bn) {
+    const long tiles = mblk * ((N + bn - 1) / bn);
+    return double((tiles + sms - 1) / sms) * double(bn + 16);
+  };
+  const int bn = cost(256) <= cost(128) ? 256 : 128;
+  EpiArgs ea{};
+  ea.c = C;
+  ea.ldc = ldc;
+  ea.bias = bias;
+  ea.n_out = N;
+  ea.cos_tab = cos_tab;
+  ea.sin_tab = sin_tab;
+  ea.qn = qn;
+  ea.kn = kn;
+  ea.q_cols = HQ * D;
+  ea.rope_cols = (HQ + HKV) * D;
+  ea.D = D;
+  ea.eps = eps;
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  if (bn == 256) {
+    const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
+    launch_gemm<256, kEpiQkvRope>(ta, tb, M, N, K, ea, 0, status, stream);
+  } else {
+    const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
+    launch_gemm<128, kEpiQkvRope>(ta, tb, M, N, K, ea, 0, status, stream);
+  }
+}
+
 void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
                     __nv_bfloat16 *act, long ldact, int M, int n_out, int K, int bn,
                     int grid_limit, uint32_t *status, cudaStream_t stream) {
@@ -215,7 +267,10 @@ void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, 
   const int half = bn / 2;
   const int nblk = (n_out + half - 1) / half;
   const int n_b_rows = nblk * bn;
-  EpiArgs ea{act, ldact, nullptr, n_out, nullptr};
+  EpiArgs ea{};
+  ea.c = act;
+  ea.ldc = ldact;
+  ea.n_out = n_out;
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   switch (bn) {
     case 256: {

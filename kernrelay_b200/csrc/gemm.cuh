@@ -32,6 +32,7 @@ enum EpiMode : int {
   kEpiStore = 0,    // C = bf16(acc [+ bias])
   kEpiSiluMul = 1,  // C[:, j] = bf16(silu(acc[:, g(j)]) * acc[:, u(j)]), interleaved blocks
   kEpiStoreF32 = 2, // out_f32 = acc (fp32, unrounded; consumed by the residual Add+RMSNorm)
+  kEpiQkvRope = 3,  // fused QKV: (+bias), per-head QK-RMSNorm (optional) and RoPE on q, k
 };
 
 // RELAY selects the fused relay kernel's instantiation (same layout today; kept
@@ -267,9 +268,15 @@ __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16 *dst, const float
 struct EpiArgs {
   __nv_bfloat16 *c;           // output
   long ldc;                   // output row pitch (elements)
-  const __nv_bfloat16 *bias;  // [N] or null (kEpiStore only)
+  const __nv_bfloat16 *bias;  // [N] or null (kEpiStore, kEpiQkvRope)
   int n_out;                  // valid output columns
   float *out_f32;             // kEpiStoreF32: output [M, ldc] fp32
+  // kEpiQkvRope: heads of D columns; columns [0, q_cols) are q heads, [q_cols,
+  // rope_cols) k heads (normalised with qn / kn when non-null, then rotated), the
+  // rest v heads (bias only).  cos / sin: bf16 [max_pos, D], position = row.
+  const __nv_bfloat16 *cos_tab, *sin_tab, *qn, *kn;
+  int q_cols, rope_cols, D;
+  float eps;
 };
 
 // The accumulator chunk a warp holds is row-per-thread (thread = TMEM lane = row,
@@ -344,7 +351,117 @@ __device__ __forceinline__ void epi_stage_store_f32(const float *stage, float *o
   __syncwarp();
 }
 
-// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32
+// ---- kEpiQkvRope: fused QKV epilogue (one thread = one output row = one position)
+// For every q / k head of the tile: v = acc + bias; with QK-norm, the head's
+// RMSNorm over D (sum of squares from a first pass over TMEM; the normalised value
+// times the weight is rounded to bf16 as HF's Qwen3 RMSNorm returns bf16); then
+// rotate-half RoPE with the bf16 cos / sin tables of this row's position:
+//   out[d] = v[d] cos[d] - v[d + D/2] sin[d],  out[d + D/2] = v[d + D/2] cos[d + D/2] + v[d] sin[d + D/2]
+// (same math as qk_norm_rope_kernel, without rounding q / k to bf16 before it).
+// v heads only get the bias.  Needs BN % D == 0 (heads never straddle tiles).
+__device__ __forceinline__ void epi_load32(uint32_t taddr, const __nv_bfloat16 *bias, int col,
+                                           float *v) {
+  uint32_t r[32];
+  tmem_ld_32x32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (bias) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4 *>(bias + col) + q);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(ws[e]);
+        v[q * 8 + 2 * e] += f.x;
+        v[q * 8 + 2 * e + 1] += f.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void unpack8_f(const uint4 &w, float *f) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = unpack_bf16x2(ws[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+template <int BN, typename RowPtr>
+__device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPtr bf16_row,
+                                             const EpiArgs &ea, int row, int nb) {
+  const int D = ea.D, half = D / 2, nch = D / 32;
+#pragma unroll 1
+  for (int h0 = 0; h0 < BN; h0 += D) {
+    const int hcol = nb * BN + h0;  // first column of this head
+    if (hcol >= ea.n_out) break;    // warp-uniform
+    if (hcol >= ea.rope_cols) {
+      // v head: bias only
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        float v[32];
+        epi_load32(tbase + h0 + c * 32, ea.bias, hcol + c * 32, v);
+        epi_stage_put(stage, v);
+        epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + c * 32, ea.n_out - hcol - c * 32);
+      }
+      continue;
+    }
+    const __nv_bfloat16 *nw = hcol < ea.q_cols ? ea.qn : ea.kn;
+    float rn = 1.f;
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        float v[32];
+        epi_load32(tbase + h0 + c * 32, ea.bias, hcol + c * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
+      }
+      rn = rsqrtf(ss / float(D) + ea.eps);
+    }
+    const __nv_bfloat16 *ct = ea.cos_tab + size_t(row) * D;
+    const __nv_bfloat16 *st = ea.sin_tab + size_t(row) * D;
+#pragma unroll 1
+    for (int c = 0; c < nch / 2; ++c) {
+      const int dlo = c * 32, dhi = half + c * 32;
+      float lo[32], hi[32];
+      epi_load32(tbase + h0 + dlo, ea.bias, hcol + dlo, lo);
+      epi_load32(tbase + h0 + dhi, ea.bias, hcol + dhi, hi);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float wl[8], wh[8], cl[8], sl[8], ch[8], sh[8];
+        unpack8_f(__ldg(reinterpret_cast<const uint4 *>(ct + dlo) + q), cl);
+        unpack8_f(__ldg(reinterpret_cast<const uint4 *>(st + dlo) + q), sl);
+        unpack8_f(__ldg(reinterpret_cast<const uint4 *>(ct + dhi) + q), ch);
+        unpack8_f(__ldg(reinterpret_cast<const uint4 *>(st + dhi) + q), sh);
+        if (nw) {
+          unpack8_f(__ldg(reinterpret_cast<const uint4 *>(nw + dlo) + q), wl);
+          unpack8_f(__ldg(reinterpret_cast<const uint4 *>(nw + dhi) + q), wh);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float a = lo[q * 8 + e], b = hi[q * 8 + e];
+          if (nw) {
+            a = bf16_round(a * rn * wl[e]);
+            b = bf16_round(b * rn * wh[e]);
+          }
+          lo[q * 8 + e] = a * cl[e] - b * sl[e];
+          hi[q * 8 + e] = b * ch[e] + a * sh[e];
+        }
+      }
+      epi_stage_put(stage, lo);
+      epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + dlo, 32);
+      epi_stage_put(stage, hi);
+      epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + dhi, 32);
+    }
+  }
+}
+
+// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32 / kEpiQkvRope
 template <int BN, int MODE>
 __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
                                               int M, const EpiArgs &ea, uint32_t *status) {
@@ -371,7 +488,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
     auto bf16_row = [&](int r) -> __nv_bfloat16 * {
       return (row0 + r < M) ? ea.c + static_cast<long>(row0 + r) * ea.ldc : nullptr;
     };
-    if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
+    if constexpr (MODE == kEpiQkvRope) {
+      // rows past M are not stored; clamp their table position
+      epi_qkv_rope<BN>(tbase, stage, bf16_row, ea, min(mb * kBM + quad * 32 + lane, M - 1), nb);
+    } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = nb * BN + c * 32;

@@ -167,6 +167,7 @@ class Engine {
   Manifest m_;
   Mode mode_;
   int layer_begin_ = 0, layer_end_ = 0;
+  bool fuse_rope_ = false;  // QK-norm + RoPE in the QKV GEMM epilogue
   int Iloc_ = 0, nqkv_ = 0, bn_gu_ = 256, bn_down_ = 256, gu_rows_ = 0;
   int lm_rows_ = 0;
   int launches_ = 0;

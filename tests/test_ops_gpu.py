@@ -180,6 +180,39 @@ def _rope_tables(S, D, theta):
     return cos, sin
 
 
+@pytest.mark.parametrize("S,HQ,HKV,D,qk_norm,bias", [(256, 4, 2, 128, True, False),
+                                                     (200, 6, 2, 64, False, True),
+                                                     (384, 28, 4, 128, False, True)])
+def test_gemm_qkv_rope(cuda, krlib, S, HQ, HKV, D, qk_norm, bias):
+    """Fused QKV GEMM + bias + QK-norm + RoPE epilogue vs torch fp32 of the same op
+    (GEMM in fp32; the normalised q/k rounded to bf16 as in the kernel)."""
+    import torch
+    g = torch.Generator().manual_seed(S + D)
+    H = 512
+    N = (HQ + 2 * HKV) * D
+    A = _bf(torch.randn(S, H, generator=g)).to(cuda)
+    B = _bf(torch.randn(N, H, generator=g) * 0.05).to(cuda)
+    b = _bf(torch.randn(N, generator=g) * 0.1).to(cuda) if bias else None
+    cos, sin = _rope_tables(S, D, 1e6)
+    cos, sin = cos.to(cuda), sin.to(cuda)
+    qn = _bf(1 + 0.1 * torch.randn(D, generator=g)).to(cuda) if qk_norm else None
+    kn = _bf(1 + 0.1 * torch.randn(D, generator=g)).to(cuda) if qk_norm else None
+    out = krlib.gemm_qkv_rope(A, B, HQ, HKV, D, cos, sin, bias=b, q_norm=qn, k_norm=kn)
+    torch.cuda.synchronize()
+    x = A.float() @ B.float().T
+    if b is not None:
+        x = x + b.float()
+    x = x.view(S, HQ + 2 * HKV, D)
+    q, k, v = x[:, :HQ], x[:, HQ:HQ + HKV], x[:, HQ + HKV:]
+    if qk_norm:
+        q = (q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + 1e-6) * qn.float()).to(torch.bfloat16).float()
+        k = (k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + 1e-6) * kn.float()).to(torch.bfloat16).float()
+    qr = _rope_ref(q, cos.float(), sin.float())
+    kr = _rope_ref(k, cos.float(), sin.float())
+    ref = torch.cat([qr, kr, v], 1).reshape(S, N)
+    _close(out, ref, rel=1e-2, abs_=2e-2)
+
+
 @pytest.mark.parametrize("D,qk_norm", [(64, False), (128, True), (128, False)])
 def test_qk_norm_rope(cuda, krlib, D, qk_norm):
     import torch
