@@ -27,11 +27,13 @@ extern "C" {
 const char *kr_version(void);
 
 /* Run a KernRelay schedule.json (generic DAG executor).
- * Replaces kr_plan_run (include/kernrelay.h:26-27, exec/kr_api.cpp:23-46).
- * Returns 2 on NULL schedule_json/out_json, as the reference does.  The B200
- * build validates the schedule and writes a JSON result file; executing the
- * generic E3/E5/E9 DAGs on CUDA streams is not part of this build, so a valid
- * schedule yields rc 3 and {"error":"plan executor not built"}. */
+ * Replaces kr_plan_run (include/kernrelay.h:26-27, exec/kr_api.cpp:23-46,
+ * exec/exec_main.cpp RunPlanCli).  devices: "" / NULL = 0..nranks-1, else exactly
+ * nranks comma-separated ids.  mode: direct | graph | graph_per_stream |
+ * graph_segment.  Writes the result JSON {dag, group, nranks, iters, warmup, p50_us,
+ * gate_timeouts, checksum, ok, times_us, ... device_p50_us, node_checksums} to
+ * out_json and prints it.  Returns 0, 2 on NULL schedule_json/out_json (as the
+ * reference does), 1 on any other failure with {"error": "..."} in out_json. */
 int kr_plan_run(const char *schedule_json, int iters, int warmup, const char *devices,
                 const char *mode, const char *out_json);
 

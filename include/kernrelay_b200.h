@@ -146,6 +146,11 @@ int krb_relay_down_single_noalloc(const void *act, const void *w_down, const voi
  * kr_wait_* status word 2 after maxSpins, kernels/kr_wait_aiv.cpp:22-33.) */
 int krb_relay_timeout_probe(int S, int H, int K, int tiles, float timeout_ms, uint32_t *status_out);
 
+/* Parse and validate a schedule.json exactly as kr_plan_run does, without a GPU:
+ * JSON {dag, group, nranks, nodes, tasks, publishes, lanes, segments,
+ * lane_order_acyclic} or {"error": ...} (rc 1) with kr_plan_run's message. */
+int krb_plan_check(const char *schedule_json, char *out, size_t cap);
+
 /* Host view of the tp_split relay plan for (S, H, tiles, k, rank, bn): JSON
  * {R, Rk, num_n, rs_expect, ag_expect, nseg, blocks: [[tile, first_owner,
  * last_owner] per 128-row block]} -- the row routing the device epilogue uses

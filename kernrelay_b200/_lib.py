@@ -72,6 +72,7 @@ SIGNATURES = [
                                               c_int, c_void_p, c_void_p]),
     ("krb_relay_timeout_probe", c_int, [c_int, c_int, c_int, c_int, c_float, c_u32p]),
     ("krb_relay_plan", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_char_p, c_size_t]),
+    ("krb_plan_check", c_int, [c_char_p, c_char_p, c_size_t]),
     ("krb_engine_create", c_int, [c_char_p, c_char_p, c_int, c_int, c_int, c_int, c_int,
                                   ctypes.POINTER(c_void_p)]),
     ("krb_engine_destroy", None, [c_void_p]),
@@ -308,6 +309,15 @@ def relay_plan(S, H, tiles, k, rank, bn):
     rc = lib().krb_relay_plan(S, H, tiles, k, rank, bn, buf, len(buf))
     if rc != 0:
         raise KrbError(buf.value.decode(errors="replace"))
+    return json.loads(buf.value.decode())
+
+
+def plan_check(schedule_json):
+    """Validate a schedule.json like kr_plan_run (no GPU needed); raises KrbError."""
+    buf = ctypes.create_string_buffer(1 << 16)
+    rc = lib().krb_plan_check(str(schedule_json).encode(), buf, len(buf))
+    if rc != 0:
+        raise KrbError(json.loads(buf.value.decode()).get("error", "plan check failed"))
     return json.loads(buf.value.decode())
 
 

@@ -21,6 +21,7 @@
 #include "kernrelay.h"
 #include "kernrelay_b200.h"
 #include "model.h"
+#include "plan.h"
 #include "ptx.cuh"
 #include "synth.cuh"
 
@@ -137,24 +138,18 @@ KRB_EXPORT const char *kr_version(void) { return "KernRelay 0.3 (libkernrelay, B
 KRB_EXPORT int kr_plan_run(const char *schedule_json, int iters, int warmup, const char *devices,
                            const char *mode, const char *out_json) {
   if (!schedule_json || !out_json) return 2;  // kr_api.cpp:27
-  (void)iters;
-  (void)warmup;
-  (void)devices;
-  std::string err;
   try {
-    const std::string m = mode ? mode : "direct";
-    if (m != "direct" && m != "graph" && m != "graph_per_stream" && m != "graph_segment")
-      throw std::runtime_error("unknown plan mode " + m);
-    krb::json::Value doc = krb::json::parse_file(schedule_json);
-    (void)doc;
-    err = "plan executor not built in the B200 library (TP-MLP prefill path only)";
+    const std::string res = krb::plan::run(schedule_json, iters, warmup, devices ? devices : "",
+                                           mode ? mode : "direct", out_json);
+    std::printf("%s\n", res.c_str());  // the reference prints its result line too
+    std::fflush(stdout);
+    return 0;
   } catch (const std::exception &e) {
-    err = e.what();
+    g_last_error = e.what();
+    std::ofstream f(out_json);
+    f << "{\"error\":\"" << krb::json::escape(e.what()) << "\"}\n";
+    return 1;
   }
-  std::ofstream f(out_json);
-  f << "{\"error\":\"" << krb::json::escape(err) << "\"}\n";
-  g_last_error = err;
-  return 3;
 }
 
 KRB_EXPORT int kr_qwen_run(const char *model_dir, const char *mode, int seq, int device,
@@ -851,6 +846,15 @@ KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float tim
     if (ghost) cudaFree(ghost);
     if (bufs) cudaFree(bufs);
     return fail(e);
+  }
+}
+
+KRB_EXPORT int krb_plan_check(const char *schedule_json, char *out, size_t out_cap) {
+  try {
+    if (!schedule_json) throw std::runtime_error("schedule path required");
+    return write_out(krb::plan::check(schedule_json), out, out_cap);
+  } catch (const std::exception &e) {
+    return write_error(e.what(), out, out_cap);
   }
 }
 

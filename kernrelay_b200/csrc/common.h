@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -36,6 +37,10 @@ CUtensorMap make_tmap_2d_bf16(const void *base, uint64_t rows, uint64_t cols, ui
 void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
                __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int N, int K,
                int bn, int grid_limit, uint32_t *status, cudaStream_t stream);
+
+// fp16 variant of gemm_bf16 (no bias): C[M,N] = f16(A[M,K] . B[N,K]^T), fp32 accumulate.
+void gemm_f16(const __half *A, long lda, const __half *B, long ldb, __half *C, long ldc, int M,
+              int N, int K, int bn, uint32_t *status, cudaStream_t stream);
 
 // fp32 output: out[M,N] = A . B^T unrounded (row pitch ld), for residual updates.
 void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb, float *out,

@@ -25,7 +25,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     if (lane == 0) gemm_producer<BN>(s, &ta, &tb, ts, K, status);
   } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN>(s, ts, K, status);
+    if (lane == 0) gemm_mma<BN, 0, MODE == kEpiStoreF16>(s, ts, K, status);
   } else {
     gemm_epilogue<BN, MODE>(s, ts, M, ea, status);
   }
@@ -174,6 +174,41 @@ void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ld
     }
     default:
       throw CudaError("gemm_bf16: unsupported bn " + std::to_string(bn));
+  }
+}
+
+void gemm_f16(const __half *A, long lda, const __half *B, long ldb, __half *C, long ldc, int M,
+              int N, int K, int bn, uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_f16: empty shape");
+  if (N % 8 != 0 || ldc % 8 != 0) throw CudaError("gemm_f16: N and ldc must be multiples of 8");
+  if (reinterpret_cast<uintptr_t>(C) % 16) throw CudaError("gemm_f16: C must be 16-byte aligned");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
+  EpiArgs ea{};
+  ea.c = reinterpret_cast<__nv_bfloat16 *>(C);  // 2-byte rows; the F16 epilogue packs fp16
+  ea.ldc = ldc;
+  ea.n_out = N;
+  // TMA moves 2-byte elements without conversion, so the bf16 tensor map serves fp16 too
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  switch (bn) {
+    case 256: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
+      launch_gemm<256, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    case 224: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
+      launch_gemm<224, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    case 128: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
+      launch_gemm<128, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
+      break;
+    }
+    default:
+      throw CudaError("gemm_f16: unsupported bn " + std::to_string(bn));
   }
 }
 

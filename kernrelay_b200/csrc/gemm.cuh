@@ -33,6 +33,7 @@ enum EpiMode : int {
   kEpiSiluMul = 1,  // C[:, j] = bf16(silu(acc[:, g(j)]) * acc[:, u(j)]), interleaved blocks
   kEpiStoreF32 = 2, // out_f32 = acc (fp32, unrounded; consumed by the residual Add+RMSNorm)
   kEpiQkvRope = 3,  // fused QKV: (+bias), per-head QK-RMSNorm (optional) and RoPE on q, k
+  kEpiStoreF16 = 4, // fp16 A, B and C: C = f16(acc)  (the plan executor's matmul)
 };
 
 // RELAY selects the fused relay kernel's instantiation (same layout today; kept
@@ -195,11 +196,12 @@ drain:
 }
 
 // ---- warp 1, one thread: tcgen05.mma issuer
-template <int BN, int RELAY = 0>
+// F16 selects fp16 operands (both A and B) instead of bf16.
+template <int BN, int RELAY = 0, bool F16 = false>
 __device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const TileSched &ts,
                                          int K, uint32_t *status) {
   using C = GemmCfg<BN, RELAY>;
-  constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN);
+  constexpr uint32_t idesc = F16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
   const uint32_t tmem = *s.tmem_slot;
   const int nkb = (K + kBK - 1) / kBK;
   int stage = 0;
@@ -294,8 +296,9 @@ __device__ __forceinline__ void epi_stage_put(float *stage, const float *v) {
   __syncwarp();
 }
 
-// bf16 write-back: lane l covers row (l/4 + 8*it) columns [8*(l%4), +8)
-template <typename RowPtr>
+// bf16 write-back: lane l covers row (l/4 + 8*it) columns [8*(l%4), +8).  F16 rounds to
+// fp16 instead (same 2-byte layout; the row pointers then address an fp16 matrix).
+template <bool F16 = false, typename RowPtr>
 __device__ __forceinline__ void epi_stage_store_bf16(const float *stage, RowPtr row_ptr,
                                                      const __nv_bfloat16 *bias, int col0,
                                                      int valid_cols) {
@@ -321,10 +324,17 @@ __device__ __forceinline__ void epi_stage_store_bf16(const float *stage, RowPtr 
     __nv_bfloat16 *dst = row_ptr(r);
     if (dst && c < valid_cols) {
       uint4 w;
-      w.x = pack_bf16x2(x.x + b[0], x.y + b[1]);
-      w.y = pack_bf16x2(x.z + b[2], x.w + b[3]);
-      w.z = pack_bf16x2(y.x + b[4], y.y + b[5]);
-      w.w = pack_bf16x2(y.z + b[6], y.w + b[7]);
+      if constexpr (F16) {
+        w.x = pack_f16x2(x.x + b[0], x.y + b[1]);
+        w.y = pack_f16x2(x.z + b[2], x.w + b[3]);
+        w.z = pack_f16x2(y.x + b[4], y.y + b[5]);
+        w.w = pack_f16x2(y.z + b[6], y.w + b[7]);
+      } else {
+        w.x = pack_bf16x2(x.x + b[0], x.y + b[1]);
+        w.y = pack_bf16x2(x.z + b[2], x.w + b[3]);
+        w.z = pack_bf16x2(y.x + b[4], y.y + b[5]);
+        w.w = pack_bf16x2(y.z + b[6], y.w + b[7]);
+      }
       *reinterpret_cast<uint4 *>(dst + col0 + c) = w;
     }
   }
@@ -461,7 +471,8 @@ __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPt
   }
 }
 
-// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32 / kEpiQkvRope
+// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32 / kEpiQkvRope /
+// kEpiStoreF16
 template <int BN, int MODE>
 __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
                                               int M, const EpiArgs &ea, uint32_t *status) {
@@ -491,7 +502,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
     if constexpr (MODE == kEpiQkvRope) {
       // rows past M are not stored; clamp their table position
       epi_qkv_rope<BN>(tbase, stage, bf16_row, ea, min(mb * kBM + quad * 32 + lane, M - 1), nb);
-    } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
+    } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32 || MODE == kEpiStoreF16) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = nb * BN + c * 32;
@@ -505,6 +516,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
         epi_stage_put(stage, v);
         if constexpr (MODE == kEpiStore)
           epi_stage_store_bf16(stage, bf16_row, ea.bias, col0, ea.n_out - col0);
+        else if constexpr (MODE == kEpiStoreF16)
+          epi_stage_store_bf16<true>(stage, bf16_row, nullptr, col0, ea.n_out - col0);
         else
           epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, ea.n_out - col0);
       }

@@ -1,0 +1,385 @@
+// fp16 operator kernels of the schedule executor (kr_plan_run).  One launcher per
+// operator kind of the reference's generic executor (exec/runtime/op_impl.cpp:59-76);
+// matmul goes to the tcgen05 GEMM (gemm_f16), collectives to NCCL.  Every launcher is
+// asynchronous on `stream` and validates its shape on the host.
+#include <algorithm>
+
+#include "common.h"
+#include "plan_ops.h"
+#include "ptx.cuh"
+
+namespace krb {
+namespace plan {
+
+namespace {
+
+constexpr int kEwThreads = 256;
+
+int ew_grid(int64_t work, int device_sms) {
+  const int64_t blocks = (work + kEwThreads - 1) / kEwThreads;
+  return int(std::max<int64_t>(1, std::min<int64_t>(blocks, int64_t(device_sms) * 8)));
+}
+
+int cur_sms() {
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  return sm_count(dev);
+}
+
+// exec/exec_main.cpp:74-79: value = (((h >> 8) % 23) - 11) / 256 with
+// h = u32(index) * 2654435761 + seed * 40503 + 7 (all arithmetic mod 2^32).
+__device__ __forceinline__ float det_value(uint32_t seed, uint64_t index) {
+  const uint32_t h = uint32_t(index) * 2654435761u + seed * 40503u + 7u;
+  const int v = int((h >> 8) % 23u) - 11;
+  return float(v) * 0.00390625f;
+}
+
+__global__ void det_fill_kernel(__half *dst, uint64_t n, uint32_t seed) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    dst[i] = __float2half_rn(det_value(seed, i));
+}
+
+// dst[n][k] = value of element (k, n) of the logical row-major [K, N] matrix
+__global__ void det_fill_t_kernel(__half *dst, int64_t K, int64_t N, uint32_t seed) {
+  const uint64_t total = uint64_t(K) * uint64_t(N);
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < total;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t n = i / uint64_t(K), k = i - n * uint64_t(K);
+    dst[i] = __float2half_rn(det_value(seed, k * uint64_t(N) + n));
+  }
+}
+
+// exec_main.cpp:521-523: idx[i] = (i * 131 + 7 + seed) % dim0 in 64-bit arithmetic
+__global__ void emb_index_kernel(int64_t *idx, int64_t rows, int64_t dim0, uint32_t seed) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < rows;
+       i += int64_t(gridDim.x) * blockDim.x)
+    idx[i] = int64_t((uint64_t(i) * 131u + 7u + seed) % uint64_t(dim0));
+}
+
+// ---- elementwise: 8 halves per vector when every pointer is 16-byte aligned and n % 8 == 0
+struct Ew {
+  enum Kind { Add, Gelu, Scale, Cast };
+};
+
+__device__ __forceinline__ float gelu_f(float x) {
+  // tanh-form GELU written as x * sigmoid(2 z), z = sqrt(2/pi) (x + 0.044715 x^3)
+  const float z = 1.5957691216057308f * (x + 0.044715f * x * x * x);
+  return x / (1.0f + expf(-z));
+}
+
+template <int KIND>
+__device__ __forceinline__ float ew_op(float a, float b, float k, uint32_t iters) {
+  if constexpr (KIND == Ew::Add) {
+    return a + b;
+  } else if constexpr (KIND == Ew::Gelu) {
+    return gelu_f(a);
+  } else {
+    // out = in * k, repeated `iters` times like the reference's duration knob
+    // (custom_aiv.cpp:46-49); every repetition produces the same product.
+    float r = a;
+#pragma unroll 1
+    for (uint32_t it = 0; it < iters; ++it) {
+      r = __fmul_rn(a, k);
+      asm volatile("" : "+f"(r));
+    }
+    return r;
+  }
+}
+
+template <int KIND>
+__global__ void ew_vec_kernel(const __half *a, const __half *b, __half *out, uint64_t nvec,
+                              float k, uint32_t iters) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < nvec;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint4 va = reinterpret_cast<const uint4 *>(a)[i];
+    uint4 vb = make_uint4(0, 0, 0, 0);
+    if constexpr (KIND == Ew::Add) vb = reinterpret_cast<const uint4 *>(b)[i];
+    const __half2 *ha = reinterpret_cast<const __half2 *>(&va);
+    const __half2 *hb = reinterpret_cast<const __half2 *>(&vb);
+    uint4 vo;
+    __half2 *ho = reinterpret_cast<__half2 *>(&vo);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = __half22float2(ha[e]);
+      const float2 fb = __half22float2(hb[e]);
+      ho[e] = __floats2half2_rn(ew_op<KIND>(fa.x, fb.x, k, iters), ew_op<KIND>(fa.y, fb.y, k, iters));
+    }
+    reinterpret_cast<uint4 *>(out)[i] = vo;
+  }
+}
+
+template <int KIND>
+__global__ void ew_scalar_kernel(const __half *a, const __half *b, __half *out, uint64_t n,
+                                 float k, uint32_t iters) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const float fb = (KIND == Ew::Add) ? __half2float(b[i]) : 0.f;
+    out[i] = __float2half_rn(ew_op<KIND>(__half2float(a[i]), fb, k, iters));
+  }
+}
+
+__global__ void cast_kernel(const __half *in, float *out, uint64_t n) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    out[i] = __half2float(in[i]);
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int KIND>
+void launch_ew(const __half *a, const __half *b, __half *out, uint64_t n, float k, uint32_t iters,
+               cudaStream_t stream) {
+  if (n == 0) return;
+  const bool vec = n % 8 == 0 && aligned16(a) && aligned16(out) && (!b || aligned16(b));
+  const int sms = cur_sms();
+  if (vec) {
+    ew_vec_kernel<KIND><<<ew_grid(int64_t(n / 8), sms), kEwThreads, 0, stream>>>(a, b, out, n / 8,
+                                                                                 k, iters);
+  } else {
+    ew_scalar_kernel<KIND><<<ew_grid(int64_t(n), sms), kEwThreads, 0, stream>>>(a, b, out, n, k,
+                                                                               iters);
+  }
+  KRB_CUDA(cudaGetLastError());
+}
+
+// ---- row reductions (softmax over the last dim, LayerNorm over the last dim)
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_reduce(float v, float *red, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  __syncthreads();  // red[] may still be read by the previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < int(blockDim.x >> 5); ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  return r;
+}
+
+__global__ void __launch_bounds__(kRowThreads) softmax_rows_kernel(const __half *in, __half *out,
+                                                                   int64_t cols) {
+  __shared__ float red[32];
+  const __half *x = in + blockIdx.x * cols;
+  __half *y = out + blockIdx.x * cols;
+  float m = -INFINITY;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, __half2float(x[c]));
+  m = block_reduce(m, red, true);
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += expf(__half2float(x[c]) - m);
+  s = block_reduce(s, red, false);
+  const float inv = 1.0f / s;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    y[c] = __float2half_rn(expf(__half2float(x[c]) - m) * inv);
+}
+
+__global__ void __launch_bounds__(kRowThreads) layernorm_rows_kernel(
+    const __half *in, const __half *w, const __half *b, __half *out, int64_t cols, float eps) {
+  __shared__ float red[32];
+  const __half *x = in + blockIdx.x * cols;
+  __half *y = out + blockIdx.x * cols;
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += __half2float(x[c]);
+  const float mean = block_reduce(s, red, false) / float(cols);
+  float v = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float d = __half2float(x[c]) - mean;
+    v += d * d;
+  }
+  const float rstd = rsqrtf(block_reduce(v, red, false) / float(cols) + eps);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float d = (__half2float(x[c]) - mean) * rstd;
+    y[c] = __float2half_rn(d * __half2float(w[c]) + __half2float(b[c]));
+  }
+}
+
+// ---- per-row sort / top-k: bitonic sort of 64-bit keys in shared memory, one CTA per row.
+// Key = (order-preserving 16-bit image of the fp16 value) << 32 | index part.  -0 is folded
+// onto +0 so equal values tie and the index part decides: ascending sort keeps the lower
+// index first (stable), top-k (descending) stores ~index so the lower index also wins.
+__device__ __forceinline__ uint32_t f16_order(uint16_t h) {
+  if (h == 0x8000u) h = 0;
+  return (h & 0x8000u) ? (~uint32_t(h) & 0xFFFFu) : (uint32_t(h) | 0x8000u);
+}
+__device__ __forceinline__ uint16_t f16_from_order(uint32_t o) {
+  return (o & 0x8000u) ? uint16_t(o & 0x7FFFu) : uint16_t(~o & 0xFFFFu);
+}
+
+template <bool kDesc>
+__global__ void row_sort_kernel(const __half *in, int64_t cols, int P, int64_t k_out,
+                                __half *vals, int64_t *idx) {
+  extern __shared__ uint64_t keys[];
+  const int64_t row = blockIdx.x;
+  const uint16_t *x = reinterpret_cast<const uint16_t *>(in) + row * cols;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    uint64_t key;
+    if (i < cols) {
+      const uint64_t o = f16_order(x[i]);
+      key = kDesc ? (o << 32) | (0xFFFFFFFFull - uint64_t(i)) : (o << 32) | uint64_t(i);
+    } else {
+      key = kDesc ? 0ull : ~0ull;  // padding sorts behind every real element
+    }
+    keys[i] = key;
+  }
+  __syncthreads();
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = ((i & size) == 0) != kDesc;  // ascending run when `up`
+          const uint64_t a = keys[i], b = keys[j];
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  uint16_t *v = reinterpret_cast<uint16_t *>(vals) + row * k_out;
+  int64_t *ix = idx + row * k_out;
+  for (int64_t i = threadIdx.x; i < k_out; i += blockDim.x) {
+    const uint64_t key = keys[i];
+    v[i] = f16_from_order(uint32_t(key >> 32));
+    const uint32_t lo = uint32_t(key & 0xFFFFFFFFull);
+    ix[i] = kDesc ? int64_t(0xFFFFFFFFu - lo) : int64_t(lo);
+  }
+}
+
+template <bool kDesc>
+void launch_row_sort(const __half *in, int64_t rows, int64_t cols, int64_t k_out, __half *vals,
+                     int64_t *idx, cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (cols <= 0 || cols > kMaxSortCols) throw CudaError("sort/topk: cols out of range (1..16384)");
+  if (k_out <= 0 || k_out > cols) throw CudaError("topk: k out of range");
+  int P = 1;
+  while (P < cols) P <<= 1;
+  const size_t smem = size_t(P) * sizeof(uint64_t);
+  auto kern = row_sort_kernel<kDesc>;
+  if (smem > 48 * 1024)
+    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  kern<<<unsigned(rows), 512, smem, stream>>>(in, cols, P, k_out, vals, idx);
+  KRB_CUDA(cudaGetLastError());
+}
+
+// ---- embedding gather: out[r] = weight[idx[r]]; an index outside [0, V) writes zeros and
+// raises kStatusBadIndex.
+__global__ void embedding_kernel(const __half *weight, const int64_t *idx, __half *out,
+                                 int64_t rows, int64_t cols, int64_t V, uint32_t *status) {
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  const int64_t id = idx[r];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0) atomicOr(status, kStatusBadIndex);
+  const __half *src = weight + (ok ? id : 0) * cols;
+  __half *dst = out + r * cols;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) dst[c] = ok ? src[c] : __float2half(0.f);
+}
+
+// ---- scalar accumulation probes (custom_aic.cpp:12-38, custom_aicpu.aicpu:13-25): each
+// block walks its contiguous share sequentially, acc = acc * 0.9990234375 + in[i] in fp32
+// with separate roundings, `iters` passes, and writes fp16(acc) to out[begin].
+__global__ void mac_kernel(const __half *in, __half *out, uint32_t elems, uint32_t iters,
+                           float acc0) {
+  if (threadIdx.x != 0) return;
+  const uint32_t per = (elems + gridDim.x - 1) / gridDim.x;
+  const uint32_t begin = blockIdx.x * per;
+  if (begin >= elems) return;
+  const uint32_t count = min(per, elems - begin);
+  float acc = acc0;
+  for (uint32_t it = 0; it < iters; ++it)
+    for (uint32_t i = 0; i < count; ++i)
+      acc = __fadd_rn(__fmul_rn(acc, 0.9990234375f), __half2float(in[begin + i]));
+  out[begin] = __float2half_rn(acc);
+}
+
+}  // namespace
+
+void det_fill_f16(__half *dst, uint64_t n, uint32_t seed, cudaStream_t stream) {
+  if (n == 0) return;
+  det_fill_kernel<<<ew_grid(int64_t(n), cur_sms()), kEwThreads, 0, stream>>>(dst, n, seed);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void det_fill_f16_t(__half *dst, int64_t K, int64_t N, uint32_t seed, cudaStream_t stream) {
+  if (K <= 0 || N <= 0) return;
+  det_fill_t_kernel<<<ew_grid(K * N, cur_sms()), kEwThreads, 0, stream>>>(dst, K, N, seed);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void embedding_indices(int64_t *idx, int64_t rows, int64_t dim0, uint32_t seed,
+                       cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (dim0 <= 0) throw CudaError("embedding: dim0 must be positive");
+  emb_index_kernel<<<ew_grid(rows, cur_sms()), kEwThreads, 0, stream>>>(idx, rows, dim0, seed);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void add_f16(const __half *a, const __half *b, __half *out, uint64_t n, cudaStream_t stream) {
+  launch_ew<Ew::Add>(a, b, out, n, 0.f, 1, stream);
+}
+
+void gelu_f16(const __half *in, __half *out, uint64_t n, cudaStream_t stream) {
+  launch_ew<Ew::Gelu>(in, nullptr, out, n, 0.f, 1, stream);
+}
+
+void scale_f16(const __half *in, __half *out, uint64_t n, float k, uint32_t iters,
+               cudaStream_t stream) {
+  launch_ew<Ew::Scale>(in, nullptr, out, n, k, std::max<uint32_t>(iters, 1), stream);
+}
+
+void cast_f16_f32(const __half *in, float *out, uint64_t n, cudaStream_t stream) {
+  if (n == 0) return;
+  cast_kernel<<<ew_grid(int64_t(n), cur_sms()), kEwThreads, 0, stream>>>(in, out, n);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void softmax_rows_f16(const __half *in, __half *out, int64_t rows, int64_t cols,
+                      cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (cols <= 0) throw CudaError("softmax: empty rows");
+  softmax_rows_kernel<<<unsigned(rows), kRowThreads, 0, stream>>>(in, out, cols);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void layernorm_rows_f16(const __half *in, const __half *w, const __half *b, __half *out,
+                        int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (cols <= 0) throw CudaError("layernorm: empty rows");
+  layernorm_rows_kernel<<<unsigned(rows), kRowThreads, 0, stream>>>(in, w, b, out, cols, eps);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void topk_rows_f16(const __half *in, int64_t rows, int64_t cols, int64_t k, __half *vals,
+                   int64_t *idx, cudaStream_t stream) {
+  launch_row_sort<true>(in, rows, cols, k, vals, idx, stream);
+}
+
+void sort_rows_f16(const __half *in, int64_t rows, int64_t cols, __half *vals, int64_t *idx,
+                   cudaStream_t stream) {
+  launch_row_sort<false>(in, rows, cols, cols, vals, idx, stream);
+}
+
+void embedding_f16(const __half *weight, const int64_t *idx, __half *out, int64_t rows,
+                   int64_t cols, int64_t V, uint32_t *status, cudaStream_t stream) {
+  if (rows <= 0) return;
+  embedding_kernel<<<unsigned(rows), 128, 0, stream>>>(weight, idx, out, rows, cols, V, status);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void mac_f16(const __half *in, __half *out, uint32_t elems, uint32_t iters, uint32_t blocks,
+             float acc0, cudaStream_t stream) {
+  if (elems == 0) return;
+  mac_kernel<<<std::max<uint32_t>(blocks, 1), 32, 0, stream>>>(in, out, elems,
+                                                               std::max<uint32_t>(iters, 1), acc0);
+  KRB_CUDA(cudaGetLastError());
+}
+
+}  // namespace plan
+}  // namespace krb

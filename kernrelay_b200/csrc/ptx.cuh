@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace krb {
@@ -24,6 +25,7 @@ enum StatusBits : uint32_t {
   kStatusLocalWait = 1u << 5,    // relay: local tile counter never completed
   kStatusFlagWait = 1u << 6,     // stand-alone flag wait (publish/wait pair)
   kStatusBadArgs = 1u << 7,      // kernel refused its arguments
+  kStatusBadIndex = 1u << 8,     // plan executor: embedding index outside [0, V)
 };
 
 // Limit of every mbarrier wait: far beyond any legal wait inside one kernel.
@@ -233,6 +235,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Same with A and B fp16 (a_format = b_format = 0); both operands must be fp16.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // ---------------------------------------------------------------- named barriers
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -302,6 +309,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&u);
   return __bfloat1622float2(v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
 }
 
 __device__ __forceinline__ float bf16_round(float x) {
