@@ -2,6 +2,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.h"
@@ -81,15 +83,19 @@ static double wave_eff(long tiles, int sms) {
 
 int pick_bn_store(int M, int N, int sms) {
   const int cands[3] = {256, 224, 128};
+  // relative throughput of one tile: a 128-wide tile moves 1.33x the operand bytes per
+  // FLOP of a 256-wide one and measured ~0.65 of its rate on B200 (fp16 M=8192 N=2048
+  // row chunks: ~775 against ~1300 TFLOP/s)
+  const double tile_eff[3] = {1.0, 0.97, 0.65};
   const long mblk = (M + kBM - 1) / kBM;
   int best = 256;
   double best_score = -1;
-  for (int bn : cands) {
+  for (int i = 0; i < 3; ++i) {
+    const int bn = cands[i];
     const long tiles = mblk * ((N + bn - 1) / bn);
     // efficiency of waves, times column utilisation of the last N block
     const double col_util = double(N) / double(((N + bn - 1) / bn) * bn);
-    // wider tiles read A fewer times; small bias towards them
-    const double score = wave_eff(tiles, sms) * col_util * (1.0 + 0.02 * (bn / 32));
+    const double score = wave_eff(tiles, sms) * col_util * tile_eff[i];
     if (score > best_score + 1e-9) {
       best_score = score;
       best = bn;
@@ -116,6 +122,19 @@ int pick_bn_silu(int M, int n_out, int sms) {
   return best;
 }
 
+// Tile raster of a plain GEMM.  Row blocks fastest (one band over all rows) keeps a B
+// column block hot while a wave sweeps the rows and re-reads A once per column block;
+// that is right while A stays in L2.  When A is too large for that (tall activations, a
+// small weight) column blocks go fastest instead (band = 1), so each A row block is read
+// once and the small B stays resident.  KRB_GEMM_RASTER=row|col forces one order.
+static int pick_band(long M, long N, long K, int num_m) {
+  static const char *force = std::getenv("KRB_GEMM_RASTER");
+  if (force && std::strcmp(force, "row") == 0) return num_m;
+  if (force && std::strcmp(force, "col") == 0) return 1;
+  const double a_bytes = double(M) * double(K) * 2.0, b_bytes = double(N) * double(K) * 2.0;
+  return (a_bytes > 48e6 && b_bytes < 24e6) ? 1 : num_m;
+}
+
 template <int BN, int MODE>
 static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int n_b_rows, int K,
                         const EpiArgs &ea, int grid_limit, uint32_t *status, cudaStream_t stream) {
@@ -132,7 +151,7 @@ static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int
   TileSched ts;
   ts.num_m = (M + kBM - 1) / kBM;
   ts.num_n = (n_b_rows + BN - 1) / BN;
-  ts.band = ts.num_m;
+  ts.band = pick_band(M, n_b_rows, K, ts.num_m);
   const int tiles = ts.num_m * ts.num_n;
   int grid = std::min(tiles, sm_count(dev));
   if (grid_limit > 0) grid = std::min(grid, grid_limit);

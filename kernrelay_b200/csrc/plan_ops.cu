@@ -63,9 +63,12 @@ struct Ew {
 };
 
 __device__ __forceinline__ float gelu_f(float x) {
-  // tanh-form GELU written as x * sigmoid(2 z), z = sqrt(2/pi) (x + 0.044715 x^3)
+  // tanh-form GELU written as x * sigmoid(2 z), z = sqrt(2/pi) (x + 0.044715 x^3), with
+  // the hardware exp2 / reciprocal approximations (relative error ~1e-6, far below the
+  // fp16 output's 2^-11): the accurate expf + IEEE divide made this kernel issue-bound.
+  // exp overflow gives rcp(inf) = 0, so large negative x returns -0 like the exact form.
   const float z = 1.5957691216057308f * (x + 0.044715f * x * x * x);
-  return x / (1.0f + expf(-z));
+  return x * __frcp_rn(1.0f + __expf(-z));
 }
 
 template <int KIND>
@@ -88,24 +91,44 @@ __device__ __forceinline__ float ew_op(float a, float b, float k, uint32_t iters
 }
 
 template <int KIND>
+__device__ __forceinline__ uint4 ew_vec8(uint4 va, uint4 vb, float k, uint32_t iters) {
+  const __half2 *ha = reinterpret_cast<const __half2 *>(&va);
+  const __half2 *hb = reinterpret_cast<const __half2 *>(&vb);
+  uint4 vo;
+  __half2 *ho = reinterpret_cast<__half2 *>(&vo);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 fa = __half22float2(ha[e]);
+    const float2 fb = __half22float2(hb[e]);
+    ho[e] = __floats2half2_rn(ew_op<KIND>(fa.x, fb.x, k, iters), ew_op<KIND>(fa.y, fb.y, k, iters));
+  }
+  return vo;
+}
+
+// Two 16-byte vectors per thread and iteration (both loads issued before any math) so
+// each SM keeps enough bytes in flight to cover HBM latency.
+template <int KIND>
 __global__ void ew_vec_kernel(const __half *a, const __half *b, __half *out, uint64_t nvec,
                               float k, uint32_t iters) {
-  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < nvec;
-       i += uint64_t(gridDim.x) * blockDim.x) {
-    const uint4 va = reinterpret_cast<const uint4 *>(a)[i];
-    uint4 vb = make_uint4(0, 0, 0, 0);
-    if constexpr (KIND == Ew::Add) vb = reinterpret_cast<const uint4 *>(b)[i];
-    const __half2 *ha = reinterpret_cast<const __half2 *>(&va);
-    const __half2 *hb = reinterpret_cast<const __half2 *>(&vb);
-    uint4 vo;
-    __half2 *ho = reinterpret_cast<__half2 *>(&vo);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 fa = __half22float2(ha[e]);
-      const float2 fb = __half22float2(hb[e]);
-      ho[e] = __floats2half2_rn(ew_op<KIND>(fa.x, fb.x, k, iters), ew_op<KIND>(fa.y, fb.y, k, iters));
+  const uint4 *va = reinterpret_cast<const uint4 *>(a);
+  const uint4 *vb = reinterpret_cast<const uint4 *>(b);
+  uint4 *vo = reinterpret_cast<uint4 *>(out);
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;
+  for (; i + stride < nvec; i += 2 * stride) {
+    const uint4 a0 = va[i], a1 = va[i + stride];
+    uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
+    if constexpr (KIND == Ew::Add) {
+      b0 = vb[i];
+      b1 = vb[i + stride];
     }
-    reinterpret_cast<uint4 *>(out)[i] = vo;
+    vo[i] = ew_vec8<KIND>(a0, b0, k, iters);
+    vo[i + stride] = ew_vec8<KIND>(a1, b1, k, iters);
+  }
+  if (i < nvec) {
+    uint4 b0 = make_uint4(0, 0, 0, 0);
+    if constexpr (KIND == Ew::Add) b0 = vb[i];
+    vo[i] = ew_vec8<KIND>(va[i], b0, k, iters);
   }
 }
 
@@ -123,6 +146,19 @@ __global__ void cast_kernel(const __half *in, float *out, uint64_t n) {
   for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
        i += uint64_t(gridDim.x) * blockDim.x)
     out[i] = __half2float(in[i]);
+}
+
+// 8 halves in (16 bytes), 8 floats out (two 16-byte stores)
+__global__ void cast_vec_kernel(const uint4 *in, float4 *out, uint64_t nvec) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < nvec;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint4 u = in[i];
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+    const float2 f0 = __half22float2(h[0]), f1 = __half22float2(h[1]);
+    const float2 f2 = __half22float2(h[2]), f3 = __half22float2(h[3]);
+    out[2 * i] = make_float4(f0.x, f0.y, f1.x, f1.y);
+    out[2 * i + 1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+  }
 }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -195,6 +231,134 @@ __global__ void __launch_bounds__(kRowThreads) layernorm_rows_kernel(
     const float d = (__half2float(x[c]) - mean) * rstd;
     y[c] = __float2half_rn(d * __half2float(w[c]) + __half2float(b[c]));
   }
+}
+
+// Warp-per-row forms for rows of up to 4096 halves with cols % 8 == 0 (16-byte vectors):
+// the row stays in registers (VPL uint4 per lane), every reduction is a warp shuffle, and
+// each CTA handles 8 rows, so HBM sees one read and one write per element.
+constexpr int kRowWarps = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int VPL, bool kSoftmax>
+__global__ void __launch_bounds__(kRowWarps * 32) row_warp_kernel(
+    const __half *in, const __half *w, const __half *b, __half *out, int64_t rows, int cols,
+    float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = int64_t(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = cols >> 3;
+  const uint4 *x = reinterpret_cast<const uint4 *>(in + row * cols);
+  float v[VPL][8];
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = j * 32 + lane;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (c < nvec) u = x[c];
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      v[j][2 * e] = f.x;
+      v[j][2 * e + 1] = f.y;
+    }
+  }
+  float a = 0.f, m = 0.f;
+  if constexpr (kSoftmax) {
+    m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (j * 32 + lane < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, v[j][e]);
+    m = warp_max(m);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (j * 32 + lane < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          v[j][e] = expf(v[j][e] - m);
+          a += v[j][e];
+        }
+    a = 1.0f / warp_sum(a);
+  } else {
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a += v[j][e];  // padding lanes hold zeros
+    m = warp_sum(a) / float(cols);
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      if (j * 32 + lane < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[j][e] - m;
+          q += d * d;
+        }
+    a = rsqrtf(warp_sum(q) / float(cols) + eps);
+  }
+  uint4 *y = reinterpret_cast<uint4 *>(out + row * cols);
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int c = j * 32 + lane;
+    if (c >= nvec) continue;
+    float r[8];
+    if constexpr (kSoftmax) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = v[j][e] * a;
+    } else {
+      const uint4 wu = reinterpret_cast<const uint4 *>(w)[c];
+      const uint4 bu = reinterpret_cast<const uint4 *>(b)[c];
+      const __half2 *wh = reinterpret_cast<const __half2 *>(&wu);
+      const __half2 *bh = reinterpret_cast<const __half2 *>(&bu);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 wf = __half22float2(wh[e]), bf = __half22float2(bh[e]);
+        r[2 * e] = (v[j][2 * e] - m) * a * wf.x + bf.x;
+        r[2 * e + 1] = (v[j][2 * e + 1] - m) * a * wf.y + bf.y;
+      }
+    }
+    uint4 o;
+    __half2 *oh = reinterpret_cast<__half2 *>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) oh[e] = __floats2half2_rn(r[2 * e], r[2 * e + 1]);
+    y[c] = o;
+  }
+}
+
+// Launches the warp-per-row kernel when the row fits (returns false otherwise).
+template <bool kSoftmax>
+bool launch_row_warp(const __half *in, const __half *w, const __half *b, __half *out,
+                     int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
+  if (cols % 8 != 0 || cols > 4096 || !aligned16(in) || !aligned16(out) ||
+      (!kSoftmax && (!aligned16(w) || !aligned16(b))))
+    return false;
+  const int vpl = int((cols / 8 + 31) / 32);
+  const unsigned grid = unsigned((rows + kRowWarps - 1) / kRowWarps);
+  const int c = int(cols);
+  switch (vpl) {
+    case 1: row_warp_kernel<1, kSoftmax><<<grid, kRowWarps * 32, 0, stream>>>(in, w, b, out, rows, c, eps); break;
+    case 2: row_warp_kernel<2, kSoftmax><<<grid, kRowWarps * 32, 0, stream>>>(in, w, b, out, rows, c, eps); break;
+    case 3:
+    case 4: row_warp_kernel<4, kSoftmax><<<grid, kRowWarps * 32, 0, stream>>>(in, w, b, out, rows, c, eps); break;
+    case 5:
+    case 6:
+    case 7:
+    case 8: row_warp_kernel<8, kSoftmax><<<grid, kRowWarps * 32, 0, stream>>>(in, w, b, out, rows, c, eps); break;
+    default: row_warp_kernel<16, kSoftmax><<<grid, kRowWarps * 32, 0, stream>>>(in, w, b, out, rows, c, eps); break;
+  }
+  KRB_CUDA(cudaGetLastError());
+  return true;
 }
 
 // ---- per-row sort / top-k: bitonic sort of 64-bit keys in shared memory, one CTA per row.
@@ -279,6 +443,14 @@ __global__ void embedding_kernel(const __half *weight, const int64_t *idx, __hal
   if (!ok && threadIdx.x == 0) atomicOr(status, kStatusBadIndex);
   const __half *src = weight + (ok ? id : 0) * cols;
   __half *dst = out + r * cols;
+  if (cols % 8 == 0 && (reinterpret_cast<uintptr_t>(weight) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+    for (int64_t c = threadIdx.x; c < cols / 8; c += blockDim.x)
+      d4[c] = ok ? s4[c] : make_uint4(0, 0, 0, 0);
+    return;
+  }
   for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) dst[c] = ok ? src[c] : __float2half(0.f);
 }
 
@@ -336,7 +508,11 @@ void scale_f16(const __half *in, __half *out, uint64_t n, float k, uint32_t iter
 
 void cast_f16_f32(const __half *in, float *out, uint64_t n, cudaStream_t stream) {
   if (n == 0) return;
-  cast_kernel<<<ew_grid(int64_t(n), cur_sms()), kEwThreads, 0, stream>>>(in, out, n);
+  if (n % 8 == 0 && aligned16(in) && aligned16(out))
+    cast_vec_kernel<<<ew_grid(int64_t(n / 8), cur_sms()), kEwThreads, 0, stream>>>(
+        reinterpret_cast<const uint4 *>(in), reinterpret_cast<float4 *>(out), n / 8);
+  else
+    cast_kernel<<<ew_grid(int64_t(n), cur_sms()), kEwThreads, 0, stream>>>(in, out, n);
   KRB_CUDA(cudaGetLastError());
 }
 
@@ -344,6 +520,7 @@ void softmax_rows_f16(const __half *in, __half *out, int64_t rows, int64_t cols,
                       cudaStream_t stream) {
   if (rows <= 0) return;
   if (cols <= 0) throw CudaError("softmax: empty rows");
+  if (launch_row_warp<true>(in, nullptr, nullptr, out, rows, cols, 0.f, stream)) return;
   softmax_rows_kernel<<<unsigned(rows), kRowThreads, 0, stream>>>(in, out, cols);
   KRB_CUDA(cudaGetLastError());
 }
@@ -352,6 +529,7 @@ void layernorm_rows_f16(const __half *in, const __half *w, const __half *b, __ha
                         int64_t rows, int64_t cols, float eps, cudaStream_t stream) {
   if (rows <= 0) return;
   if (cols <= 0) throw CudaError("layernorm: empty rows");
+  if (launch_row_warp<false>(in, w, b, out, rows, cols, eps, stream)) return;
   layernorm_rows_kernel<<<unsigned(rows), kRowThreads, 0, stream>>>(in, w, b, out, cols, eps);
   KRB_CUDA(cudaGetLastError());
 }

@@ -220,3 +220,123 @@ def test_plan_parity_two_ranks(krlib, cuda, name, tmp_path):
         res = libapi.plan_run(PLANS / "small" / f"{name}.json", devices="0,1", mode=mode, iters=2,
                               warmup=1, out_json=tmp_path / f"{mode}.json")
         _compare(res, ref, f"{name}/{mode}")
+
+
+# ---------------------------------------------------------------- every operator kind
+def _standalone(name, node, chunks=1, engine="aiv", col_tiles=0):
+    """A one-node schedule in the scheduler's standalone form (schedule.py:57-64): the node
+    split into `chunks` row tasks (or `col_tiles` matmul N tiles) on one engine lane."""
+    n = dict(node, id=name, engine=engine, preds=[], iters=node.get("iters", 1),
+             blocks=node.get("blocks", 1), dtype="fp16")
+    tasks = []
+    if col_tiles:
+        n.update(tiles=col_tiles, split=True)
+        w = n["n"] // col_tiles
+        for t in range(col_tiles):
+            tasks.append({"node": name, "tile": t, "wait": [], "publish": False,
+                          "in_row_off": 0, "in_rows": n["rows"], "out_row_off": 0,
+                          "n_off": t * w, "n_tiles": w, "out_col_off": t * w, "out_cols": w})
+    else:
+        n.update(tiles=chunks, split=chunks > 1)
+        r = n["rows"] // chunks
+        for t in range(chunks):
+            tasks.append({"node": name, "tile": t, "wait": [], "publish": False,
+                          "in_row_off": t * r, "in_rows": r, "out_row_off": t * r})
+    return {"dag": "ops_" + name, "group": "standalone", "nranks": 1, "nodes": [n],
+            "streams": {engine: tasks}}
+
+
+OP_CASES = {
+    "add": ({"op": "add", "rows": 256, "cols": 512}, 2),
+    "gelu_ragged": ({"op": "gelu", "rows": 100, "cols": 333}, 1),
+    "softmax_long": ({"op": "softmax", "rows": 64, "cols": 5000}, 1),
+    "softmax_warp": ({"op": "softmax", "rows": 128, "cols": 1000}, 2),
+    "layernorm_ragged": ({"op": "layernorm", "rows": 64, "cols": 300}, 1),
+    "layernorm_wide": ({"op": "layernorm", "rows": 96, "cols": 4096}, 3),
+    "cast": ({"op": "cast", "rows": 128, "cols": 256}, 2),
+    "topk": ({"op": "topk", "rows": 64, "cols": 1000, "k": 16}, 2),
+    "sort": ({"op": "sort", "rows": 32, "cols": 700}, 1),
+    "embedding": ({"op": "embedding", "rows": 128, "cols": 256, "dim0": 1000}, 2),
+    "aiv_scale": ({"op": "custom_aiv_scale", "rows": 64, "cols": 512, "iters": 3}, 1),
+    "mix_scale": ({"op": "custom_mix_scale", "rows": 64, "cols": 512, "iters": 2}, 2),
+    "aic_mac": ({"op": "custom_aic_mac", "rows": 64, "cols": 512, "iters": 2, "blocks": 4}, 2),
+    "aicpu_scale": ({"op": "custom_aicpu_scale", "rows": 64, "cols": 256}, 1),
+}
+
+
+def _op_schedule(name):
+    if name == "matmul_ntiles":
+        return _standalone(name, {"op": "matmul", "rows": 256, "cols": 512, "k": 128, "n": 512},
+                           engine="aic", col_tiles=2)
+    node, chunks = OP_CASES[name]
+    return _standalone(name, node, chunks)
+
+
+OP_NAMES = sorted(OP_CASES) + ["matmul_ntiles"]
+
+
+@pytest.mark.parametrize("name", OP_NAMES)
+def test_op_schedules_validate_and_run_on_oracle(krlib, name, tmp_path):
+    sched = _op_schedule(name)
+    p = tmp_path / "s.json"
+    p.write_text(json.dumps(sched))
+    assert krlib.plan_check(p)["tasks"] == len(next(iter(sched["streams"].values())))
+    r = plan_ref.PlanOracle(sched).run()
+    assert np.isfinite(r["checksum"]) and r["node_abs"][name] > 0
+
+
+def test_oracle_topk_sort_semantics():
+    sched = _op_schedule("topk")
+    o = plan_ref.PlanOracle(sched)
+    o.run()
+    node = sched["nodes"][0]
+    seed = plan_ref.node_seed("topk", 0)
+    x = plan_ref.det_values(seed + 1, node["rows"] * node["cols"]).reshape(node["rows"], node["cols"])
+    vals = o.buf[0]["topk"]["out"].view(np.float16)[:node["rows"] * 16].reshape(node["rows"], 16)
+    idx = o.buf[0]["topk"]["out2"].reshape(node["rows"], 16)
+    assert np.array_equal(vals.astype(np.float32), -np.sort(-x, axis=1)[:, :16])
+    assert np.array_equal(np.take_along_axis(x, idx, axis=1), vals.astype(np.float32))
+    # ties (23 distinct values) resolve to the lower index first
+    for r in range(node["rows"]):
+        for j in range(15):
+            if vals[r, j] == vals[r, j + 1]:
+                assert idx[r, j] < idx[r, j + 1]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", OP_NAMES)
+def test_op_schedules_gpu_parity(krlib, cuda, name, tmp_path):
+    from kernrelay_b200 import libapi
+    sched = _op_schedule(name)
+    p = tmp_path / "s.json"
+    p.write_text(json.dumps(sched))
+    ref = plan_ref.PlanOracle(sched).run()
+    for mode in ("direct", "graph"):
+        res = libapi.plan_run(p, devices="0", mode=mode, iters=2, warmup=1,
+                              out_json=tmp_path / f"{mode}.json")
+        _compare(res, ref, f"{name}/{mode}")
+
+
+# ---------------------------------------------------------------- planner cost tables (row f3)
+def test_planner_curve_schedules_validate(krlib, tmp_path):
+    from kernrelay_b200 import planner_costs as pc
+    n = 0
+    for name, op, strategy, shape in pc.CURVE_CASES:
+        ks = [k for k in pc.KS if pc.valid_k(op, strategy, shape, k)]
+        assert 1 in ks and len(ks) >= 4, name
+        for k in ks:
+            s = pc.split_schedule(name, op, strategy, shape, k)
+            p = tmp_path / f"{name}_{k}.json"
+            p.write_text(json.dumps(s))
+            assert krlib.plan_check(p)["tasks"] == k
+            n += 1
+    assert n > 80
+
+
+def test_planner_fit_recovers_linear_total():
+    from kernrelay_b200 import planner_costs as pc
+    samples = {k: 250.0 + 7.5 * (k - 1) for k in (1, 2, 4, 8, 16)}
+    f = pc.fit(samples, 16)
+    assert f["slope_us_per_tile"] == pytest.approx(7.5)
+    assert f["intercept_us"] == pytest.approx(250.0)
+    assert f["mape_all"] < 1e-12 and f["holdout_ape"] < 1e-12
