@@ -124,3 +124,23 @@ def test_relay_plan_rejects_bad_shapes(krlib):
         krlib.relay_plan(2048, 3584, 32, 1, 0, 256)    # 64-row tiles < 128
     with pytest.raises(krlib.KrbError):
         krlib.relay_plan(2048, 3584, 4, 2, 2, 256)     # rank out of range
+
+
+def test_relay_trace_summary_math():
+    """kernrelay_b200.relay_trace turns per-CTA globaltimer stamps into per-tile phases and
+    NVLink rates: direct pulls (k-1)*R*H*2 bytes per tile between 'partials arrived' and
+    'norm done'."""
+    import numpy as np
+    from kernrelay_b200 import relay_trace
+    tr = np.zeros((4, 48), dtype=np.uint64)
+    base = 1_000_000
+    tr[:, 0] = base
+    tr[:, 1] = base + 100_000          # GEMM done at 100 us
+    tr[:, 3] = base + 50_000           # tile 0 partials at 50 us
+    tr[:, 6] = base + 60_000           # tile 0 norm done at 60 us
+    s = relay_trace.summarise(tr, k=2, T=4, R=512, H=3584, kind="direct")
+    assert s["gemm_done_us"] == 100.0
+    t0 = s["tiles"][0]
+    assert t0["partials_arrived_us"] == 50.0 and t0["norm_done_us"] == 60.0
+    assert abs(t0["nvlink_gbs"] - 512 * 3584 * 2 / 10.0 / 1e3) < 1e-6
+    assert "nvlink_gbs" not in s["tiles"][1]
