@@ -247,7 +247,8 @@ def qk_norm_rope(qkv, HQ, HKV, D, cos, sin, q_norm=None, k_norm=None, eps=1e-6, 
 
 
 def attention(qkv, HQ, HKV, D, scale, impl=0, status=None, stream=None):
-    """impl 0 auto, 1 mma.sync, 2 tcgen05 (D=128)."""
+    """Causal GQA attention over the fused qkv buffer with the tcgen05 kernel (head_dim 64
+    or 128); impl 0 and 2 both select it."""
     import torch
     S = qkv.shape[0]
     out = torch.empty((S, HQ * D), dtype=torch.bfloat16, device=qkv.device)

@@ -642,28 +642,22 @@ KRB_EXPORT int krb_qk_norm_rope_bf16(void *qkv, int S, int HQ, int HKV, int D, c
 KRB_EXPORT int krb_attention_prefill_bf16(const void *qkv, void *out, int S, int HQ, int HKV, int D,
                                           float scale, int impl, uint32_t *status, void *stream) {
   KRB_OP_BEGIN
-  const bool tc = impl == 2 || (impl == 0 && D == 128);
-  if (impl < 0 || impl > 2) throw std::runtime_error("attention: impl must be 0, 1 or 2");
-  if (!tc) {
-    krb::attention_prefill_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(out), S, HQ, HKV,
-                                D, scale, as_stream(stream));
-  } else {
-    // V^T scratch, stream-ordered: allocated and released on the caller's stream
-    cudaStream_t s = as_stream(stream);
-    const long ldv = (long(S) + 7) / 8 * 8;
-    void *vt = nullptr;
-    KRB_CUDA(cudaMallocAsync(&vt, size_t(HKV) * D * ldv * 2, s));
-    try {
-      krb::attention_vt_bf16(static_cast<const bf *>(qkv), static_cast<bf *>(vt), ldv, S, HQ, HKV,
-                             D, s);
-      krb::attention_tc_bf16(static_cast<const bf *>(qkv), static_cast<const bf *>(vt), ldv,
-                             static_cast<bf *>(out), S, HQ, HKV, D, scale, status, s);
-    } catch (...) {
-      cudaFreeAsync(vt, s);
-      throw;
-    }
-    KRB_CUDA(cudaFreeAsync(vt, s));
+  // impl 0 / 2: the tcgen05 kernel (the only attention of this build; 1 was mma.sync)
+  if (impl != 0 && impl != 2) throw std::runtime_error("attention: impl must be 0 or 2 (tcgen05)");
+  // V^T scratch, stream-ordered: allocated and released on the caller's stream
+  cudaStream_t s = as_stream(stream);
+  const long ldv = (long(S) + 7) / 8 * 8;
+  void *vt = nullptr;
+  KRB_CUDA(cudaMallocAsync(&vt, size_t(HKV) * D * ldv * 2, s));
+  try {
+    krb::attention_vt(static_cast<const bf *>(qkv), static_cast<__half *>(vt), ldv, S, HQ, HKV, D, s);
+    krb::attention_tc_bf16(static_cast<const bf *>(qkv), static_cast<const __half *>(vt), ldv,
+                           static_cast<bf *>(out), S, HQ, HKV, D, scale, status, s);
+  } catch (...) {
+    cudaFreeAsync(vt, s);
+    throw;
   }
+  KRB_CUDA(cudaFreeAsync(vt, s));
   KRB_OP_END
 }
 

@@ -1,25 +1,13 @@
 // Causal GQA prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // Replaces aclnnFlashAttentionScore (BSND, sparse_mode 3, scale 1/sqrt(D);
-// qwen_main.cpp:591-614) for head_dim 128.  One CTA = one query head x 128
-// query rows; it walks the 128-key blocks 0..diagonal:
-//
-//   warp 0      TMA: Q once (2 x 64-column chunks, 128-byte swizzle); K blocks
-//               from the fused qkv buffer and V^T blocks from a transposed copy
-//               of V ([kv_head * D + d][key]), double-buffered.
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into TMEM (two S buffers),
-//               then O += P_{j-1} V_{j-1} with P read from TMEM (the "TS" form).
-//               QK^T of block j is issued before PV of block j-1 so the tensor
-//               pipe has work while the softmax of j-1 finishes.
-//   warps 2..5  softmax: thread = query row = TMEM lane.  Loads the 128 scores of
-//               its row, applies the causal mask, keeps the running max and sum
-//               in fp32 (log2 domain), writes P (bf16, rounded; the row sum uses
-//               the rounded values) into TMEM, rescales the O row in TMEM when
-//               the running max grew, and finally normalises O and stores bf16.
-//
-// Every operand is K-major with the same 128-byte-swizzle descriptor: Q [row][d],
-// K [key][d], V^T [d][key] and P [row][key] (TMEM: lane = row, 2 keys per column).
-// All waits are bounded (status bits as in the GEMM).
+// qwen_main.cpp:591-614) for head_dim 64 and 128.  One CTA = one query head x two
+// consecutive 128-row query tiles; it walks the 128-key blocks up to the diagonal.
+// Q and K tiles come from the fused qkv buffer, V from a transposed copy
+// ([kv_head * D + d][key]) so that every operand is K-major with the same
+// 128-byte-swizzle descriptor: Q [row][d], K [key][d], V^T [d][key] and P [row][key]
+// (TMEM: lane = row, 2 keys per column).  All waits are bounded (status bits as in
+// the GEMM).
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
@@ -32,44 +20,9 @@ namespace krb {
 
 namespace {
 
-constexpr int kAttnThreads = 192;
-constexpr int kTileRows = 128;       // query rows per CTA = keys per block
+constexpr int kTileRows = 128;               // query rows per tile = keys per block
 constexpr uint32_t kChunkBytes = 128 * 128;  // 128 rows x 64 bf16 (one swizzle width)
-constexpr uint32_t kTileBytes = 2 * kChunkBytes;  // 128 rows x 128 bf16
-// TMEM columns
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256, kColP = 384, kTmemCols = 512;
-
-struct AttnSmem {
-  uint8_t *q;  // K stage s at q + (1 + s) * kTileBytes, V^T stage s at q + (3 + s) * kTileBytes
-  uint64_t *q_full, *kv_full, *kv_empty, *s_full, *s_free, *p_ready, *o_done;
-  uint32_t *tmem_slot;
-};
-
-__device__ __forceinline__ AttnSmem carve(uint8_t *raw) {
-  AttnSmem a;
-  uint8_t *base =
-      reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-  a.q = base;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + 5 * kTileBytes);
-  a.q_full = bars;
-  a.kv_full = bars + 1;   // [2]
-  a.kv_empty = bars + 3;  // [2]
-  a.s_full = bars + 5;    // [2]
-  a.s_free = bars + 7;    // [2]
-  a.p_ready = bars + 9;
-  a.o_done = bars + 10;
-  a.tmem_slot = reinterpret_cast<uint32_t *>(bars + 11);
-  return a;
-}
-
-__device__ __forceinline__ uint8_t *k_stage(const AttnSmem &a, int st) {
-  return a.q + (1 + st) * kTileBytes;
-}
-__device__ __forceinline__ uint8_t *v_stage(const AttnSmem &a, int st) {
-  return a.q + (3 + st) * kTileBytes;
-}
-
-constexpr uint32_t kAttnSmemBytes = 5 * kTileBytes + 11 * 8 + 16 + 1024;
+constexpr uint32_t kTmemCols = 512;
 
 // descriptor of k-step kk (16 elements) of a 128 x 128 K-major tile stored as two
 // 64-element chunks of 128 rows (128-byte swizzle)
@@ -155,23 +108,33 @@ __device__ __forceinline__ void tmem_st_32x32_x16(uint32_t taddr, const uint32_t
 //               one tile's softmax runs, the tensor pipe works on the other tile.
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B (thread = row).
 // TMEM (512 columns): tile X's S at 256X (P written over its first 64 columns as
-// packed bf16 pairs once read), O at 256X + 128.  The softmax reads S twice
-// (row max, then exp and P) so a thread holds 32 scores at a time.
+// packed fp16 pairs once read), O at 256X + 128 (D columns).  PV multiplies fp16 P by
+// fp16 V^T (the transposed copy of V is written in fp16).  The softmax reads S
+// twice (row max, then exp and P) so a thread holds 32 scores at a time.
+// Shared memory: six tiles of 256*D bytes (Q_A, Q_B, K x2, V^T x2): a Q or K tile is
+// D/64 chunks of 128 rows x 64 elements, a V^T tile two chunks of D rows x 64 keys.
 constexpr int kAttn2Threads = 320;
-constexpr uint32_t kAttn2SmemBytes = 6 * kTileBytes + 12 * 8 + 16 + 1024;
+
+template <int D>
+struct Attn2Cfg {
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  static constexpr uint32_t kTile = 256u * D;     // bytes of one Q, K or V^T tile
+  static constexpr uint32_t kVChunk = 128u * D;   // D rows x 64 keys
+  static constexpr uint32_t kSmem = 6 * kTile + 12 * 8 + 16 + 1024;
+};
 
 struct Attn2Smem {
-  uint8_t *q;  // Q_A, Q_B; K stage s at q + (2 + s) * kTileBytes; V^T stage s at q + (4 + s) * kTileBytes
+  uint8_t *q;  // Q_A, Q_B; K stage s at q + (2 + s) * tile; V^T stage s at q + (4 + s) * tile
   uint64_t *q_full, *kv_full, *kv_empty, *s_full, *p_ready, *o_done;  // [1], [2], [2], [2], [2], [2]
   uint32_t *tmem_slot;
 };
 
-__device__ __forceinline__ Attn2Smem carve2(uint8_t *raw) {
+__device__ __forceinline__ Attn2Smem carve2(uint8_t *raw, uint32_t tile_bytes) {
   Attn2Smem a;
   uint8_t *base =
       reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   a.q = base;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + 6 * kTileBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + 6 * tile_bytes);
   a.q_full = bars;
   a.kv_full = bars + 1;
   a.kv_empty = bars + 3;
@@ -184,9 +147,9 @@ __device__ __forceinline__ Attn2Smem carve2(uint8_t *raw) {
 
 // One key block of the two-tile kernel's softmax for one row (thread): row max
 // (pass 1), lazy O rescale, P = 2^(s*scale - m) rounded to bf16 written over S's
-// first 64 columns (pass 2; chunk c's P lands on columns already read), and the
+// first 64 columns as fp16 pairs (pass 2; chunk c's P lands on columns already read), and the
 // running max / sum update.  The chunk loops stay rolled (code size).
-template <bool kMask>
+template <bool kMask, int D>
 __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_col, int key0,
                                                     int row, int S, float scale_log2, bool has_o,
                                                     float &m_run, float &l_run) {
@@ -216,7 +179,7 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
   // PV of the previous block is complete (the commit that released this S covers it)
   if (has_o && __any_sync(0xffffffffu, grow)) {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
       tmem_ld_32x32(o_col + c * 32, r);
       tmem_wait_ld();
@@ -245,9 +208,11 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
       const float a0 = fmaf(s0, scale_log2, -m_use), a1 = fmaf(s1, scale_log2, -m_use);
       const float p0 = (e & 1) ? exp2_poly(a0) : ex2_approx(a0);
       const float p1 = (e & 1) ? exp2_poly(a1) : ex2_approx(a1);
-      pk[e] = pack_bf16x2(p0, p1);
+      // P in fp16 (P <= 2^kRescaleLog2 = 256: far inside its range; 8x finer than bf16)
+      pk[e] = pack_f16x2(p0, p1);
       // the row sum uses the rounded probabilities that the PV product sees
-      r8[e & 7] += __uint_as_float(pk[e] << 16) + __uint_as_float(pk[e] & 0xffff0000u);
+      const float2 pr = __half22float2(*reinterpret_cast<const __half2 *>(&pk[e]));
+      r8[e & 7] += pr.x + pr.y;
     }
     tmem_st_32x32_x16(s_col + c * 16, pk);
   }
@@ -259,26 +224,29 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
 
 }  // namespace
 
+// Grid (heads of this launch, tile pairs); query head h = h0 + blockIdx.x reads KV head
+// kv0 + blockIdx.x / group.  HQ is the head count of the qkv layout (K columns start at
+// HQ * D).  Pairs are dispatched longest first over all heads (blocks go x-fastest).
+template <int D>
 __global__ void __launch_bounds__(kAttn2Threads, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_vt,
-                    __nv_bfloat16 *__restrict__ out, long ldo, int S, int HQ, int group,
-                    float scale_log2, uint32_t *status) {
+                    __nv_bfloat16 *__restrict__ out, long ldo, int S, int HQ, int h0, int kv0,
+                    int group, float scale_log2, uint32_t *status) {
+  using C = Attn2Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
-  const Attn2Smem sm = carve2(smem_raw);
+  const Attn2Smem sm = carve2(smem_raw, C::kTile);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // grid (HQ, tile pairs), longest pair first over all heads (see attn_tc_kernel)
   const int npairs = gridDim.y;
   const int pr = npairs - 1 - blockIdx.y;
-  const int h = blockIdx.x;
-  const int kvh = h / group;
+  const int h = h0 + blockIdx.x;
+  const int kvh = kv0 + blockIdx.x / group;
   const int nqb = (S + kTileRows - 1) / kTileRows;
   const int qa = 2 * pr, qb = 2 * pr + 1;
   const bool has_b = qb < nqb;
   const int nA = qa + 1;              // key blocks of tile A (causal)
   const int nB = has_b ? qb + 1 : 0;  // key blocks of tile B
   const int nkb = has_b ? nB : nA;
-  constexpr int D = 128;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tm_qk);
@@ -306,12 +274,13 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     if (lane == 0) {
       // ---------------- TMA producer
       bool ok = true;
-      mbar_arrive_expect_tx(sm.q_full, (has_b ? 2 : 1) * kTileBytes);
-      tma_load_2d(sm.q, &tm_qk, sm.q_full, h * D, qa * kTileRows);
-      tma_load_2d(sm.q + kChunkBytes, &tm_qk, sm.q_full, h * D + 64, qa * kTileRows);
-      if (has_b) {
-        tma_load_2d(sm.q + kTileBytes, &tm_qk, sm.q_full, h * D, qb * kTileRows);
-        tma_load_2d(sm.q + kTileBytes + kChunkBytes, &tm_qk, sm.q_full, h * D + 64, qb * kTileRows);
+      mbar_arrive_expect_tx(sm.q_full, (has_b ? 2 : 1) * C::kTile);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sm.q + c * kChunkBytes, &tm_qk, sm.q_full, h * D + 64 * c, qa * kTileRows);
+        if (has_b)
+          tma_load_2d(sm.q + C::kTile + c * kChunkBytes, &tm_qk, sm.q_full, h * D + 64 * c,
+                      qb * kTileRows);
       }
       int issued = 0;
       for (int j = 0; j < nkb && ok; ++j) {
@@ -321,14 +290,15 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kTileBytes);
-        uint8_t *kst = sm.q + (2 + st) * kTileBytes;
-        uint8_t *vst = sm.q + (4 + st) * kTileBytes;
+        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * C::kTile);
+        uint8_t *kst = sm.q + (2 + st) * C::kTile;
+        uint8_t *vst = sm.q + (4 + st) * C::kTile;
         const int kc = (HQ + kvh) * D;
-        tma_load_2d(kst, &tm_qk, &sm.kv_full[st], kc, j * kTileRows);
-        tma_load_2d(kst + kChunkBytes, &tm_qk, &sm.kv_full[st], kc + 64, j * kTileRows);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(kst + c * kChunkBytes, &tm_qk, &sm.kv_full[st], kc + 64 * c, j * kTileRows);
         tma_load_2d(vst, &tm_vt, &sm.kv_full[st], j * kTileRows, kvh * D);
-        tma_load_2d(vst + kChunkBytes, &tm_vt, &sm.kv_full[st], j * kTileRows + 64, kvh * D);
+        tma_load_2d(vst + C::kVChunk, &tm_vt, &sm.kv_full[st], j * kTileRows + 64, kvh * D);
         ++issued;
       }
       // no TMA write may still be in flight when the CTA exits
@@ -340,15 +310,20 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
+      constexpr uint32_t idesc_o = idesc_f16_f32(128, D);  // P and V^T both fp16
       // descriptors of every smem tile, computed once; k-step kk of a tile is the
       // base descriptor plus the step's byte offset >> 4 in the start-address field
       // (all offsets stay inside the 14-bit field: shared memory < 256 KB)
-      const uint64_t dq0 = tile_desc(sm.q, 0), dq1 = tile_desc(sm.q + kTileBytes, 0);
-      const uint64_t dk0 = tile_desc(sm.q + 2 * kTileBytes, 0), dk1 = tile_desc(sm.q + 3 * kTileBytes, 0);
-      const uint64_t dv0 = tile_desc(sm.q + 4 * kTileBytes, 0), dv1 = tile_desc(sm.q + 5 * kTileBytes, 0);
+      const uint64_t dq0 = tile_desc(sm.q, 0), dq1 = tile_desc(sm.q + C::kTile, 0);
+      const uint64_t dk0 = tile_desc(sm.q + 2 * C::kTile, 0), dk1 = tile_desc(sm.q + 3 * C::kTile, 0);
+      const uint64_t dv0 = tile_desc(sm.q + 4 * C::kTile, 0), dv1 = tile_desc(sm.q + 5 * C::kTile, 0);
+      // Q / K: 16 head dims per step, 64 per chunk of 128 rows; V^T: 16 keys per step,
+      // 64 per chunk of D rows
       auto kstep = [](int kk) -> uint64_t {
         return static_cast<uint64_t>(((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4);
+      };
+      auto vstep = [](int kk) -> uint64_t {
+        return static_cast<uint64_t>(((kk >> 2) * C::kVChunk + (kk & 3) * 32) >> 4);
       };
       // issue order per key block j: PV(A,j), QK(A,j+1), PV(B,j), QK(B,j+1) -- tile
       // A's next scores are computed while tile B's softmax runs and vice versa
@@ -381,7 +356,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
           const uint64_t vd = st ? dv1 : dv0;
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_bf16_ts(tmem + 256 * x + 128, tmem + 256 * x + kk * 8, vd + kstep(kk), idesc_o,
+            umma_bf16_ts(tmem + 256 * x + 128, tmem + 256 * x + kk * 8, vd + vstep(kk), idesc_o,
                          (j > 0 || kk > 0));
           umma_commit(&sm.o_done[x]);
           if (j + 1 < nx) {
@@ -416,9 +391,9 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
       // blocks: a uniform branch picks the masked or the plain instantiation (a
       // per-element short-circuit test cost ~10x the max loop itself)
       if (key0 + kTileRows - 1 > q0 || key0 + kTileRows > S)
-        attn2_softmax_block<true>(s_col, o_col, key0, row, S, scale_log2, j > 0, m_run, l_run);
+        attn2_softmax_block<true, D>(s_col, o_col, key0, row, S, scale_log2, j > 0, m_run, l_run);
       else
-        attn2_softmax_block<false>(s_col, o_col, key0, row, S, scale_log2, j > 0, m_run, l_run);
+        attn2_softmax_block<false, D>(s_col, o_col, key0, row, S, scale_log2, j > 0, m_run, l_run);
       tc_fence_before();
       mbar_arrive(&sm.p_ready[x]);
     }
@@ -455,273 +430,57 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_vt,
-                   __nv_bfloat16 *__restrict__ out, long ldo, int S, int HQ, int group,
-                   float scale_log2, uint32_t *status) {
-  extern __shared__ uint8_t smem_raw[];
-  const AttnSmem sm = carve(smem_raw);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  // grid (HQ, q tiles): blocks are dispatched x-fastest, so every head's longest
-  // causal row tile goes first and the shortest last (longest-processing-time
-  // order over the whole grid, not per head)
-  const int nqb = gridDim.y;
-  const int qb = nqb - 1 - blockIdx.y;
-  const int h = blockIdx.x;
-  const int kvh = h / group;
-  const int q0 = qb * kTileRows;
-  const int nkb = min(qb + 1, (S + kTileRows - 1) / kTileRows);
-  constexpr int D = 128;
-
-  if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tm_qk);
-    tma_prefetch_desc(&tm_vt);
-    mbar_init(sm.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.kv_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1);
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], 128);
-    }
-    mbar_init(sm.p_ready, 128);
-    mbar_init(sm.o_done, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(sm.tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *sm.tmem_slot;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
-      bool ok = true;
-      mbar_arrive_expect_tx(sm.q_full, kTileBytes);
-      tma_load_2d(sm.q, &tm_qk, sm.q_full, h * D, q0);
-      tma_load_2d(sm.q + kChunkBytes, &tm_qk, sm.q_full, h * D + 64, q0);
-      int issued = 0;
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&sm.kv_empty[st], ((j >> 1) & 1) ^ 1, kMbarLimitNs)) {
-          report_status(status, kStatusTmaWait);
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kTileBytes);
-        const int kc = (HQ + kvh) * D;
-        tma_load_2d(k_stage(sm, st), &tm_qk, &sm.kv_full[st], kc, j * kTileRows);
-        tma_load_2d(k_stage(sm, st) + kChunkBytes, &tm_qk, &sm.kv_full[st], kc + 64, j * kTileRows);
-        tma_load_2d(v_stage(sm, st), &tm_vt, &sm.kv_full[st], j * kTileRows, kvh * D);
-        tma_load_2d(v_stage(sm, st) + kChunkBytes, &tm_vt, &sm.kv_full[st], j * kTileRows + 64, kvh * D);
-        ++issued;
-      }
-      // no TMA write may still be in flight when the CTA exits
-      mbar_wait(sm.q_full, 0, kMbarLimitNs / 4);
-      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
-        mbar_wait(&sm.kv_full[j & 1], (j >> 1) & 1, kMbarLimitNs / 4);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D);
-      bool ok = mbar_wait(sm.q_full, 0, kMbarLimitNs);
-      for (int j = 0; j <= nkb && ok; ++j) {
-        if (j < nkb) {
-          const int st = j & 1;
-          ok = mbar_wait(&sm.kv_full[st], (j >> 1) & 1, kMbarLimitNs);
-          if (ok && j >= 2) ok = mbar_wait(&sm.s_free[st], ((j >> 1) - 1) & 1, kMbarLimitNs);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t sacc = tmem + (st ? kColS1 : kColS0);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_bf16(sacc, tile_desc(sm.q, kk), tile_desc(k_stage(sm, st), kk), idesc_s, kk > 0);
-          umma_commit(&sm.s_full[st]);
-        }
-        if (j >= 1) {
-          const int i = j - 1;
-          ok = mbar_wait(sm.p_ready, i & 1, kMbarLimitNs);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_bf16_ts(tmem + kColO, tmem + kColP + kk * 8, tile_desc(v_stage(sm, i & 1), kk), idesc_o,
-                         (i > 0 || kk > 0));
-          umma_commit(sm.o_done);
-          umma_commit(&sm.kv_empty[i & 1]);
-        }
-      }
-      if (!ok) report_status(status, kStatusMmaWait);
-    }
-  } else {
-    // ---------------- softmax / correction / epilogue (128 threads)
-    const int quad = warp & 3;
-    const int rloc = quad * 32 + lane;
-    const int row = q0 + rloc;
-    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      ok = mbar_wait(&sm.s_full[sb], (j >> 1) & 1, kMbarLimitNs);
-      if (!ok) break;
-      tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32(tmem + lane_addr + (sb ? kColS1 : kColS0) + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]);
-      }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[sb]);
-      const int key0 = j * kTileRows;
-      if (key0 + kTileRows - 1 > q0 || key0 + kTileRows > S) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (key0 + c > row || key0 + c >= S) s[c] = -INFINITY;
-      }
-      // row max with eight independent chains (scale_log2 > 0 commutes with max)
-      float m8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) m8[e] = s[e];
-#pragma unroll
-      for (int c = 8; c < 128; ++c) m8[c & 7] = fmaxf(m8[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
-      const bool grow = mx - m_run > kRescaleLog2;  // true on the first block (m_run = -inf)
-      const float m_use = grow ? mx : m_run;
-      const float alpha = grow ? ex2_approx(m_run - mx) : 1.f;  // 0 on the first block
-      uint32_t p[64];
-      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(fmaf(s[2 * c], scale_log2, -m_use));
-        const float p1 = ex2_approx(fmaf(s[2 * c + 1], scale_log2, -m_use));
-        p[c] = pack_bf16x2(p0, p1);
-        // the row sum uses the rounded probabilities that the PV product sees
-        r8[c & 7] += __uint_as_float(p[c] << 16) + __uint_as_float(p[c] & 0xffff0000u);
-      }
-      const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
-      l_run = l_run * alpha + rs;
-      if (j > 0) {
-        // PV_{j-1} must be complete before O is rescaled and P is overwritten
-        ok = mbar_wait(sm.o_done, (j - 1) & 1, kMbarLimitNs);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32(tmem + lane_addr + kColO + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st_32x32(tmem + lane_addr + kColO + c * 32, r);
-          }
-        }
-      }
-      m_run = m_use;
-      {
-        uint32_t lo[32], hi[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          lo[e] = p[e];
-          hi[e] = p[32 + e];
-        }
-        tmem_st_32x32(tmem + lane_addr + kColP, lo);
-        tmem_st_32x32(tmem + lane_addr + kColP + 32, hi);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(sm.p_ready);
-    }
-    if (ok) ok = mbar_wait(sm.o_done, (nkb - 1) & 1, kMbarLimitNs);
-    if (!ok) {
-      report_status(status, kStatusEpiWait);
-    } else {
-      tc_fence_after();
-      const float inv = 1.f / l_run;
-      __nv_bfloat16 *orow = out + static_cast<long>(row) * ldo + static_cast<long>(h) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32(tmem + lane_addr + kColO + c * 32, r);
-        tmem_wait_ld();
-        if (row < S) {
-          uint4 *o4 = reinterpret_cast<uint4 *>(orow + c * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]) * inv, __uint_as_float(r[q * 8 + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]) * inv, __uint_as_float(r[q * 8 + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]) * inv, __uint_as_float(r[q * 8 + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]) * inv, __uint_as_float(r[q * 8 + 7]) * inv);
-            o4[q] = w;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-}
-
 // ------------------------------------------------------------------ host side
-// V^T [HKV*D rows][ldv >= S] from the fused qkv buffer (one transpose launch).
-void attention_vt_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *vt, long ldv, int S, int HQ,
-                       int HKV, int D, cudaStream_t stream) {
+// fp16 V^T [HKV*D rows][ldv >= S] of KV heads [kv0, kv0 + nkv) from the fused qkv buffer
+void attention_vt(const __nv_bfloat16 *qkv, __half *vt, long ldv, int S, int HQ, int HKV, int D,
+                  cudaStream_t stream, int kv0, int nkv) {
+  if (nkv < 0) nkv = HKV - kv0;
+  if (kv0 < 0 || nkv <= 0 || kv0 + nkv > HKV) throw CudaError("attention_vt: KV head range");
   const long ld = static_cast<long>(HQ + 2 * HKV) * D;
-  transpose_bf16(qkv + static_cast<long>(HQ + HKV) * D, ld, vt, ldv, S, HKV * D, stream);
+  transpose_bf16_to_f16(qkv + static_cast<long>(HQ + HKV + kv0) * D, ld,
+                        vt + static_cast<long>(kv0) * D * ldv, ldv, S, nkv * D, stream);
 }
 
-void attention_tc_bf16(const __nv_bfloat16 *qkv, const __nv_bfloat16 *vt, long ldv,
-                       __nv_bfloat16 *out, int S, int HQ, int HKV, int D, float scale,
-                       uint32_t *status, cudaStream_t stream) {
-  if (D != 128) throw CudaError("attention_tc: head_dim must be 128");
-  if (HKV <= 0 || HQ % HKV) throw CudaError("attention_tc: HQ % HKV != 0");
-  if (ldv % 8) throw CudaError("attention_tc: V^T pitch must be a multiple of 8");
+template <int D>
+static void launch_attn_tc2(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
+                            __nv_bfloat16 *out, int S, int HQ, int HKV, int h0, int nh, int kv0,
+                            int group, float scale, uint32_t *status, cudaStream_t stream) {
+  using C = Attn2Cfg<D>;
   const long ld = static_cast<long>(HQ + 2 * HKV) * D;
   const CUtensorMap tm_qk = make_tmap_2d_bf16(qkv, S, ld, ld, kTileRows, 64);
   // V^T map: only the first S key columns are valid; TMA zero-fills beyond them
-  const CUtensorMap tm_vt = make_tmap_2d_bf16(vt, static_cast<uint64_t>(HKV) * D, S, ldv, kTileRows, 64);
+  const CUtensorMap tm_vt = make_tmap_2d_bf16(vt, static_cast<uint64_t>(HKV) * D, S, ldv, D, 64);
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static bool configured[64] = {false};
   if (!configured[dev & 63]) {
-    KRB_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(kAttnSmemBytes)));
-    KRB_CUDA(cudaFuncSetAttribute(attn_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(kAttn2SmemBytes)));
+    KRB_CUDA(cudaFuncSetAttribute(attn_tc2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(C::kSmem)));
     configured[dev & 63] = true;
   }
-  // KRB_ATTN=tc1: the one-tile kernel (kept for comparison)
-  static const bool one_tile = [] {
-    const char *e = std::getenv("KRB_ATTN");
-    return e && std::string(e) == "tc1";
-  }();
   const int nqb = (S + kTileRows - 1) / kTileRows;
-  const float sl2 = scale * 1.4426950408889634f;
-  if (one_tile) {
-    dim3 grid(HQ, nqb);
-    attn_tc_kernel<<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(
-        tm_qk, tm_vt, out, static_cast<long>(HQ) * D, S, HQ, HQ / HKV, sl2, status);
-  } else {
-    dim3 grid(HQ, (nqb + 1) / 2);
-    attn_tc2_kernel<<<grid, kAttn2Threads, kAttn2SmemBytes, stream>>>(
-        tm_qk, tm_vt, out, static_cast<long>(HQ) * D, S, HQ, HQ / HKV, sl2, status);
-  }
+  dim3 grid(nh, (nqb + 1) / 2);
+  attn_tc2_kernel<D><<<grid, kAttn2Threads, C::kSmem, stream>>>(
+      tm_qk, tm_vt, out, static_cast<long>(HQ) * D, S, HQ, h0, kv0, group,
+      scale * 1.4426950408889634f, status);
   KRB_CUDA(cudaGetLastError());
+}
+
+void attention_tc_bf16(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
+                       __nv_bfloat16 *out, int S, int HQ, int HKV, int D, float scale,
+                       uint32_t *status, cudaStream_t stream, int h0, int nh, int kv0, int group) {
+  if (D != 64 && D != 128) throw CudaError("attention_tc: head_dim must be 64 or 128");
+  if (HKV <= 0 || HQ % HKV) throw CudaError("attention_tc: HQ % HKV != 0");
+  if (ldv % 8) throw CudaError("attention_tc: V^T pitch must be a multiple of 8");
+  if (S <= 0) throw CudaError("attention_tc: empty sequence");
+  if (nh < 0) nh = HQ;
+  if (group <= 0) group = HQ / HKV;
+  if (h0 < 0 || nh <= 0 || h0 + nh > HQ || kv0 < 0 || kv0 + (nh - 1) / group >= HKV)
+    throw CudaError("attention_tc: head range outside the qkv layout");
+  if (D == 128)
+    launch_attn_tc2<128>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status, stream);
+  else
+    launch_attn_tc2<64>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status, stream);
 }
 
 }  // namespace krb

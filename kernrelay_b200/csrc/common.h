@@ -92,23 +92,23 @@ void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
                        const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
                        const __nv_bfloat16 *q_norm, const __nv_bfloat16 *k_norm, float eps,
                        cudaStream_t stream);
-// Causal GQA prefill attention over the fused qkv buffer; out [S, HQ*D].
-void attention_prefill_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *out, int S, int HQ,
-                            int HKV, int D, float scale, cudaStream_t stream);
-// Same over explicit Q/K/V head bases (row pitch ld): query head h of nq reads
-// KV head h / group; out row pitch ldo.
-void attention_heads_bf16(const __nv_bfloat16 *q, const __nv_bfloat16 *k, const __nv_bfloat16 *v,
-                          long ld, __nv_bfloat16 *out, long ldo, int S, int nq, int group, int D,
-                          float scale, cudaStream_t stream);
-// tcgen05 attention (head_dim 128): V^T scratch [HKV*D][ldv >= S] from qkv,
-// then the attention itself reading Q/K from qkv and V from V^T.
-void attention_vt_bf16(const __nv_bfloat16 *qkv, __nv_bfloat16 *vt, long ldv, int S, int HQ,
-                       int HKV, int D, cudaStream_t stream);
-void attention_tc_bf16(const __nv_bfloat16 *qkv, const __nv_bfloat16 *vt, long ldv,
+// tcgen05 causal GQA prefill attention (head_dim 64 or 128).  attention_vt writes
+// V^T in fp16 ([kv head * D + d][key], pitch ldv >= S) for KV heads [kv0, kv0 + nkv)
+// (nkv < 0: all); attention_tc_bf16 reads Q/K from qkv and V from V^T, out [S, HQ*D].
+// A launch may cover query heads [h0, h0 + nh) reading KV heads kv0 + (h - h0) / group
+// (nh < 0: all HQ heads, group <= 0: HQ / HKV).  The probabilities enter the PV
+// product in fp16 (both operands fp16), a finer rounding than bf16.
+void attention_vt(const __nv_bfloat16 *qkv, __half *vt, long ldv, int S, int HQ, int HKV,
+                  int D, cudaStream_t stream, int kv0 = 0, int nkv = -1);
+void attention_tc_bf16(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
                        __nv_bfloat16 *out, int S, int HQ, int HKV, int D, float scale,
-                       uint32_t *status, cudaStream_t stream);
+                       uint32_t *status, cudaStream_t stream, int h0 = 0, int nh = -1,
+                       int kv0 = 0, int group = -1);
 // Transpose a row-major [rows, cols] bf16 matrix into [cols, rows] (dst pitch ld_dst).
 void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, long ld_dst,
                     int rows, int cols, cudaStream_t stream);
+// Same, converting to fp16 on the way.
+void transpose_bf16_to_f16(const __nv_bfloat16 *src, long ld_src, __half *dst, long ld_dst,
+                           int rows, int cols, cudaStream_t stream);
 
 }  // namespace krb

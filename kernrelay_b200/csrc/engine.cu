@@ -405,13 +405,10 @@ void Engine::alloc_activations() {
   xf_ = A(S * H);
   if (has_logits()) logits_ = A(size_t(lm_rows_) * size_t(c.V));
   last_f32_ = static_cast<float *>(alloc(size_t(c.V) * 4));
-  // tcgen05 attention for head_dim 128 (KRB_ATTN=mma selects the mma.sync kernel)
-  const char *ae = std::getenv("KRB_ATTN");
-  attn_tc_ = (c.D == 128) && !(ae && std::string(ae) == "mma");
-  if (attn_tc_) {
-    ldvt_ = (long(S) + 7) / 8 * 8;
-    vt_ = A(size_t(c.HKV) * c.D * ldvt_);
-  }
+  // tcgen05 attention reads V transposed ([kv head * D + d][key])
+  if (c.D != 64 && c.D != 128) throw std::runtime_error("attention: head_dim must be 64 or 128");
+  ldvt_ = (long(S) + 7) / 8 * 8;
+  vt_ = reinterpret_cast<__half *>(A(size_t(c.HKV) * c.D * ldvt_));
   // token ids (ids.bin int64 [S], reference UploadIds :473-485)
   ids_ = static_cast<int64_t *>(alloc(S * 8));
   std::ifstream f(m_.dir + "/ids.bin", std::ios::binary | std::ios::ate);
@@ -509,15 +506,10 @@ void Engine::layer(int l, StageTimes *st) {
     rec.end();
   }
   rec.begin(st ? &st->attn : nullptr);
-  if (attn_tc_) {
-    attention_vt_bf16(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);
-    attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
-                      status_, stream_);
-    ++launches_;
-  } else {
-    attention_prefill_bf16(qkv_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
-                           stream_);
-  }
+  attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);
+  attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
+                    status_, stream_);
+  ++launches_;
   rec.end();
   if (mode_.fused) {
     // o_proj output kept in fp32 (no bf16 rounding of o); residual add fused into the norm

@@ -200,9 +200,8 @@ class Engine {
   uint32_t *status_ = nullptr;
   float *last_f32_ = nullptr;
   float *dump_ = nullptr;  // [L, S, H] fp32 when layer dumps are on
-  __nv_bfloat16 *vt_ = nullptr;  // V^T [HKV*D, ldvt_] for the tcgen05 attention
+  __half *vt_ = nullptr;  // fp16 V^T [HKV*D, ldvt_] for the tcgen05 attention
   long ldvt_ = 0;
-  bool attn_tc_ = false;
 
   // relay
   SymLayout sym_layout_{};

@@ -318,9 +318,15 @@ void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
 }
 
 // ------------------------------------------------------------------ transpose
+__device__ __forceinline__ void store_as(__nv_bfloat16 *p, __nv_bfloat16 v) { *p = v; }
+__device__ __forceinline__ void store_as(__half *p, __nv_bfloat16 v) {
+  *p = __float2half_rn(__bfloat162float(v));
+}
+
+// 32 x 32 tiles through padded shared memory; TD = bf16 (copy) or fp16 (converted)
+template <typename TD>
 __global__ void transpose_kernel(const __nv_bfloat16 *__restrict__ src, long ld_src,
-                                 __nv_bfloat16 *__restrict__ dst, long ld_dst, int rows,
-                                 int cols) {
+                                 TD *__restrict__ dst, long ld_dst, int rows, int cols) {
   __shared__ __nv_bfloat16 tile[32][33];
   const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -330,7 +336,7 @@ __global__ void transpose_kernel(const __nv_bfloat16 *__restrict__ src, long ld_
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int c = c0 + i, r = r0 + threadIdx.x;
-    if (r < rows && c < cols) dst[c * ld_dst + r] = tile[threadIdx.x][i];
+    if (r < rows && c < cols) store_as(dst + c * ld_dst + r, tile[threadIdx.x][i]);
   }
 }
 
@@ -338,7 +344,15 @@ void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, l
                     int rows, int cols, cudaStream_t stream) {
   dim3 block(32, 8);
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-  transpose_kernel<<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  transpose_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void transpose_bf16_to_f16(const __nv_bfloat16 *src, long ld_src, __half *dst, long ld_dst,
+                           int rows, int cols, cudaStream_t stream) {
+  dim3 block(32, 8);
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose_kernel<__half><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
   KRB_CUDA(cudaGetLastError());
 }
 

@@ -101,12 +101,15 @@ std::string Engine::profile_many(const std::string &spec_path) {
       const int hkv = kv_div ? c.HKV / k : 1;
       shape = "attention|" + std::to_string(c.HQ) + "x" + std::to_string(S) + "x" + std::to_string(D);
       // k head groups; with k > HKV each group gets one KV head, cycling (reference :1689-1704)
+      // each group: V^T of its KV heads, then the tcgen05 attention over its query heads
+      // (the same two kernels as the prefill's attention stage)
       call = [=](int g) {
         const int kv_off = kv_div ? g * hkv : g % c.HKV;
         const int group = std::max(1, hq / hkv);
-        attention_heads_bf16(qkv_ + size_t(g) * hq * D, qkv_ + size_t(nq) + size_t(kv_off) * D,
-                             qkv_ + size_t(nq + nkv) + size_t(kv_off) * D, nqkv_, attn_ + size_t(g) * hq * D,
-                             nq, S, hq, group, D, float(1.0 / std::sqrt(double(D))), stream_);
+        attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_, kv_off, hkv);
+        attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D,
+                          float(1.0 / std::sqrt(double(D))), status_, stream_, g * hq, hq, kv_off,
+                          group);
       };
     } else {
       continue;

@@ -220,8 +220,21 @@ def main():
     ap.add_argument("--seq", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--merge-into", help="existing cost table: re-measure only the Qwen "
+                                         "operator keys into it (curves, collectives kept)")
     args = ap.parse_args()
     out = Path(args.out_dir)
+    if args.merge_into:
+        costs = json.loads(Path(args.merge_into).read_text(encoding="utf-8"))
+        for cfg in [c for c in args.qwen.split(",") if c]:
+            costs["full"].update({k: round(v, 3) for k, v in
+                                  measure_qwen(cfg, args.seq, int(args.devices.split(",")[0])).items()})
+        costs["full"] = dict(sorted(costs["full"].items()))
+        out.mkdir(parents=True, exist_ok=True)
+        dst = out / Path(args.merge_into).name
+        dst.write_text(json.dumps(costs, indent=1) + "\n", encoding="utf-8")
+        print(json.dumps({"out": str(dst), "full": len(costs["full"])}))
+        return
     out.mkdir(parents=True, exist_ok=True)
     devs = args.devices.split(",")
     dev0 = devs[0]

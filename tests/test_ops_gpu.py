@@ -254,8 +254,9 @@ def _attn_ref(qkv, S, HQ, HKV, D, scale):
 
 
 @pytest.mark.parametrize("S,HQ,HKV,D,impl", [
-    (128, 4, 2, 64, 1), (200, 4, 1, 128, 1), (512, 8, 2, 128, 1), (70, 2, 2, 64, 1),
-    # tcgen05/TMEM kernel: multiples of the 128-row tile, ragged S, GQA groups, MHA
+    # tcgen05/TMEM kernel: multiples of the 128-row tile, ragged S, GQA groups, MHA,
+    # head_dim 64 (Qwen2.5-0.5B: 14 / 2 heads) and 128
+    (128, 4, 2, 64, 2), (70, 2, 2, 64, 0), (512, 14, 2, 64, 2), (1000, 4, 1, 64, 2),
     (128, 2, 1, 128, 2), (512, 8, 2, 128, 2), (200, 4, 1, 128, 2), (1000, 4, 4, 128, 2),
     (2048, 28, 4, 128, 2),
 ])
