@@ -52,11 +52,12 @@ int krb_gemm_bf16(const void *A, long lda, const void *B, long ldb, void *C, lon
  * optional RMSNorm over D (q_norm / k_norm; Qwen3) and rotate-half RoPE with the bf16
  * cos / sin tables [max_pos, D] at position = row, in the GEMM epilogue; v heads get the
  * bias only.  D in {64, 128}.  Replaces EmitQkv + EmitQkNorm + aclnnApplyRotaryPosEmb
- * (qwen_main.cpp:1336-1357, 567-582) as one kernel. */
+ * (qwen_main.cpp:1336-1357, 567-582) as one kernel. *  vt (optional, fp16 [HKV*D][ldvt >= M]): the v heads also written transposed,
+ *  vt[(c - (HQ+HKV)*D) * ldvt + row] = fp16(bf16 value) -- the attention's V^T. */
 int krb_gemm_qkv_rope_bf16(const void *A, long lda, const void *B, long ldb, void *C, long ldc,
                            const void *bias, int M, int K, int HQ, int HKV, int D,
                            const void *cos_tab, const void *sin_tab, const void *q_norm,
-                           const void *k_norm, float eps, void *stream);
+                           const void *k_norm, float eps, void *vt, long ldvt, void *stream);
 
 /* out[M,N] = A[M,K] . B[N,K]^T in fp32 (unrounded; row pitch ld) -- the o_proj and
  * single-device down_proj form whose output feeds the fp32 residual stream. */

@@ -51,7 +51,8 @@ SIGNATURES = [
                                    c_int, c_int, c_int, c_void_p]),
     ("krb_gemm_qkv_rope_bf16", c_int, [c_void_p, c_long, c_void_p, c_long, c_void_p, c_long,
                                        c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
-                                       c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
+                                       c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_long,
+                                       c_void_p]),
     ("krb_rmsnorm_bf16", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float,
                                  c_void_p]),
     ("krb_add_rmsnorm_bf16", c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -226,15 +227,17 @@ def embed(ids, table, status=None, stream=None):
 
 
 def gemm_qkv_rope(A, B, HQ, HKV, D, cos, sin, bias=None, q_norm=None, k_norm=None, eps=1e-6,
-                  stream=None):
-    """Fused QKV GEMM (+bias) with per-head QK-norm and RoPE in the epilogue."""
+                  vt=None, stream=None):
+    """Fused QKV GEMM (+bias) with per-head QK-norm and RoPE in the epilogue; with `vt`
+    (fp16 [HKV*D, ldvt >= M]) the v heads are also written transposed."""
     import torch
     M, K = A.shape
     N = (HQ + 2 * HKV) * D
     out = torch.empty((M, N), dtype=torch.bfloat16, device=A.device)
     check(lib().krb_gemm_qkv_rope_bf16(_ptr(A), A.stride(0), _ptr(B), B.stride(0), _ptr(out),
                                        out.stride(0), _ptr(bias), M, K, HQ, HKV, D, _ptr(cos),
-                                       _ptr(sin), _ptr(q_norm), _ptr(k_norm), eps, _stream(stream)),
+                                       _ptr(sin), _ptr(q_norm), _ptr(k_norm), eps, _ptr(vt),
+                                       vt.stride(0) if vt is not None else 0, _stream(stream)),
           "gemm_qkv_rope")
     return out
 

@@ -567,13 +567,13 @@ KRB_EXPORT int krb_gemm_qkv_rope_bf16(const void *A, long lda, const void *B, lo
                                       long ldc, const void *bias, int M, int K, int HQ, int HKV,
                                       int D, const void *cos_tab, const void *sin_tab,
                                       const void *q_norm, const void *k_norm, float eps,
-                                      void *stream) {
+                                      void *vt, long ldvt, void *stream) {
   KRB_OP_BEGIN
   krb::gemm_qkv_rope_bf16(static_cast<const bf *>(A), lda, static_cast<const bf *>(B), ldb,
                           static_cast<bf *>(C), ldc, static_cast<const bf *>(bias), M, K, HQ, HKV, D,
                           static_cast<const bf *>(cos_tab), static_cast<const bf *>(sin_tab),
                           static_cast<const bf *>(q_norm), static_cast<const bf *>(k_norm), eps,
-                          nullptr, as_stream(stream));
+                          nullptr, as_stream(stream), static_cast<__half *>(vt), ldvt);
   KRB_OP_END
 }
 

@@ -54,7 +54,8 @@ void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B
                         int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
                         const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
                         const __nv_bfloat16 *kn, float eps, uint32_t *status,
-                        cudaStream_t stream);
+                        cudaStream_t stream, __half *vt = nullptr,
+                        long ldvt = 0);
 
 // act[M, n_out] = silu(gate) * up, with B rows interleaved in blocks of bn:
 // rows [b*bn, b*bn+bn/2) gate, [b*bn+bn/2, (b+1)*bn) up for outputs [b*bn/2, (b+1)*bn/2).

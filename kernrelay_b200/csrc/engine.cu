@@ -486,13 +486,14 @@ void Engine::layer(int l, StageTimes *st) {
   const float eps = float(c.eps);
   const LayerW &w = lw_[l];
   StageRec rec(stream_, st, g_events);
-  launches_ += 4;  // qkv, attention, o, gate/up (+ add_norm counted there)
+  launches_ += 4;  // QKV GEMM, attention, o_proj GEMM, gate/up GEMM (others where they launch)
   rec.begin(st ? &st->qkv : nullptr);
   if (fuse_rope_) {
     // QK-norm and RoPE in the QKV GEMM's epilogue (no separate pass over q / k)
+    // (and writes the fp16 V^T the attention reads: no separate transpose)
     gemm_qkv_rope_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, H, c.HQ,
                        c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
-                       c.qk_norm ? w.kn : nullptr, eps, status_, stream_);
+                       c.qk_norm ? w.kn : nullptr, eps, status_, stream_, vt_, ldvt_);
     rec.end();
   } else {
     // unfused serial modes: the reference's separate ops (qwen_main.cpp:1336-1357, 567-582)
@@ -506,10 +507,12 @@ void Engine::layer(int l, StageTimes *st) {
     rec.end();
   }
   rec.begin(st ? &st->attn : nullptr);
-  attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);
+  if (!fuse_rope_) {
+    attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);  // the fused QKV epilogue writes it otherwise
+    ++launches_;
+  }
   attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
                     status_, stream_);
-  ++launches_;
   rec.end();
   if (mode_.fused) {
     // o_proj output kept in fp32 (no bf16 rounding of o); residual add fused into the norm

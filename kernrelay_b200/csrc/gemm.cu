@@ -270,7 +270,7 @@ void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B
                         int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
                         const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
                         const __nv_bfloat16 *kn, float eps, uint32_t *status,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, __half *vt, long ldvt) {
   const int N = (HQ + 2 * HKV) * D;
   if (M <= 0 || K <= 0 || HQ <= 0 || HKV <= 0) throw CudaError("gemm_qkv_rope: empty shape");
   if (D != 64 && D != 128) throw CudaError("gemm_qkv_rope: head_dim must be 64 or 128");
@@ -300,6 +300,9 @@ void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B
   ea.rope_cols = (HQ + HKV) * D;
   ea.D = D;
   ea.eps = eps;
+  ea.vt = vt;
+  ea.ldvt = ldvt;
+  if (vt && ldvt < M) throw CudaError("gemm_qkv_rope: V^T pitch below the row count");
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
   if (bn == 256) {
     const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);

@@ -279,6 +279,10 @@ struct EpiArgs {
   const __nv_bfloat16 *cos_tab, *sin_tab, *qn, *kn;
   int q_cols, rope_cols, D;
   float eps;
+  // kEpiQkvRope, optional: the v heads also go out transposed in fp16 for the attention,
+  // vt[(col - rope_cols) * ldvt + row] = fp16(bf16(v)) (null: not written)
+  __half *vt;
+  long ldvt;
 };
 
 // The accumulator chunk a warp holds is row-per-thread (thread = TMEM lane = row,
@@ -403,18 +407,24 @@ __device__ __forceinline__ void unpack8_f(const uint4 &w, float *f) {
 
 template <int BN, typename RowPtr>
 __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPtr bf16_row,
-                                             const EpiArgs &ea, int row, int nb) {
+                                             const EpiArgs &ea, int row, bool row_ok, int nb) {
   const int D = ea.D, half = D / 2, nch = D / 32;
 #pragma unroll 1
   for (int h0 = 0; h0 < BN; h0 += D) {
     const int hcol = nb * BN + h0;  // first column of this head
     if (hcol >= ea.n_out) break;    // warp-uniform
     if (hcol >= ea.rope_cols) {
-      // v head: bias only
+      // v head: bias only; with ea.vt also transposed (lanes = 32 consecutive rows, so
+      // each store instruction writes 64 contiguous bytes of one V^T row)
 #pragma unroll 1
       for (int c = 0; c < nch; ++c) {
         float v[32];
         epi_load32(tbase + h0 + c * 32, ea.bias, hcol + c * 32, v);
+        if (ea.vt && row_ok) {
+          __half *dst = ea.vt + static_cast<long>(hcol - ea.rope_cols + c * 32) * ea.ldvt + row;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dst[static_cast<long>(j) * ea.ldvt] = __float2half_rn(bf16_round(v[j]));
+        }
         epi_stage_put(stage, v);
         epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + c * 32, ea.n_out - hcol - c * 32);
       }
@@ -501,7 +511,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
     };
     if constexpr (MODE == kEpiQkvRope) {
       // rows past M are not stored; clamp their table position
-      epi_qkv_rope<BN>(tbase, stage, bf16_row, ea, min(mb * kBM + quad * 32 + lane, M - 1), nb);
+      const int erow = mb * kBM + quad * 32 + lane;
+      epi_qkv_rope<BN>(tbase, stage, bf16_row, ea, min(erow, M - 1), erow < M, nb);
     } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32 || MODE == kEpiStoreF16) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {

@@ -197,8 +197,13 @@ def test_gemm_qkv_rope(cuda, krlib, S, HQ, HKV, D, qk_norm, bias):
     cos, sin = cos.to(cuda), sin.to(cuda)
     qn = _bf(1 + 0.1 * torch.randn(D, generator=g)).to(cuda) if qk_norm else None
     kn = _bf(1 + 0.1 * torch.randn(D, generator=g)).to(cuda) if qk_norm else None
-    out = krlib.gemm_qkv_rope(A, B, HQ, HKV, D, cos, sin, bias=b, q_norm=qn, k_norm=kn)
+    ldvt = (S + 7) // 8 * 8
+    vt = torch.full((HKV * D, ldvt), float("nan"), dtype=torch.float16, device=cuda)
+    out = krlib.gemm_qkv_rope(A, B, HQ, HKV, D, cos, sin, bias=b, q_norm=qn, k_norm=kn, vt=vt)
     torch.cuda.synchronize()
+    # the transposed v heads are exactly the stored bf16 v columns, in fp16
+    v_cols = out[:, (HQ + HKV) * D:]
+    assert torch.equal(vt[:, :S], v_cols.float().half().T)
     x = A.float() @ B.float().T
     if b is not None:
         x = x + b.float()
