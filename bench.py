@@ -43,9 +43,10 @@ sys.path.insert(0, str(REPO))
 os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 METRIC = "Qwen2.5-7B prefill tok/s @seq2048 at 1/2/4/8 B200; tp_split vs tp speedup"
-# the reference's published numbers for this metric (Ascend 910B3, real weights)
+# the reference's published prefill times for this metric (Ascend 910B3, real weights): 146.2 ms
+# single-device and 118.153 ms tp2 at S = 2048 -> tokens/s
 PUBLISHED_TOKS = {1: 2048 / 0.1462, 2: 2048 / 0.118153}
-NVLINK_GBS = 770.0   # measured peer copy per direction (profiling recipe); 900 nominal
+NVLINK_GBS = 770.0   # measured peer copy per direction on these B200s; 900 nominal
 
 
 def peaks():
