@@ -205,6 +205,12 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
       else throw std::runtime_error("KRB_RELAY must be direct or rsag");
     }
     if (relay_direct_ && k > 4) throw std::runtime_error("direct relay supports up to 4 ranks");
+    if (const char *e = std::getenv("KRB_RELAY_ORDER")) {
+      if (!std::strcmp(e, "ready")) relay_ready_order_ = 1;
+      else if (std::strcmp(e, "pipeline")) throw std::runtime_error("KRB_RELAY_ORDER must be ready or pipeline");
+    }
+    if (relay_ready_order_ && opts_.tiles > 32)
+      throw std::runtime_error("KRB_RELAY_ORDER=ready supports up to 32 row tiles");
     if (const char *e = std::getenv("KRB_RELAY_TRACE"))
       if (std::atoi(e) > 0) {
         const size_t n = size_t(sm_count(opts_.device)) * kTraceSlots;
@@ -564,6 +570,7 @@ void Engine::layer(int l, StageTimes *st) {
     ra.ag_expect = ag_expect_;
     ra.done_expect = relay_done_expect(S, H, opts_.tiles, bn_down_);
     ra.direct = relay_direct_;
+    ra.ready_order = relay_ready_order_;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch());
     ra.layer = l;
     ra.L = c.L;

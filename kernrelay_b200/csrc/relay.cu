@@ -214,6 +214,17 @@ __device__ __forceinline__ bool wait_all_sources(const RelayArgs &ra, size_t cnt
   return ok;
 }
 
+// Non-blocking: true when every source's counter of tile t has reached target (one
+// acquire load each; called by a single thread, which then publishes the result).
+__device__ __forceinline__ bool sources_ready(const RelayArgs &ra, size_t cnt_base, int t,
+                                              uint32_t target) {
+  for (int src = 0; src < ra.k; ++src) {
+    const uint32_t *p = flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128);
+    if (static_cast<int32_t>(ld_acquire_sys(p) - target) < 0) return false;
+  }
+  return true;
+}
+
 __device__ __forceinline__ float warp_allsum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -602,20 +613,15 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     return rs_ok;
   };
 
-  // Software pipeline over the row tiles: the reduce-scatter of tile t+1 runs
-  // while the all-gather of tile t is still in flight on the other ranks.
-  bool rs_ok_next = rs_phase(0);
-  for (int t = 0; t < ra.T; ++t) {
-    const bool rs_ok = rs_ok_next;
-    if (t + 1 < ra.T) rs_ok_next = rs_phase(t + 1);
-    // ---- wait for every owner's reduced slice of tile t, then Add+RMSNorm
+  // ---- all-gather step of tile t: wait for every owner's reduced slice, then Add+RMSNorm
+  auto ag_phase = [&](int t, bool rs_ok) {
     const bool ag_ok =
         wait_all_sources(ra, ag_cnt_base, t, ag_target, kStatusAgWait, timeout, flag_smem);
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 5 + 4 * t);
     if (!rs_ok || !ag_ok) timeout = 0;
-    if (!ag_ok) continue;
+    if (!ag_ok) return;
     if (ra.bulk) {
-      if (stuck) continue;
+      if (stuck) return;
       if (leader) fence_proxy_async_global();
       for (int q = gp; q < ra.R; q += GP) {
         const size_t g = size_t(t) * ra.R + q;
@@ -635,7 +641,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
         phase ^= 1;
       }
       if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
-      continue;
+      return;
     }
     for (int q = gp; q < ra.R; q += GP) {
       const size_t g = size_t(t) * ra.R + q;
@@ -648,6 +654,51 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
                           pair_ss);
     }
     if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+  };
+
+  // Phase order over the row tiles (one call site per phase keeps register pressure
+  // down).  Default: the software pipeline rs(0), rs(1), ag(0), rs(2), ag(1), ...: the
+  // reduce-scatter of tile t+1 runs while the all-gather of tile t is still in flight
+  // on the other ranks.  ra.ready_order: once the reduce-scatter is ahead, take
+  // whichever of rs(next_rs) and ag(next_ag) is ready first (reduce-scatter when both
+  // are: the peers' all-gathers wait on it) instead of blocking ag(t) behind the
+  // partials of tile t+1.  An all-gather never runs before its own reduce-scatter.
+  uint32_t rs_failed = 0;  // bit t: the reduce-scatter of tile t failed (T <= 32)
+  int next_rs = 0, next_ag = 0;
+  while (next_ag < ra.T) {
+    bool do_rs = next_rs < ra.T;
+    if (do_rs && next_rs > next_ag) {
+      if (!ra.ready_order) {
+        do_rs = next_rs == next_ag + 1;
+      } else {
+        // one thread polls both counter sets and publishes a uniform choice:
+        // 1 reduce-scatter ready, 2 all-gather ready, 3 limit reached (the blocking
+        // all-gather wait then reports it)
+        const uint64_t t0 = globaltimer_ns();
+        int choice = 0;
+        while (choice == 0) {
+          if (threadIdx.x == kRelayWarp0 * 32) {
+            int c = 0;
+            if (sources_ready(ra, rs_cnt_base, next_rs, rs_target)) c = 1;
+            else if (sources_ready(ra, ag_cnt_base, next_ag, ag_target)) c = 2;
+            else if (globaltimer_ns() - t0 > timeout) c = 3;
+            *flag_smem = c;
+          }
+          named_bar_sync(2, kRelayWarps * 32);
+          choice = *flag_smem;
+          named_bar_sync(2, kRelayWarps * 32);
+          if (choice == 0) __nanosleep(64);
+        }
+        do_rs = choice == 1;
+      }
+    }
+    if (do_rs) {
+      if (!rs_phase(next_rs)) rs_failed |= 1u << (next_rs & 31);
+      ++next_rs;
+    } else {
+      ag_phase(next_ag, ((rs_failed >> (next_ag & 31)) & 1u) == 0);
+      ++next_ag;
+    }
   }
   if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
   drain();

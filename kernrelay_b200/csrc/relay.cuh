@@ -110,6 +110,9 @@ struct RelayArgs {
   // 1: the relay warps stage remote rows in shared memory with bulk copies (set
   // by the launcher when the shared-memory budget and the alignment allow it)
   int bulk;
+  // reduce-scatter + all-gather form only: 1 = take whichever phase is ready first
+  // (KRB_RELAY_ORDER=ready), 0 = reduce-scatter of tile t+1 before all-gather of t
+  int ready_order;
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;
   const float *resid;          // h1 [S, H] fp32 residual stream

@@ -51,10 +51,11 @@ def _run_all(engines, fn):
 
 
 @pytest.mark.parametrize("k", [2, 4, 8])
-@pytest.mark.parametrize("variant", ["direct", "rsag", "nccl"])
+@pytest.mark.parametrize("variant", ["direct", "rsag", "rsag_ready", "nccl"])
 def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     """variant: the split relay's direct all-pull or reduce-scatter + all-gather
-    form (KRB_RELAY, read at engine creation), or the NCCL tp baseline."""
+    form (KRB_RELAY, read at engine creation; rsag_ready: its phases in readiness order,
+    KRB_RELAY_ORDER=ready), or the NCCL tp baseline."""
     if _ngpu() < k:
         pytest.skip(f"needs {k} GPUs")
     if variant == "direct" and k > 4:
@@ -62,12 +63,15 @@ def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     d, ref, cfg = tiny
     split = variant != "nccl"
     mode = f"tp{k}_split" if split else f"tp{k}"
+    relay = variant.split("_")[0]
     if split:
-        monkeypatch.setenv("KRB_RELAY", variant)
+        monkeypatch.setenv("KRB_RELAY", relay)
+    if variant == "rsag_ready":
+        monkeypatch.setenv("KRB_RELAY_ORDER", "ready")
     engines = [krlib.Engine(d, mode, 512, rank=r, world=k, device=r, tiles=4) for r in range(k)]
     try:
         if split:
-            assert engines[0].info()["relay"] == variant
+            assert engines[0].info()["relay"] == relay
         if split:
             krlib.Engine.link(engines)
         else:
