@@ -54,6 +54,10 @@ CONFIGS = {
     # test-sized shapes of both families
     "tiny-qwen2": ModelConfig("qwen2.5", 256, 512, 2, 4, 2, 64, 1024, True, True, False, 1e6),
     "tiny-qwen3": ModelConfig("qwen3_vl", 256, 768, 2, 2, 1, 128, 1024, False, False, True, 5e6),
+    # the 0.5B head layout (14 / 2 heads of 64, GQA 7, QKV bias) at two layers
+    "small-qwen2-gqa7": ModelConfig("qwen2.5", 896, 1024, 2, 14, 2, 64, 2048, True, True, False, 1e6),
+    # Qwen3-VL head layout (GQA 4, head_dim 128, QK-norm, theta 5e6; q width != hidden)
+    "small-qwen3-gqa4": ModelConfig("qwen3_vl", 512, 1024, 2, 8, 2, 128, 2048, False, False, True, 5e6),
 }
 
 

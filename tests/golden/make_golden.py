@@ -33,6 +33,8 @@ CASES = {
     # name: (config, seq, norm_std)
     "tiny_qwen2_s64": ("tiny-qwen2", 64, 0.1),
     "tiny_qwen3_s48": ("tiny-qwen3", 48, 0.1),
+    "small_qwen2_gqa7_s40": ("small-qwen2-gqa7", 40, 0.1),
+    "small_qwen3_gqa4_s40": ("small-qwen3-gqa4", 40, 0.1),
 }
 
 
@@ -107,7 +109,8 @@ def make(name: str, out_dir: Path):
 
 
 def main():
-    for name in CASES:
+    names = sys.argv[1:] or list(CASES)
+    for name in names:
         make(name, HERE)
 
 

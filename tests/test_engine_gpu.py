@@ -26,7 +26,8 @@ def _maxrel(a, b):
 @pytest.fixture(scope="module")
 def tiny_models(tmp_path_factory, krlib):
     out = {}
-    for name, L, seq in (("tiny-qwen2", 3, 256), ("tiny-qwen3", 3, 256)):
+    for name, L, seq in (("tiny-qwen2", 3, 256), ("tiny-qwen3", 3, 256),
+                         ("small-qwen2-gqa7", 3, 256), ("small-qwen3-gqa4", 3, 256)):
         cfg = model_gen.config_with(name, L=L)
         d = model_gen.write_model(tmp_path_factory.mktemp(name) / "m", cfg, seq, norm_std=0.1)
         ref = qwen_ref.prefill(qwen_ref.Model(d))
@@ -47,7 +48,10 @@ def _check(eng, ref, L, label):
 
 @pytest.mark.parametrize("mode", ["serial_fused", "serial", "graph_whole", "relay_flag",
                                   "tp1", "tp1_split"])
-@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-qwen3"])
+@pytest.mark.parametrize("model", ["tiny-qwen2", "tiny-qwen3",
+                                   # the 0.5B head layout (GQA 7, D 64, bias) and the
+                                   # Qwen3-VL one (GQA 4, D 128, QK-norm, q width != H)
+                                   "small-qwen2-gqa7", "small-qwen3-gqa4"])
 def test_engine_matches_oracle(cuda, krlib, tiny_models, model, mode):
     d, ref = tiny_models[model]
     eng = krlib.Engine(d, mode, 256, tiles=2)
