@@ -465,3 +465,17 @@ def test_op_schedules_oracle_matches_torch_operators(name):
     assert name in got
     tol = REL_TOL * ref["node_abs"][name] + 1e-6
     assert abs(got[name] - ref["node_checksums"][name]) <= tol, (name, got[name], ref["node_checksums"][name])
+
+
+@pytest.mark.parametrize("name", ["e5_mm_ar_full_a", "e5_mm_ag_part_a", "e5_mm_rs_part_a",
+                                  "f03_mm_ar_c4_a", "e4_mm_cross_hccl_a", "e9_mixed_a"])
+def test_collective_dags_at_four_ranks_match_torch(name):
+    """The collective DAGs with nranks = 4: reduce-scatter blocks at rank * rows / 4,
+    all-gather placement by rank, allreduce sums -- oracle against the torch evaluation."""
+    sched = _load({"file": f"small/{name}.json"})
+    sched["nranks"] = 4
+    ref = plan_ref.PlanOracle(sched).run()
+    got = _torch_eval(sched)
+    for nid, v in got.items():
+        tol = REL_TOL * ref["node_abs"][nid] + 1e-6
+        assert abs(v - ref["node_checksums"][nid]) <= tol, (name, nid, v, ref["node_checksums"][nid])
