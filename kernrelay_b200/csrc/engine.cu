@@ -205,9 +205,11 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
       else throw std::runtime_error("KRB_RELAY must be direct or rsag");
     }
     if (relay_direct_ && k > 4) throw std::runtime_error("direct relay supports up to 4 ranks");
+    relay_ready_order_ = 1;  // rsag phases in readiness order (KRB_RELAY_ORDER=pipeline: fixed)
     if (const char *e = std::getenv("KRB_RELAY_ORDER")) {
       if (!std::strcmp(e, "ready")) relay_ready_order_ = 1;
-      else if (std::strcmp(e, "pipeline")) throw std::runtime_error("KRB_RELAY_ORDER must be ready or pipeline");
+      else if (!std::strcmp(e, "pipeline")) relay_ready_order_ = 0;
+      else throw std::runtime_error("KRB_RELAY_ORDER must be ready or pipeline");
     }
     if (relay_ready_order_ && opts_.tiles > 32)
       throw std::runtime_error("KRB_RELAY_ORDER=ready supports up to 32 row tiles");

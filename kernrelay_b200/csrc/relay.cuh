@@ -111,7 +111,7 @@ struct RelayArgs {
   // by the launcher when the shared-memory budget and the alignment allow it)
   int bulk;
   // reduce-scatter + all-gather form only: 1 = take whichever phase is ready first
-  // (KRB_RELAY_ORDER=ready), 0 = reduce-scatter of tile t+1 before all-gather of t
+  // (default), 0 = reduce-scatter of tile t+1 before all-gather of t (KRB_RELAY_ORDER=pipeline)
   int ready_order;
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;

@@ -51,11 +51,11 @@ def _run_all(engines, fn):
 
 
 @pytest.mark.parametrize("k", [2, 4, 8])
-@pytest.mark.parametrize("variant", ["direct", "rsag", "rsag_ready", "nccl"])
+@pytest.mark.parametrize("variant", ["direct", "rsag", "rsag_pipeline", "nccl"])
 def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     """variant: the split relay's direct all-pull or reduce-scatter + all-gather
-    form (KRB_RELAY, read at engine creation; rsag_ready: its phases in readiness order,
-    KRB_RELAY_ORDER=ready), or the NCCL tp baseline."""
+    form (KRB_RELAY, read at engine creation; rsag runs its phases in readiness order,
+    rsag_pipeline in the fixed order, KRB_RELAY_ORDER=pipeline), or the NCCL tp baseline."""
     if _ngpu() < k:
         pytest.skip(f"needs {k} GPUs")
     if variant == "direct" and k > 4:
@@ -66,8 +66,8 @@ def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     relay = variant.split("_")[0]
     if split:
         monkeypatch.setenv("KRB_RELAY", relay)
-    if variant == "rsag_ready":
-        monkeypatch.setenv("KRB_RELAY_ORDER", "ready")
+    if variant == "rsag_pipeline":
+        monkeypatch.setenv("KRB_RELAY_ORDER", "pipeline")
     engines = [krlib.Engine(d, mode, 512, rank=r, world=k, device=r, tiles=4) for r in range(k)]
     try:
         if split:
