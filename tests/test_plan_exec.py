@@ -479,3 +479,25 @@ def test_collective_dags_at_four_ranks_match_torch(name):
     for nid, v in got.items():
         tol = REL_TOL * ref["node_abs"][nid] + 1e-6
         assert abs(v - ref["node_checksums"][nid]) <= tol, (name, nid, v, ref["node_checksums"][nid])
+
+
+def test_committed_planner_tables_keep_the_reference_format():
+    """kernrelay_b200/configs/*_b200.json are read by the reference planner's Costs class
+    (launch_us, traffic_gbps, l2_mb, event_us, full; curve cases keyed by op and shape with
+    base_best_us and fit.slope_us_per_tile / fit.intercept_us)."""
+    cfg = Path(__file__).resolve().parents[1] / "kernrelay_b200" / "configs"
+    costs = json.loads((cfg / "planner2_costs_b200.json").read_text(encoding="utf-8"))
+    curves = json.loads((cfg / "planner_curves_b200.json").read_text(encoding="utf-8"))
+    for key in ("launch_us", "traffic_gbps", "l2_mb", "event_us", "full", "split"):
+        assert key in costs, key
+    assert all(isinstance(v, (int, float)) and v >= 0 for v in costs["full"].values())
+    for op in ("matmul", "gelu", "softmax", "layernorm", "attention", "allreduce"):
+        assert any(k.startswith(op + "|") for k in costs["full"]), op
+    assert len(curves["cases"]) == 16
+    for c in curves["cases"]:
+        s = c["shape"]
+        key = ("matmul|%dx%dx%d" % (s["M"], s["K"], s["N"]) if c["op"] == "matmul"
+               else "%s|%dx%d" % (c["op"], s["rows"], s["cols"]))
+        assert key in costs["full"], key                    # every curve's k = 1 point is a cost
+        assert c["base_best_us"] > 0 and c["strategy"] in ("row", "col")
+        assert c["fit"]["slope_us_per_tile"] >= 0 and c["fit"]["intercept_us"] > 0
