@@ -129,7 +129,9 @@ int krb_relay_down_single(const void *act, const void *w_down, const void *resid
  * ((2 * tiles + 2) * 128 bytes are used, so tiles <= 127; more returns an error).
  * The call zeroes them on `stream`, launches, and returns without synchronising.
  * The first call on a device does its set-up (symbol lookup, kernel attributes)
- * and should come before any stream capture on that device.  Calls that overlap
+ * and should come before any stream capture on that device.  The looked-up address
+ * is kept for the life of the process: do not reset the device (cudaDeviceReset or
+ * a primary-context reset) between calls.  Calls that overlap
  * in time on one device (different streams or threads) share the scratch and
  * race; calls in order on one stream are safe.  k = 1 only, like
  * krb_relay_down_single. */
@@ -167,6 +169,18 @@ int krb_engine_create(const char *model_dir, const char *mode, int seq, int rank
                       int device, int tiles, krb_engine **out);
 void krb_engine_destroy(krb_engine *e);
 
+/* An engine for the isolated TP-MLP micro-DAG (the reference's mm -> AllReduce ->
+ * AddNorm tile loop, qwen_main.cpp:1274-1302, without the rest of the layer): per
+ * rank X_r [seq, intermediate/world] ~ N(0,1) and W_r [intermediate/world, hidden]
+ * ~ N(0,0.02) generated with seed + rank, residual R [seq, hidden] ~ N(0,1) with
+ * seed, gamma = 1, eps 1e-6.  mode: tp{k} (GEMM -> NCCL AllReduce -> Add+RMSNorm) or
+ * tp{k}_split (the fused relay, `tiles` row tiles).  Every engine call below
+ * applies; one run is one micro-DAG step and every rank's outputs are read with
+ * krb_engine_final_hidden (h = R + sum of the partials, fp32) and krb_engine_final_x
+ * (x = RMSNorm(h), bf16). */
+int krb_microdag_create(int seq, int hidden, int intermediate, int tiles, int rank, int world,
+                        int device, const char *mode, uint64_t seed, krb_engine **out);
+
 /* tp_split: cudaIpcMemHandle_t (64 bytes) of this rank's relay region. */
 int krb_engine_ipc_handle(krb_engine *e, void *handle_out, size_t cap);
 /* tp_split: map every peer's relay region; handles = world x 64 bytes (own entry ignored). */
@@ -194,8 +208,12 @@ int krb_engine_stage_times(krb_engine *e, char *out, size_t cap);
 /* last-row logits vs ref files; JSON {argmax, ref_argmax, maxdiff, abs_mean, has_ref} */
 int krb_engine_verify(krb_engine *e, char *out, size_t cap);
 int krb_engine_last_logits(krb_engine *e, float *out, int n);
-/* copy the fp32 residual stream after the final layer ([S,H], rank 0) to host */
+/* copy the fp32 residual stream after the final layer ([S,H], rank 0; every rank of
+ * a micro-DAG engine) to host */
 int krb_engine_final_hidden(krb_engine *e, float *out, size_t n);
+/* copy the final normed rows xf ([S,H] bf16 bits, rank 0; every rank of a
+ * micro-DAG engine) to host */
+int krb_engine_final_x(krb_engine *e, uint16_t *out, size_t n);
 /* keep a copy of the residual stream after every layer of the next runs
  * (test-sized models: L*S*H*2 bytes of device memory) */
 int krb_engine_layer_dump(krb_engine *e, int on);

@@ -76,6 +76,8 @@ SIGNATURES = [
     ("krb_plan_check", c_int, [c_char_p, c_char_p, c_size_t]),
     ("krb_engine_create", c_int, [c_char_p, c_char_p, c_int, c_int, c_int, c_int, c_int,
                                   ctypes.POINTER(c_void_p)]),
+    ("krb_microdag_create", c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_char_p,
+                                    c_u64, ctypes.POINTER(c_void_p)]),
     ("krb_engine_destroy", None, [c_void_p]),
     ("krb_engine_ipc_handle", c_int, [c_void_p, c_void_p, c_size_t]),
     ("krb_engine_open_peers", c_int, [c_void_p, c_void_p, c_size_t]),
@@ -93,6 +95,7 @@ SIGNATURES = [
     ("krb_engine_verify", c_int, [c_void_p, c_char_p, c_size_t]),
     ("krb_engine_last_logits", c_int, [c_void_p, c_void_p, c_int]),
     ("krb_engine_final_hidden", c_int, [c_void_p, c_void_p, c_size_t]),
+    ("krb_engine_final_x", c_int, [c_void_p, c_void_p, c_size_t]),
     ("krb_engine_layer_dump", c_int, [c_void_p, c_int]),
     ("krb_engine_layer_hidden", c_int, [c_void_p, c_int, c_void_p, c_size_t]),
     ("krb_engine_info", c_int, [c_void_p, c_char_p, c_size_t]),
@@ -331,12 +334,42 @@ class Engine:
     its relay region.  For tp modes the ranks are wired with open_peers (split)
     or init_nccl (baseline) after all engines exist."""
 
-    def __init__(self, model_dir, mode, seq, rank=0, world=1, device=0, tiles=4):
-        h = c_void_p()
-        check(lib().krb_engine_create(str(model_dir).encode(), mode.encode(), seq, rank, world,
-                                      device, tiles, ctypes.byref(h)), "engine_create")
+    def __init__(self, model_dir, mode, seq, rank=0, world=1, device=0, tiles=4, _handle=None):
+        h = _handle
+        if h is None:
+            h = c_void_p()
+            check(lib().krb_engine_create(str(model_dir).encode(), mode.encode(), seq, rank, world,
+                                          device, tiles, ctypes.byref(h)), "engine_create")
         self.h = h
         self.rank, self.world, self.device = rank, world, device
+
+    @classmethod
+    def microdag(cls, seq, hidden, intermediate, mode, rank=0, world=1, device=0, tiles=4,
+                 seed=1234):
+        """The isolated TP-MLP micro-DAG (krb_microdag_create): this rank's down GEMM over
+        X_r, W_r, the reduction over the ranks and the Add+RMSNorm with R."""
+        h = c_void_p()
+        check(lib().krb_microdag_create(seq, hidden, intermediate, tiles, rank, world, device,
+                                        mode.encode(), seed, ctypes.byref(h)), "microdag_create")
+        return cls(None, mode, seq, rank=rank, world=world, device=device, tiles=tiles, _handle=h)
+
+    def final_hidden(self):
+        """fp32 [S, H] residual after the last layer (micro-DAG: h = R + sum of partials)."""
+        import numpy as np
+        info = self.info()
+        n = info["seq"] * info["H"]
+        out = np.empty(n, dtype=np.float32)
+        check(lib().krb_engine_final_hidden(self.h, out.ctypes.data_as(c_void_p), n), "final_hidden")
+        return out.reshape(info["seq"], info["H"])
+
+    def final_x(self):
+        """bf16 [S, H] final normed rows as fp32 numpy (micro-DAG: x = RMSNorm(h))."""
+        import numpy as np
+        info = self.info()
+        n = info["seq"] * info["H"]
+        out = np.empty(n, dtype=np.uint16)
+        check(lib().krb_engine_final_x(self.h, out.ctypes.data_as(c_void_p), n), "final_x")
+        return (out.astype(np.uint32) << 16).view(np.float32).reshape(info["seq"], info["H"])
 
     def close(self):
         if self.h:

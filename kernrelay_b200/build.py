@@ -84,7 +84,8 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False) -> Pa
         objs.append(obj)
         cmd = [nvcc] + common + ["-c", str(src), "-o", str(obj)]
         if src.suffix == ".cpp":
-            cmd = [nvcc, "-x", "cu"] + common + ["-c", str(src), "-o", str(obj)]
+            # host runtime: C++20 (std::barrier for the per-device worker threads)
+            cmd = [nvcc, "-x", "cu"] + common + ["-std=c++20", "-c", str(src), "-o", str(obj)]
         jobs.append(cmd)
 
     def run(cmd):

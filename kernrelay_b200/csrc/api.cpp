@@ -4,6 +4,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <barrier>
 #include <chrono>
 #include <condition_variable>
 #include <cstdio>
@@ -108,27 +109,6 @@ std::string stage_json(krb::Engine &e, const std::string &mode, int warmup, int 
      << ",\"has_ref\":" << (v.has_ref ? "true" : "false") << "}";
   return os.str();
 }
-
-class Barrier {
- public:
-  explicit Barrier(int n) : n_(n) {}
-  void wait() {
-    std::unique_lock<std::mutex> lk(m_);
-    const int gen = gen_;
-    if (++count_ == n_) {
-      count_ = 0;
-      ++gen_;
-      cv_.notify_all();
-    } else {
-      cv_.wait(lk, [&] { return gen_ != gen; });
-    }
-  }
-
- private:
-  std::mutex m_;
-  std::condition_variable cv_;
-  int n_, count_ = 0, gen_ = 0;
-};
 
 }  // namespace
 
@@ -421,7 +401,7 @@ KRB_EXPORT int kr_qwen_tp_run(const char *model_dir, const char *mode, int seq, 
         throw std::runtime_error("ncclCommInitAll failed");
       for (int r = 0; r < k; ++r) eng[r]->set_nccl(comms[r]);
     }
-    Barrier bar(k + 1);
+    std::barrier<> bar(k + 1);  // the k workers and the timing thread
     std::mutex mu;
     std::string err;
     std::vector<std::string> stage(k);
@@ -447,25 +427,25 @@ KRB_EXPORT int kr_qwen_tp_run(const char *model_dir, const char *mode, int seq, 
         v = e.verify();
         if (e.mode().graph) e.capture_graph();
       });
-      bar.wait();
+      bar.arrive_and_wait();
       for (int w = 0; w < warmup; ++w) {
-        bar.wait();
+        bar.arrive_and_wait();
         guard([&] {
           e.run();
           e.sync();
         });
-        bar.wait();
+        bar.arrive_and_wait();
       }
       std::vector<double> samples;
       for (int i = 0; i < std::max(1, iters); ++i) {
-        bar.wait();
+        bar.arrive_and_wait();
         const auto t0 = Clock::now();
         guard([&] {
           e.run();
           e.sync();
         });
         samples.push_back(us_between(t0, Clock::now()));
-        bar.wait();
+        bar.arrive_and_wait();
       }
       guard([&] {
         v = e.verify();
@@ -474,22 +454,22 @@ KRB_EXPORT int kr_qwen_tp_run(const char *model_dir, const char *mode, int seq, 
         stage[r] = stage_json(e, "tp_rank" + std::to_string(r), warmup, iters, samples, {}, v, st,
                               e.mode().split ? e.cfg().L * t_eff : 0);
       });
-      bar.wait();
+      bar.arrive_and_wait();
     };
     std::vector<std::thread> th;
     for (int r = 0; r < k; ++r) th.emplace_back(worker, r);
-    bar.wait();  // first run + verify done
+    bar.arrive_and_wait();  // first run + verify done
     for (int w = 0; w < warmup; ++w) {
-      bar.wait();
-      bar.wait();
+      bar.arrive_and_wait();
+      bar.arrive_and_wait();
     }
     for (int i = 0; i < std::max(1, iters); ++i) {
-      bar.wait();
+      bar.arrive_and_wait();
       const auto t0 = Clock::now();
-      bar.wait();
+      bar.arrive_and_wait();
       wall.push_back(us_between(t0, Clock::now()));
     }
-    bar.wait();
+    bar.arrive_and_wait();
     for (auto &t : th) t.join();
     eng.clear();  // graphs that hold NCCL work go before the communicators
     for (int r = 0; r < k; ++r) {
@@ -886,6 +866,36 @@ struct krb_engine {
   ncclComm_t comm = nullptr;
 };
 
+KRB_EXPORT int krb_microdag_create(int seq, int hidden, int intermediate, int tiles, int rank,
+                                   int world, int device, const char *mode, uint64_t seed,
+                                   krb_engine **out) {
+  try {
+    if (!mode || !out) throw std::runtime_error("null argument");
+    krb::EngineOpts o;
+    o.mode = mode;
+    o.seq = seq;
+    o.rank = rank;
+    o.world = world;
+    o.device = device;
+    o.tiles = tiles;
+    o.microdag = true;
+    o.md_H = hidden;
+    o.md_I = intermediate;
+    o.md_seed = seed;
+    auto *h = new krb_engine();
+    try {
+      h->e = std::make_unique<krb::Engine>(o);
+    } catch (...) {
+      delete h;
+      throw;
+    }
+    *out = h;
+    return 0;
+  } catch (const std::exception &e) {
+    return fail(e);
+  }
+}
+
 KRB_EXPORT int krb_engine_create(const char *model_dir, const char *mode, int seq, int rank,
                                  int world, int device, int tiles, krb_engine **out) {
   try {
@@ -1099,10 +1109,24 @@ KRB_EXPORT int krb_engine_final_hidden(krb_engine *h, float *out, size_t n) {
   const krb::ModelCfg &c = h->e->cfg();
   const size_t need = size_t(c.seq) * c.H;
   if (n < need) throw std::runtime_error("buffer too small");
-  if (h->e->rank() != 0) throw std::runtime_error("only rank 0 holds the final hidden state");
+  if (h->e->rank() != 0 && !h->e->microdag())
+    throw std::runtime_error("only rank 0 holds the final hidden state");
   KRB_CUDA(cudaSetDevice(h->e->device()));
   KRB_CUDA(cudaStreamSynchronize(h->e->stream()));
   KRB_CUDA(cudaMemcpy(out, h->e->hidden_ptr(), need * 4, cudaMemcpyDeviceToHost));
+  KRB_OP_END
+}
+
+KRB_EXPORT int krb_engine_final_x(krb_engine *h, uint16_t *out, size_t n) {
+  KRB_OP_BEGIN
+  const krb::ModelCfg &c = h->e->cfg();
+  const size_t need = size_t(c.seq) * c.H;
+  if (n < need) throw std::runtime_error("buffer too small");
+  if (h->e->rank() != 0 && !h->e->microdag())
+    throw std::runtime_error("only rank 0 holds the final normed rows");
+  KRB_CUDA(cudaSetDevice(h->e->device()));
+  KRB_CUDA(cudaStreamSynchronize(h->e->stream()));
+  KRB_CUDA(cudaMemcpy(out, h->e->final_x_ptr(), need * 2, cudaMemcpyDeviceToHost));
   KRB_OP_END
 }
 

@@ -150,7 +150,26 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
     throw std::runtime_error("mode tp degree does not match world size");
   KRB_CUDA(cudaSetDevice(opts_.device));
   KRB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-  m_ = load_manifest(opts_.model_dir);
+  if (opts_.microdag) {
+    // no model directory: one "layer" holding only the down projection
+    if (!mode_.tp) throw std::runtime_error("micro-DAG: mode must be tp{k} or tp{k}_split");
+    if (opts_.md_H <= 0 || opts_.md_I <= 0) throw std::runtime_error("micro-DAG: bad shape");
+    m_.dir.clear();
+    ModelCfg &g = m_.cfg;
+    g.arch = "tp_mlp_microdag";
+    g.H = opts_.md_H;
+    g.I = opts_.md_I;
+    g.L = 1;
+    g.HQ = g.HKV = 1;
+    g.D = 128;
+    g.V = 0;
+    g.eps = 1e-6;
+    g.seq = opts_.seq;
+    g.max_pos = opts_.seq;
+    g.seed = opts_.md_seed;
+  } else {
+    m_ = load_manifest(opts_.model_dir);
+  }
   const ModelCfg &c = m_.cfg;
   if (c.seq != opts_.seq) throw std::runtime_error("manifest seq mismatch");
   if (c.I % opts_.world) throw std::runtime_error("intermediate size not divisible by tp degree");
@@ -186,8 +205,12 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
   }
   status_ = static_cast<uint32_t *>(alloc(256));
   KRB_CUDA(cudaMemset(status_, 0, 256));
-  load_weights();
-  alloc_activations();
+  if (opts_.microdag) {
+    load_microdag();
+  } else {
+    load_weights();
+    alloc_activations();
+  }
   if (mode_.split) {
     const int S = opts_.seq, T = opts_.tiles, k = opts_.world;
     if ((S / T) % 128) throw std::runtime_error("tp_split needs seq/tiles to be a multiple of 128");
@@ -549,6 +572,16 @@ void Engine::layer(int l, StageTimes *st) {
   float *sum_out = last ? hf_ : h0_;
   __nv_bfloat16 *x_out = last ? xf_ : x_;
   const bool do_norm = !last || opts_.rank == 0;
+  down_stage(l, st, gamma ? gamma : lw_[l].ln1, sum_out, x_out, do_norm);  // rank != 0, last: unused
+}
+
+void Engine::down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float *sum_out,
+                        __nv_bfloat16 *x_out, bool do_norm) {
+  const ModelCfg &c = m_.cfg;
+  const int S = opts_.seq, H = c.H;
+  const float eps = float(c.eps);
+  const LayerW &w = lw_[l];
+  StageRec rec(stream_, st, g_events);
   if (mode_.split) {
     RelayArgs ra{};
     ra.S = S;
@@ -577,7 +610,7 @@ void Engine::layer(int l, StageTimes *st) {
     ra.layer = l;
     ra.L = c.L;
     ra.resid = h1_;
-    ra.gamma = gamma ? gamma : lw_[l].ln1;  // rank != 0, last layer: unused
+    ra.gamma = gamma;
     ra.sum_out = sum_out;
     ra.x_out = x_out;
     ra.eps = eps;
@@ -636,9 +669,52 @@ void Engine::epilogue(StageTimes *st) {
 
 void Engine::enqueue() { enqueue_stage(nullptr); }
 
+void Engine::microdag_enqueue(StageTimes *st) {
+  if (mode_.split) {
+    bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch()), stream_);
+    ++launches_;
+  }
+  down_stage(0, st, md_gamma_, hf_, xf_, true);  // every rank normalises its rows
+}
+
+// Micro-DAG inputs, generated on the device: X_r, W_r with seed
+// md_seed + rank, R with md_seed, gamma = 1.
+void Engine::load_microdag() {
+  const ModelCfg &c = m_.cfg;
+  const size_t S = size_t(opts_.seq), H = size_t(c.H), K = size_t(Iloc_);
+  const uint64_t sr = opts_.md_seed + uint64_t(opts_.rank);
+  auto A = [&](size_t elems) { return static_cast<__nv_bfloat16 *>(alloc(elems * 2)); };
+  auto F = [&](size_t elems) { return static_cast<float *>(alloc(elems * 4)); };
+  __nv_bfloat16 *stg = nullptr;
+  KRB_CUDA(cudaMalloc(reinterpret_cast<void **>(&stg), std::max(K * H, S * H) * 2));
+  lw_.resize(1);
+  // W_r [K, H] (the reference's down_proj.weight_t layout) -> Wdown [H, K]
+  lw_[0].wdown = A(H * K);
+  synth_normal_device(stg, K * H, synth_key("microdag.W_down", sr), 0.02, 0.0, stream_);
+  transpose_bf16(stg, H, lw_[0].wdown, K, K, H, stream_);
+  act_ = A(S * K);
+  synth_normal_device(act_, S * K, synth_key("microdag.X", sr), 1.0, 0.0, stream_);
+  h1_ = F(S * H);  // residual R, exact in fp32
+  synth_normal_device(stg, S * H, synth_key("microdag.R", opts_.md_seed), 1.0, 0.0, stream_);
+  bf16_row_to_f32(stg, h1_, int(S * H), stream_);
+  md_gamma_ = A(H);
+  fill_const_device(md_gamma_, H, 1.0f, stream_);
+  hf_ = F(S * H);
+  xf_ = A(S * H);
+  delta_ = F(S * H);
+  down_ = A(S * H);
+  if (mode_.world > 1 && !mode_.split) red_ = A(S * H);
+  KRB_CUDA(cudaStreamSynchronize(stream_));
+  KRB_CUDA(cudaFree(stg));
+}
+
 void Engine::enqueue_stage(const float *h_in) {
   KRB_CUDA(cudaSetDevice(opts_.device));
   launches_ = 0;
+  if (opts_.microdag) {
+    microdag_enqueue(nullptr);
+    return;
+  }
   const size_t SH = size_t(opts_.seq) * m_.cfg.H;
   if (layer_begin_ == 0) {
     prologue(nullptr);
@@ -746,9 +822,13 @@ StageTimes Engine::instrumented_run() {
   KRB_CUDA(cudaEventRecord(a, stream_));
   launches_ = 0;
   try {
-    prologue(&st);
-    for (int l = 0; l < m_.cfg.L; ++l) layer(l, &st);
-    epilogue(&st);
+    if (opts_.microdag) {
+      microdag_enqueue(&st);
+    } else {
+      prologue(&st);
+      for (int l = 0; l < m_.cfg.L; ++l) layer(l, &st);
+      epilogue(&st);
+    }
   } catch (...) {
     g_events = nullptr;
     throw;

@@ -83,6 +83,15 @@ struct EngineOpts {
   int lm_rows = -1;   // -1: all S rows (reference); 1: last row only
   int pp_stage = 0;   // pp modes: this engine's stage and the number of stages
   int pp_stages = 1;
+  // Isolated TP-MLP micro-DAG (no model directory): per rank, X_r [seq, md_I/world]
+  // ~ N(0,1) and W_r [md_I/world, md_H] ~ N(0,0.02) (seed md_seed + rank), residual
+  // R [seq, md_H] ~ N(0,1) (seed md_seed), gamma = 1; one step = down GEMM ->
+  // reduction over the ranks -> Add+RMSNorm, by the relay (split modes) or GEMM +
+  // NCCL AllReduce + Add+RMSNorm (tp modes).  Tensor names: microdag.X,
+  // microdag.W_down, microdag.R (the synthetic generator of synth.cuh).
+  bool microdag = false;
+  int md_H = 0, md_I = 0;
+  uint64_t md_seed = 1234;
 };
 
 // Per-stage device time accumulated by an instrumented run (microseconds).
@@ -139,7 +148,10 @@ class Engine {
   int layer_begin() const { return layer_begin_; }
   int layer_end() const { return layer_end_; }
   // this engine produces the logits: TP rank 0 of the last pipeline stage
-  bool has_logits() const { return opts_.rank == 0 && layer_end_ == m_.cfg.L; }
+  bool has_logits() const { return !opts_.microdag && opts_.rank == 0 && layer_end_ == m_.cfg.L; }
+  bool microdag() const { return opts_.microdag; }
+  // final normed rows xf [S, H] bf16 (the micro-DAG's x output)
+  const __nv_bfloat16 *final_x_ptr() const { return xf_; }
   // pp: enqueue this stage's part of one prefill; a later stage takes the fp32
   // residual stream [S, H] of the previous stage from `h_in` (device memory)
   void enqueue_stage(const float *h_in);
@@ -158,6 +170,12 @@ class Engine {
   void alloc_activations();
   void fetch(const std::string &name, __nv_bfloat16 *staging);
   void layer(int l, StageTimes *st);
+  // layer l's down projection, reduction over the ranks and Add+RMSNorm (the tile loop
+  // of qwen_main.cpp:1274-1302, or its unsplit form)
+  void down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float *sum_out,
+                  __nv_bfloat16 *x_out, bool do_norm);
+  void load_microdag();
+  void microdag_enqueue(StageTimes *st);
   void prologue(StageTimes *st);
   void epilogue(StageTimes *st);
   void add_norm(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
@@ -183,7 +201,7 @@ class Engine {
   };
   std::vector<LayerW> lw_;
   __nv_bfloat16 *embed_ = nullptr, *wlm_ = nullptr, *final_norm_ = nullptr, *cos_ = nullptr,
-                *sin_ = nullptr;
+                *sin_ = nullptr, *md_gamma_ = nullptr;
   std::vector<void *> allocs_;
   void *weight_map_ = nullptr;
   size_t weight_map_bytes_ = 0;

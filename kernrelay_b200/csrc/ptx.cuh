@@ -26,6 +26,10 @@ enum StatusBits : uint32_t {
   kStatusFlagWait = 1u << 6,     // stand-alone flag wait (publish/wait pair)
   kStatusBadArgs = 1u << 7,      // kernel refused its arguments
   kStatusBadIndex = 1u << 8,     // plan executor: embedding index outside [0, V)
+  // relay: a bulk copy from a peer still had not completed when the CTA gave up waiting
+  // for it at exit; that copy may still write this SM's shared memory, so the context
+  // must be treated as suspect (recreate it) after this bit
+  kStatusCopyDrain = 1u << 9,
 };
 
 // Limit of every mbarrier wait: far beyond any legal wait inside one kernel.

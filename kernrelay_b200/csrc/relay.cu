@@ -428,8 +428,10 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     timeout = 0;
   };
   auto drain = [&]() {
-    // no bulk copy may still be writing this CTA's shared memory when it exits
-    if (ra.bulk && stuck && leader) mbar_wait(pbar, phase, ra.timeout_ns);
+    // no bulk copy may still be writing this CTA's shared memory when it exits; if the
+    // copy does not land within another timeout the CTA leaves anyway and says so
+    if (ra.bulk && stuck && leader && !mbar_wait(pbar, phase, ra.timeout_ns))
+      report_status(ra.status, kStatusCopyDrain);
   };
 
   if constexpr (KR == 1) {
@@ -663,7 +665,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
   // whichever of rs(next_rs) and ag(next_ag) is ready first (reduce-scatter when both
   // are: the peers' all-gathers wait on it) instead of blocking ag(t) behind the
   // partials of tile t+1.  An all-gather never runs before its own reduce-scatter.
-  uint32_t rs_failed = 0;  // bit t: the reduce-scatter of tile t failed (T <= 32)
+  uint32_t rs_failed = 0;  // bit t: the reduce-scatter of tile t failed (T <= 32, host-checked)
   int next_rs = 0, next_ag = 0;
   while (next_ag < ra.T) {
     bool do_rs = next_rs < ra.T;
@@ -693,10 +695,10 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
       }
     }
     if (do_rs) {
-      if (!rs_phase(next_rs)) rs_failed |= 1u << (next_rs & 31);
+      if (!rs_phase(next_rs)) rs_failed |= 1u << next_rs;
       ++next_rs;
     } else {
-      ag_phase(next_ag, ((rs_failed >> (next_ag & 31)) & 1u) == 0);
+      ag_phase(next_ag, ((rs_failed >> next_ag) & 1u) == 0);
       ++next_ag;
     }
   }
@@ -857,6 +859,8 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
   const CUtensorMap tma = make_tmap_2d_bf16(act, ra.S, ra.K, lda, kBM, kBK);
   const int grid = sm_count(dev);
   if (ra.k > 1 && 2 * ra.T > grid) throw CudaError("relay: more row tiles than signal jobs");
+  // the reduce-scatter failure mask of the consumer holds one bit per row tile
+  if (ra.k > 1 && ra.T > 32) throw CudaError("relay: at most 32 row tiles with more than one rank");
   auto by_ranks = [&](auto bn_tag) {
     constexpr int B = decltype(bn_tag)::value;
     // bulk staging serves the exchange paths: reduce-scatter + all-gather, and the

@@ -59,6 +59,8 @@ def qwen_tp_run(model_dir, mode="tp2", seq=2048, dev0=0, dev1=1, tiles=2, warmup
 
 
 def plan_run(schedule_json, devices="0,1", mode="direct", iters=3, warmup=1, out_json=None):
+    """Run a reference-scheduler schedule.json through kr_plan_run; the library writes its
+    result (or {"error": ...}) to `out_json`, which is read back here."""
     out = Path(out_json) if out_json else Path(tempfile.mkstemp(prefix="kr_plan_", suffix=".json")[1])
     rc = lib().kr_plan_run(str(schedule_json).encode(), int(iters), int(warmup),
                            str(devices).encode(), mode.encode(), str(out).encode())
@@ -71,7 +73,8 @@ def plan_run(schedule_json, devices="0,1", mode="direct", iters=3, warmup=1, out
 
 
 def qwen_profile_many(model_dir, cases, seq=2048, device=0):
-    """cases: [{"op":..., "k":...}] -> dict; weights loaded once."""
+    """Time a list of profile cases (each {"op": name, "k": slices}) against one loaded
+    copy of the model through kr_qwen_profile_many; returns the decoded result JSON."""
     fd, path = tempfile.mkstemp(prefix="kr_profile_", suffix=".json")
     os.close(fd)
     Path(path).write_text(json.dumps({"cases": cases}), encoding="utf-8")

@@ -16,8 +16,13 @@ def _bench(args, env_extra):
 
 
 def test_reference_arm_prints_one_contract_line():
-    p = _bench(["--impl", "reference", "--steps", "1", "--warmup", "0", "--seq", "256"],
-               {"RANK": "0", "WORLD_SIZE": "1"})
+    """Each reference step is a complete prefill that is really timed: the steps times
+    ms_per_step fit inside the process's own wall time (no extrapolated steps)."""
+    import time
+    t0 = time.time()
+    p = _bench(["--impl", "reference", "--steps", "2", "--warmup", "1", "--seq", "256",
+                "--config", "qwen2.5-0.5b"], {"RANK": "0", "WORLD_SIZE": "1"})
+    wall = time.time() - t0
     assert p.returncode == 0, p.stderr[-2000:]
     lines = [l for l in p.stdout.splitlines() if l.strip()]
     assert len(lines) == 1
@@ -31,6 +36,10 @@ def test_reference_arm_prints_one_contract_line():
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
+    assert d["steps"] == 2 and d["warmup"] == 1
+    assert d["steps"] * d["ms_per_step"] / 1e3 <= wall
+    assert abs(d["steps"] * d["ms_per_step"] / 1e3 - d["timed_wall_s"]) < 0.05
+    assert d["config"]["workload"] == "qwen2.5-0.5b prefill S=256 batch 1"
 
 
 def test_reference_arm_other_ranks_exit_quietly():

@@ -1,11 +1,12 @@
 """krb_relay_down_single_noalloc (the allocation-free form of krb_relay_down_single)
-called through the C ABI against the allocating entry point on the same inputs.
+called through the C ABI against the allocating entry point on the same inputs, and
+against a plain torch fp32 computation of the same op (so a fault shared by both
+entry points, which run the same kernel, cannot pass).
 
 Named to be collected last, so it also runs after every other test of the
 session; it passes alone in a fresh process as well, where its first call does
-the per-device set-up.  Tolerance: the two entry points run the same kernel, so
-they agree to the relay test's own bound (sum: 1e-3 * max|ref| + 1e-2;
-x: 1e-2 * max|ref|)."""
+the per-device set-up.  Tolerance: the relay test's own bound (sum: 1e-3 * max|ref|
++ 1e-2; x: 1e-2 * max|ref|)."""
 import pytest
 
 
@@ -32,6 +33,9 @@ def test_noalloc_matches_allocating_entry(cuda, krlib, S, H, K, tiles, bn):
     s_ref, x_ref = krlib.relay_down_single(act, W, resid, gamma, tiles, 1e-6, bn=bn, status=status)
     torch.cuda.synchronize()
     assert status.item() == 0
+    # independent fp32 reference: sum = resid + act . W^T, x = RMSNorm(sum) * gamma
+    s_t = resid + act.float() @ W.float().T
+    x_t = s_t * torch.rsqrt(s_t.pow(2).mean(-1, keepdim=True) + 1e-6) * gamma.float()
 
     # two calls in a row on one stream, each into fresh NaN-filled outputs, so a
     # call that skipped work (stale counters, wrong epoch) cannot pass
@@ -46,6 +50,8 @@ def test_noalloc_matches_allocating_entry(cuda, krlib, S, H, K, tiles, bn):
         assert torch.isfinite(s).all() and torch.isfinite(x.float()).all()
         _close(s, s_ref, rel=1e-3, abs_=1e-2)
         _close(x, x_ref, rel=1e-2, abs_=0)
+        _close(s, s_t, rel=1e-3, abs_=1e-2)
+        _close(x, x_t, rel=1e-2, abs_=0)
 
 
 def test_noalloc_rejects_tiles_beyond_scratch(krlib):
