@@ -211,8 +211,8 @@ int krb_engine_last_logits(krb_engine *e, float *out, int n);
 /* copy the fp32 residual stream after the final layer ([S,H], rank 0; every rank of
  * a micro-DAG engine) to host */
 int krb_engine_final_hidden(krb_engine *e, float *out, size_t n);
-/* copy the final normed rows xf ([S,H] bf16 bits, rank 0; every rank of a
- * micro-DAG engine) to host */
+/* copy the final normed rows xf ([S,H] fp16, rank 0; every rank of a micro-DAG
+ * engine) to host */
 int krb_engine_final_x(krb_engine *e, uint16_t *out, size_t n);
 /* keep a copy of the residual stream after every layer of the next runs
  * (test-sized models: L*S*H*2 bytes of device memory) */

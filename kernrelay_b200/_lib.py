@@ -363,13 +363,13 @@ class Engine:
         return out.reshape(info["seq"], info["H"])
 
     def final_x(self):
-        """bf16 [S, H] final normed rows as fp32 numpy (micro-DAG: x = RMSNorm(h))."""
+        """fp16 [S, H] final normed rows as fp32 numpy (micro-DAG: x = RMSNorm(h))."""
         import numpy as np
         info = self.info()
         n = info["seq"] * info["H"]
-        out = np.empty(n, dtype=np.uint16)
+        out = np.empty(n, dtype=np.float16)
         check(lib().krb_engine_final_x(self.h, out.ctypes.data_as(c_void_p), n), "final_x")
-        return (out.astype(np.uint32) << 16).view(np.float32).reshape(info["seq"], info["H"])
+        return out.astype(np.float32).reshape(info["seq"], info["H"])
 
     def close(self):
         if self.h:

@@ -807,7 +807,10 @@ KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float tim
     ra.do_norm = 1;
     ra.timeout_ns = uint64_t(double(timeout_ms) * 1e6);
     ra.status = status;
-    krb::relay_down_layer(act, K, w, K, 256, ra, nullptr);
+    // the engine's exchange path (fp16 operands; the buffers are zero, the same bits in
+    // either format)
+    krb::relay_down_layer(reinterpret_cast<const __half *>(act), K,
+                          reinterpret_cast<const __half *>(w), K, 256, ra, nullptr);
     KRB_CUDA(cudaDeviceSynchronize());
     KRB_CUDA(cudaMemcpy(status_out, status, 4, cudaMemcpyDeviceToHost));
     cudaFree(mine);

@@ -1,4 +1,5 @@
 // Causal GQA prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Q, K and the output are bf16 or fp16 (the engine runs fp16); V^T and P are fp16.
 //
 // Replaces aclnnFlashAttentionScore (BSND, sparse_mode 3, scale 1/sqrt(D);
 // qwen_main.cpp:591-614) for head_dim 64 and 128.  One CTA = one query head x two
@@ -227,10 +228,11 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
 // Grid (heads of this launch, tile pairs); query head h = h0 + blockIdx.x reads KV head
 // kv0 + blockIdx.x / group.  HQ is the head count of the qkv layout (K columns start at
 // HQ * D).  Pairs are dispatched longest first over all heads (blocks go x-fastest).
-template <int D>
+// F16: q / k (and so the QK^T operands) and the output are fp16, else bf16.
+template <int D, bool F16>
 __global__ void __launch_bounds__(kAttn2Threads, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tm_qk, const __grid_constant__ CUtensorMap tm_vt,
-                    __nv_bfloat16 *__restrict__ out, long ldo, int S, int HQ, int h0, int kv0,
+                    uint16_t *__restrict__ out, long ldo, int S, int HQ, int h0, int kv0,
                     int group, float scale_log2, uint32_t *status) {
   using C = Attn2Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -309,7 +311,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128);
+      constexpr uint32_t idesc_s = F16 ? idesc_f16_f32(128, 128) : idesc_bf16_f32(128, 128);
       constexpr uint32_t idesc_o = idesc_f16_f32(128, D);  // P and V^T both fp16
       // descriptors of every smem tile, computed once; k-step kk of a tile is the
       // base descriptor plus the step's byte offset >> 4 in the start-address field
@@ -403,7 +405,7 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
     } else if (nx > 0) {
       tc_fence_after();
       const float inv = 1.f / l_run;
-      __nv_bfloat16 *orow = out + static_cast<long>(row) * ldo + static_cast<long>(h) * D;
+      uint16_t *orow = out + static_cast<long>(row) * ldo + static_cast<long>(h) * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
@@ -414,10 +416,10 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]) * inv, __uint_as_float(r[q * 8 + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]) * inv, __uint_as_float(r[q * 8 + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]) * inv, __uint_as_float(r[q * 8 + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]) * inv, __uint_as_float(r[q * 8 + 7]) * inv);
+            w.x = pack2<F16>(__uint_as_float(r[q * 8 + 0]) * inv, __uint_as_float(r[q * 8 + 1]) * inv);
+            w.y = pack2<F16>(__uint_as_float(r[q * 8 + 2]) * inv, __uint_as_float(r[q * 8 + 3]) * inv);
+            w.z = pack2<F16>(__uint_as_float(r[q * 8 + 4]) * inv, __uint_as_float(r[q * 8 + 5]) * inv);
+            w.w = pack2<F16>(__uint_as_float(r[q * 8 + 6]) * inv, __uint_as_float(r[q * 8 + 7]) * inv);
             o4[q] = w;
           }
         }
@@ -432,19 +434,24 @@ __global__ void __launch_bounds__(kAttn2Threads, 1)
 
 // ------------------------------------------------------------------ host side
 // fp16 V^T [HKV*D rows][ldv >= S] of KV heads [kv0, kv0 + nkv) from the fused qkv buffer
-void attention_vt(const __nv_bfloat16 *qkv, __half *vt, long ldv, int S, int HQ, int HKV, int D,
+template <typename T>
+void attention_vt(const T *qkv, __half *vt, long ldv, int S, int HQ, int HKV, int D,
                   cudaStream_t stream, int kv0, int nkv) {
   if (nkv < 0) nkv = HKV - kv0;
   if (kv0 < 0 || nkv <= 0 || kv0 + nkv > HKV) throw CudaError("attention_vt: KV head range");
   const long ld = static_cast<long>(HQ + 2 * HKV) * D;
-  transpose_bf16_to_f16(qkv + static_cast<long>(HQ + HKV + kv0) * D, ld,
-                        vt + static_cast<long>(kv0) * D * ldv, ldv, S, nkv * D, stream);
+  if constexpr (ActFmt<T>::f16)
+    transpose_f16(qkv + static_cast<long>(HQ + HKV + kv0) * D, ld,
+                  vt + static_cast<long>(kv0) * D * ldv, ldv, S, nkv * D, stream);
+  else
+    transpose_bf16_to_f16(qkv + static_cast<long>(HQ + HKV + kv0) * D, ld,
+                          vt + static_cast<long>(kv0) * D * ldv, ldv, S, nkv * D, stream);
 }
 
-template <int D>
-static void launch_attn_tc2(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
-                            __nv_bfloat16 *out, int S, int HQ, int HKV, int h0, int nh, int kv0,
-                            int group, float scale, uint32_t *status, cudaStream_t stream) {
+template <int D, bool F16>
+static void launch_attn_tc2(const void *qkv, const __half *vt, long ldv, void *out, int S, int HQ,
+                            int HKV, int h0, int nh, int kv0, int group, float scale,
+                            uint32_t *status, cudaStream_t stream) {
   using C = Attn2Cfg<D>;
   const long ld = static_cast<long>(HQ + 2 * HKV) * D;
   const CUtensorMap tm_qk = make_tmap_2d_bf16(qkv, S, ld, ld, kTileRows, 64);
@@ -454,21 +461,23 @@ static void launch_attn_tc2(const __nv_bfloat16 *qkv, const __half *vt, long ldv
   KRB_CUDA(cudaGetDevice(&dev));
   static bool configured[64] = {false};
   if (!configured[dev & 63]) {
-    KRB_CUDA(cudaFuncSetAttribute(attn_tc2_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(C::kSmem)));
+    KRB_CUDA(cudaFuncSetAttribute(attn_tc2_kernel<D, F16>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::kSmem)));
     configured[dev & 63] = true;
   }
   const int nqb = (S + kTileRows - 1) / kTileRows;
   dim3 grid(nh, (nqb + 1) / 2);
-  attn_tc2_kernel<D><<<grid, kAttn2Threads, C::kSmem, stream>>>(
-      tm_qk, tm_vt, out, static_cast<long>(HQ) * D, S, HQ, h0, kv0, group,
-      scale * 1.4426950408889634f, status);
+  attn_tc2_kernel<D, F16><<<grid, kAttn2Threads, C::kSmem, stream>>>(
+      tm_qk, tm_vt, static_cast<uint16_t *>(out), static_cast<long>(HQ) * D, S, HQ, h0, kv0,
+      group, scale * 1.4426950408889634f, status);
   KRB_CUDA(cudaGetLastError());
 }
 
-void attention_tc_bf16(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
-                       __nv_bfloat16 *out, int S, int HQ, int HKV, int D, float scale,
-                       uint32_t *status, cudaStream_t stream, int h0, int nh, int kv0, int group) {
+template <typename T>
+void attention_tc(const T *qkv, const __half *vt, long ldv, T *out, int S, int HQ, int HKV, int D,
+                  float scale, uint32_t *status, cudaStream_t stream, int h0, int nh, int kv0,
+                  int group) {
+  constexpr bool F16 = ActFmt<T>::f16;
   if (D != 64 && D != 128) throw CudaError("attention_tc: head_dim must be 64 or 128");
   if (HKV <= 0 || HQ % HKV) throw CudaError("attention_tc: HQ % HKV != 0");
   if (ldv % 8) throw CudaError("attention_tc: V^T pitch must be a multiple of 8");
@@ -478,9 +487,21 @@ void attention_tc_bf16(const __nv_bfloat16 *qkv, const __half *vt, long ldv,
   if (h0 < 0 || nh <= 0 || h0 + nh > HQ || kv0 < 0 || kv0 + (nh - 1) / group >= HKV)
     throw CudaError("attention_tc: head range outside the qkv layout");
   if (D == 128)
-    launch_attn_tc2<128>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status, stream);
+    launch_attn_tc2<128, F16>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status,
+                              stream);
   else
-    launch_attn_tc2<64>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status, stream);
+    launch_attn_tc2<64, F16>(qkv, vt, ldv, out, S, HQ, HKV, h0, nh, kv0, group, scale, status,
+                             stream);
 }
+
+template void attention_vt<__nv_bfloat16>(const __nv_bfloat16 *, __half *, long, int, int, int,
+                                          int, cudaStream_t, int, int);
+template void attention_vt<__half>(const __half *, __half *, long, int, int, int, int,
+                                   cudaStream_t, int, int);
+template void attention_tc<__nv_bfloat16>(const __nv_bfloat16 *, const __half *, long,
+                                          __nv_bfloat16 *, int, int, int, int, float, uint32_t *,
+                                          cudaStream_t, int, int, int, int);
+template void attention_tc<__half>(const __half *, const __half *, long, __half *, int, int, int,
+                                   int, float, uint32_t *, cudaStream_t, int, int, int, int);
 
 }  // namespace krb

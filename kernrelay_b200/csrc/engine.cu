@@ -318,6 +318,8 @@ void Engine::load_weights() {
   __nv_bfloat16 *stg = nullptr;
   KRB_CUDA(cudaMalloc(reinterpret_cast<void **>(&stg), max_elems * 2));
   auto A = [&](size_t elems) { return static_cast<__nv_bfloat16 *>(alloc(elems * 2)); };
+  auto A16 = [&](size_t elems) { return static_cast<__half *>(alloc(elems * 2)); };
+  auto as_bf = [](__half *p) { return reinterpret_cast<__nv_bfloat16 *>(p); };
   auto copy_into = [&](const std::string &name, __nv_bfloat16 *dst) {
     fetch(name, stg);
     KRB_CUDA(cudaMemcpyAsync(dst, stg, m_.at(name).numel() * 2, cudaMemcpyDeviceToDevice, stream_));
@@ -335,15 +337,17 @@ void Engine::load_weights() {
       continue;
     }
     // fused QKV [nq + 2 nkv, H] K-major from q/k/v weight_t [H, n]
-    w.wqkv = A(size_t(nqkv_) * H);
+    // every GEMM weight is re-laid out in bf16, then converted to fp16 in place
+    w.wqkv = A16(size_t(nqkv_) * H);
     const std::string roles[3] = {"q_proj", "k_proj", "v_proj"};
     const int widths[3] = {nq, nkv, nkv};
     int off = 0;
     for (int i = 0; i < 3; ++i) {
       fetch(p + roles[i] + ".weight_t", stg);
-      transpose_bf16(stg, widths[i], w.wqkv + size_t(off) * H, H, H, widths[i], stream_);
+      transpose_bf16(stg, widths[i], as_bf(w.wqkv) + size_t(off) * H, H, H, widths[i], stream_);
       off += widths[i];
     }
+    bf16_to_f16_inplace(w.wqkv, size_t(nqkv_) * H, stream_);
     if (c.bias) {
       w.bqkv = A(nqkv_);
       off = 0;
@@ -353,11 +357,12 @@ void Engine::load_weights() {
       }
     }
     // o_proj weight_t [nq, H] -> Wo [H, nq]
-    w.wo = A(size_t(H) * nq);
+    w.wo = A16(size_t(H) * nq);
     fetch(p + "o_proj.weight_t", stg);
-    transpose_bf16(stg, H, w.wo, nq, nq, H, stream_);
+    transpose_bf16(stg, H, as_bf(w.wo), nq, nq, H, stream_);
+    bf16_to_f16_inplace(w.wo, size_t(H) * nq, stream_);
     // gate/up weight_t [H, I]: this rank's column slab, interleaved per bn_gu_ block
-    w.wgu = A(size_t(gu_rows_) * H);
+    w.wgu = A16(size_t(gu_rows_) * H);
     KRB_CUDA(cudaMemsetAsync(w.wgu, 0, size_t(gu_rows_) * H * 2, stream_));
     const int half = bn_gu_ / 2;
     const int nblk = gu_rows_ / bn_gu_;
@@ -367,14 +372,16 @@ void Engine::load_weights() {
         const int c0 = b * half;
         const int wdt = std::min(half, Iloc_ - c0);
         if (wdt <= 0) break;
-        transpose_bf16(stg + size_t(r) * Iloc_ + c0, c.I, w.wgu + (size_t(b) * bn_gu_ + part * half) * H,
-                       H, H, wdt, stream_);
+        transpose_bf16(stg + size_t(r) * Iloc_ + c0, c.I,
+                       as_bf(w.wgu) + (size_t(b) * bn_gu_ + part * half) * H, H, H, wdt, stream_);
       }
     }
+    bf16_to_f16_inplace(w.wgu, size_t(gu_rows_) * H, stream_);
     // down weight_t [I, H]: rows [r*Iloc, (r+1)*Iloc) -> Wdown [H, Iloc]
-    w.wdown = A(size_t(H) * Iloc_);
+    w.wdown = A16(size_t(H) * Iloc_);
     fetch(p + "down_proj.weight_t", stg);
-    transpose_bf16(stg + size_t(r) * Iloc_ * H, H, w.wdown, Iloc_, Iloc_, H, stream_);
+    transpose_bf16(stg + size_t(r) * Iloc_ * H, H, as_bf(w.wdown), Iloc_, Iloc_, H, stream_);
+    bf16_to_f16_inplace(w.wdown, size_t(H) * Iloc_, stream_);
     w.ln1 = A(H);
     copy_into(p + "input_layernorm.weight", w.ln1);
     w.ln2 = A(H);
@@ -395,13 +402,17 @@ void Engine::load_weights() {
     final_norm_ = A(H);
     copy_into("final_norm.weight", final_norm_);
     const TensorSpec &lm = m_.at("lm_head.weight_t");
+    wlm_ = A16(size_t(c.V) * H);
     if (lm.synth && lm.kind == "transpose_of" && lm.alias == "embed.weight") {
-      wlm_ = embed_;  // tied: lm_head.weight_t == embed^T, i.e. Wlm [V,H] == embed
+      // tied: lm_head.weight_t == embed^T, i.e. Wlm [V,H] == embed (an fp16 copy; the
+      // gather keeps reading the bf16 table)
+      KRB_CUDA(cudaMemcpyAsync(wlm_, embed_, size_t(c.V) * H * 2, cudaMemcpyDeviceToDevice,
+                               stream_));
     } else {
-      wlm_ = A(size_t(c.V) * H);
       fetch("lm_head.weight_t", stg);
-      transpose_bf16(stg, c.V, wlm_, H, H, c.V, stream_);
+      transpose_bf16(stg, c.V, as_bf(wlm_), H, H, c.V, stream_);
     }
+    bf16_to_f16_inplace(wlm_, size_t(c.V) * H, stream_);
   }
   // rope tables [1,1,max_pos,D] -> used as [max_pos, D]
   cos_ = A(size_t(c.max_pos) * D);
@@ -420,7 +431,7 @@ void Engine::load_weights() {
 void Engine::alloc_activations() {
   const ModelCfg &c = m_.cfg;
   const size_t S = size_t(opts_.seq), H = size_t(c.H);
-  auto A = [&](size_t elems) { return static_cast<__nv_bfloat16 *>(alloc(elems * 2)); };
+  auto A = [&](size_t elems) { return static_cast<__half *>(alloc(elems * 2)); };
   auto F = [&](size_t elems) { return static_cast<float *>(alloc(elems * 4)); };
   h0_ = F(S * H);
   h1_ = F(S * H);
@@ -498,8 +509,8 @@ void Engine::prologue(StageTimes *st) {
 
 // Add + RMSNorm on the fp32 residual stream: one fused kernel, or (unfused serial
 // modes, qwen_main.cpp:976-979) an add pass followed by a separate RMSNorm pass.
-void Engine::add_norm(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
-                      __nv_bfloat16 *y, float *sum) {
+void Engine::add_norm(const float *res, const __half *delta, const __nv_bfloat16 *gamma,
+                      __half *y, float *sum) {
   const ModelCfg &c = m_.cfg;
   const float eps = float(c.eps);
   add_rmsnorm_res_f32(res, delta, gamma, y, sum, opts_.seq, c.H, eps, stream_);
@@ -522,28 +533,28 @@ void Engine::layer(int l, StageTimes *st) {
   if (fuse_rope_) {
     // QK-norm and RoPE in the QKV GEMM's epilogue (no separate pass over q / k)
     // (and writes the fp16 V^T the attention reads: no separate transpose)
-    gemm_qkv_rope_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, H, c.HQ,
-                       c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
-                       c.qk_norm ? w.kn : nullptr, eps, status_, stream_, vt_, ldvt_);
+    gemm_qkv_rope<__half>(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, H, c.HQ,
+                          c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
+                          c.qk_norm ? w.kn : nullptr, eps, status_, stream_, vt_, ldvt_);
     rec.end();
   } else {
     // unfused serial modes: the reference's separate ops (qwen_main.cpp:1336-1357, 567-582)
-    gemm_bf16(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, nqkv_, H, 0, 0,
-              status_, stream_);
+    gemm_store<__half>(x_, H, w.wqkv, H, qkv_, nqkv_, c.bias ? w.bqkv : nullptr, S, nqkv_, H, 0,
+                       0, status_, stream_);
     rec.end();
     rec.begin(st ? &st->rope : nullptr);
-    qk_norm_rope_bf16(qkv_, S, c.HQ, c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
-                      c.qk_norm ? w.kn : nullptr, eps, stream_);
+    qk_norm_rope<__half>(qkv_, S, c.HQ, c.HKV, D, cos_, sin_, c.qk_norm ? w.qn : nullptr,
+                         c.qk_norm ? w.kn : nullptr, eps, stream_);
     ++launches_;
     rec.end();
   }
   rec.begin(st ? &st->attn : nullptr);
   if (!fuse_rope_) {
-    attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);  // the fused QKV epilogue writes it otherwise
+    attention_vt<__half>(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_);  // else the QKV epilogue writes it
     ++launches_;
   }
-  attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D, float(1.0 / std::sqrt(double(D))),
-                    status_, stream_);
+  attention_tc<__half>(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D,
+                       float(1.0 / std::sqrt(double(D))), status_, stream_);
   rec.end();
   if (mode_.fused) {
     // o_proj output kept in fp32 (no bf16 rounding of o); residual add fused into the norm
@@ -556,27 +567,27 @@ void Engine::layer(int l, StageTimes *st) {
     rec.end();
   } else {
     rec.begin(st ? &st->o : nullptr);
-    gemm_bf16(attn_, c.HQ * D, w.wo, c.HQ * D, o_, H, nullptr, S, H, c.HQ * D, 0, 0, status_,
-              stream_);
+    gemm_store<__half>(attn_, c.HQ * D, w.wo, c.HQ * D, o_, H, nullptr, S, H, c.HQ * D, 0, 0,
+                       status_, stream_);
     rec.end();
     rec.begin(st ? &st->addnorm : nullptr);
     add_norm(h0_, o_, w.ln2, x_, h1_);
     rec.end();
   }
   rec.begin(st ? &st->gateup : nullptr);
-  gemm_silu_bf16(x_, H, w.wgu, H, act_, Iloc_, S, Iloc_, H, bn_gu_, 0, status_, stream_);
+  gemm_silu<__half>(x_, H, w.wgu, H, act_, Iloc_, S, Iloc_, H, bn_gu_, 0, status_, stream_);
   rec.end();
 
   const bool last = (l + 1 == c.L);
   const __nv_bfloat16 *gamma = last ? final_norm_ : lw_[l + 1].ln1;
   float *sum_out = last ? hf_ : h0_;
-  __nv_bfloat16 *x_out = last ? xf_ : x_;
+  __half *x_out = last ? xf_ : x_;
   const bool do_norm = !last || opts_.rank == 0;
   down_stage(l, st, gamma ? gamma : lw_[l].ln1, sum_out, x_out, do_norm);  // rank != 0, last: unused
 }
 
 void Engine::down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float *sum_out,
-                        __nv_bfloat16 *x_out, bool do_norm) {
+                        __half *x_out, bool do_norm) {
   const ModelCfg &c = m_.cfg;
   const int S = opts_.seq, H = c.H;
   const float eps = float(c.eps);
@@ -612,7 +623,7 @@ void Engine::down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float
     ra.resid = h1_;
     ra.gamma = gamma;
     ra.sum_out = sum_out;
-    ra.x_out = x_out;
+    ra.x_out = reinterpret_cast<__nv_bfloat16 *>(x_out);  // holds fp16 (the relay's T)
     ra.eps = eps;
     ra.do_norm = do_norm ? 1 : 0;
     ra.timeout_ns = flag_timeout_ns_;
@@ -637,13 +648,14 @@ void Engine::down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float
     return;
   }
   rec.begin(st ? &st->down : nullptr);
-  gemm_bf16(act_, Iloc_, w.wdown, Iloc_, down_, H, nullptr, S, H, Iloc_, bn_down_, 0, status_, stream_);
+  gemm_store<__half>(act_, Iloc_, w.wdown, Iloc_, down_, H, nullptr, S, H, Iloc_, bn_down_, 0,
+                     status_, stream_);
   rec.end();
-  const __nv_bfloat16 *red = down_;
+  const __half *red = down_;
   if (mode_.tp && mode_.world > 1) {
     if (!nccl_) throw std::runtime_error("tp: NCCL communicator missing");
     rec.begin(st ? &st->allreduce : nullptr);
-    if (ncclAllReduce(down_, red_, size_t(S) * H, ncclBfloat16, ncclSum, nccl_, stream_) != ncclSuccess)
+    if (ncclAllReduce(down_, red_, size_t(S) * H, ncclHalf, ncclSum, nccl_, stream_) != ncclSuccess)
       throw std::runtime_error("ncclAllReduce failed");
     rec.end();
     red = red_;
@@ -662,8 +674,8 @@ void Engine::epilogue(StageTimes *st) {
   ++launches_;
   rec.begin(st ? &st->lm_head : nullptr);
   const int r0 = opts_.seq - lm_rows_;
-  gemm_bf16(xf_ + size_t(r0) * c.H, c.H, wlm_, c.H, logits_, c.V, nullptr, lm_rows_, c.V, c.H, 0, 0,
-            status_, stream_);
+  gemm_store<__half>(xf_ + size_t(r0) * c.H, c.H, wlm_, c.H, logits_, c.V, nullptr, lm_rows_, c.V,
+                     c.H, 0, 0, status_, stream_);
   rec.end();
 }
 
@@ -684,26 +696,31 @@ void Engine::load_microdag() {
   const size_t S = size_t(opts_.seq), H = size_t(c.H), K = size_t(Iloc_);
   const uint64_t sr = opts_.md_seed + uint64_t(opts_.rank);
   auto A = [&](size_t elems) { return static_cast<__nv_bfloat16 *>(alloc(elems * 2)); };
+  auto A16 = [&](size_t elems) { return static_cast<__half *>(alloc(elems * 2)); };
   auto F = [&](size_t elems) { return static_cast<float *>(alloc(elems * 4)); };
   __nv_bfloat16 *stg = nullptr;
   KRB_CUDA(cudaMalloc(reinterpret_cast<void **>(&stg), std::max(K * H, S * H) * 2));
   lw_.resize(1);
   // W_r [K, H] (the reference's down_proj.weight_t layout) -> Wdown [H, K]
-  lw_[0].wdown = A(H * K);
+  // bf16 values (the configuration's dtype), held in fp16 exactly like the engine's weights
+  lw_[0].wdown = A16(H * K);
   synth_normal_device(stg, K * H, synth_key("microdag.W_down", sr), 0.02, 0.0, stream_);
-  transpose_bf16(stg, H, lw_[0].wdown, K, K, H, stream_);
-  act_ = A(S * K);
-  synth_normal_device(act_, S * K, synth_key("microdag.X", sr), 1.0, 0.0, stream_);
+  transpose_bf16(stg, H, reinterpret_cast<__nv_bfloat16 *>(lw_[0].wdown), K, K, H, stream_);
+  bf16_to_f16_inplace(lw_[0].wdown, H * K, stream_);
+  act_ = A16(S * K);
+  synth_normal_device(reinterpret_cast<__nv_bfloat16 *>(act_), S * K, synth_key("microdag.X", sr),
+                      1.0, 0.0, stream_);
+  bf16_to_f16_inplace(act_, S * K, stream_);
   h1_ = F(S * H);  // residual R, exact in fp32
   synth_normal_device(stg, S * H, synth_key("microdag.R", opts_.md_seed), 1.0, 0.0, stream_);
   bf16_row_to_f32(stg, h1_, int(S * H), stream_);
   md_gamma_ = A(H);
   fill_const_device(md_gamma_, H, 1.0f, stream_);
   hf_ = F(S * H);
-  xf_ = A(S * H);
+  xf_ = A16(S * H);
   delta_ = F(S * H);
-  down_ = A(S * H);
-  if (mode_.world > 1 && !mode_.split) red_ = A(S * H);
+  down_ = A16(S * H);
+  if (mode_.world > 1 && !mode_.split) red_ = A16(S * H);
   KRB_CUDA(cudaStreamSynchronize(stream_));
   KRB_CUDA(cudaFree(stg));
 }
@@ -765,7 +782,7 @@ void Engine::enqueue_host(const int64_t *ids_host, float *last_logits_host) {
   run();
   if (has_logits() && last_logits_host) {
     const ModelCfg &c = m_.cfg;
-    bf16_row_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
+    f16_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
     KRB_CUDA(cudaMemcpyAsync(last_logits_host, last_f32_, size_t(c.V) * 4, cudaMemcpyDeviceToHost,
                              stream_));
   }
@@ -855,7 +872,7 @@ std::vector<float> Engine::last_logits() {
   std::vector<float> out;
   if (!has_logits()) return out;
   KRB_CUDA(cudaSetDevice(opts_.device));
-  bf16_row_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
+  f16_to_f32(logits_ + size_t(lm_rows_ - 1) * c.V, last_f32_, c.V, stream_);
   out.resize(c.V);
   KRB_CUDA(cudaMemcpyAsync(out.data(), last_f32_, size_t(c.V) * 4, cudaMemcpyDeviceToHost, stream_));
   KRB_CUDA(cudaStreamSynchronize(stream_));

@@ -11,27 +11,37 @@
 
 namespace krb {
 
-template <int BN, int MODE>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// configuration variant of a plain GEMM: fp32 outputs stage in fp32, the rest in 2 bytes
+template <int MODE>
+constexpr int plain_cfg() {
+  return MODE == kEpiStoreF32 ? kCfgPlainF32 : kCfgPlain;
+}
+
+// F16: fp16 operands and 2-byte outputs (bf16 otherwise); fp32 accumulation either way.
+// 10 warps: TMA producer, MMA issuer, 8 epilogue warps.
+template <int BN, int MODE, bool F16>
+__global__ void __launch_bounds__(GemmCfg<BN, plain_cfg<MODE>()>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                 TileSched ts, int M, int K, EpiArgs ea, uint32_t *status) {
+  constexpr int V = plain_cfg<MODE>();
+  using C = GemmCfg<BN, V>;
   extern __shared__ uint8_t smem_raw[];
-  const GemmSmemView<BN> s = GemmSmemView<BN>::carve(smem_raw);
+  const GemmSmemView<BN, V> s = GemmSmemView<BN, V>::carve(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
   }
-  gemm_setup<BN>(s, 128);
+  gemm_setup<BN, V>(s, C::kEpiWarps * 32);
   if (warp == 0) {
-    if (lane == 0) gemm_producer<BN>(s, &ta, &tb, ts, K, status);
+    if (lane == 0) gemm_producer<BN, V>(s, &ta, &tb, ts, K, status);
   } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN, 0, MODE == kEpiStoreF16>(s, ts, K, status);
+    if (lane == 0) gemm_mma<BN, V, F16>(s, ts, K, status);
   } else {
-    gemm_epilogue<BN, MODE>(s, ts, M, ea, status);
+    gemm_epilogue<BN, V, MODE, F16>(s, ts, M, ea, status);
   }
-  gemm_teardown<BN>(s);
+  gemm_teardown<BN, V>(s);
 }
 
 // ------------------------------------------------------------------ host side
@@ -135,14 +145,14 @@ static int pick_band(long M, long N, long K, int num_m) {
   return (a_bytes > 48e6 && b_bytes < 24e6) ? 1 : num_m;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, bool F16>
 static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int n_b_rows, int K,
                         const EpiArgs &ea, int grid_limit, uint32_t *status, cudaStream_t stream) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, plain_cfg<MODE>()>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static bool configured[64] = {false};
-  auto kern = gemm_kernel<BN, MODE>;
+  auto kern = gemm_kernel<BN, MODE, F16>;
   if (!configured[dev & 63]) {
     KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(C::kSmemBytes)));
@@ -155,84 +165,75 @@ static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int
   const int tiles = ts.num_m * ts.num_n;
   int grid = std::min(tiles, sm_count(dev));
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
-  kern<<<grid, kGemmThreads, C::kSmemBytes, stream>>>(ta, tb, ts, M, K, ea, status);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, ts, M, K, ea, status);
   KRB_CUDA(cudaGetLastError());
+}
+
+// B tensor map for one tile width and the launch of MODE for element type T
+template <int MODE, typename T>
+static void dispatch_bn(int bn, const CUtensorMap &ta, const T *B, long ldb, int M, int n_b_rows,
+                        int K, const EpiArgs &ea, int grid_limit, uint32_t *status,
+                        cudaStream_t stream, const char *what) {
+  constexpr bool F16 = ActFmt<T>::f16;
+  switch (bn) {
+    case 256: {
+      const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 256, kBK);
+      launch_gemm<256, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+      break;
+    }
+    case 224:
+      if constexpr (MODE != kEpiSiluMul && MODE != kEpiQkvRope) {
+        const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 224, kBK);
+        launch_gemm<224, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+        break;
+      }
+      [[fallthrough]];
+    case 128:
+      if (bn == 128) {
+        const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 128, kBK);
+        launch_gemm<128, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+        break;
+      }
+      [[fallthrough]];
+    default:
+      throw CudaError(std::string(what) + ": unsupported bn " + std::to_string(bn));
+  }
+}
+
+template <typename T>
+void gemm_store(const T *A, long lda, const T *B, long ldb, T *C, long ldc,
+                const __nv_bfloat16 *bias, int M, int N, int K, int bn, int grid_limit,
+                uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm: empty shape");
+  if (N % 8 != 0 || ldc % 8 != 0) throw CudaError("gemm: N and ldc must be multiples of 8");
+  if (reinterpret_cast<uintptr_t>(C) % 16 || (bias && reinterpret_cast<uintptr_t>(bias) % 16))
+    throw CudaError("gemm: C/bias must be 16-byte aligned");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
+  EpiArgs ea{};
+  ea.c = reinterpret_cast<__nv_bfloat16 *>(C);  // 2-byte rows; the epilogue packs T
+  ea.ldc = ldc;
+  ea.bias = bias;
+  ea.n_out = N;
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  dispatch_bn<kEpiStore>(bn, ta, B, ldb, M, N, K, ea, grid_limit, status, stream, "gemm");
 }
 
 void gemm_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
                __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int N, int K,
                int bn, int grid_limit, uint32_t *status, cudaStream_t stream) {
-  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_bf16: empty shape");
-  if (N % 8 != 0 || ldc % 8 != 0) throw CudaError("gemm_bf16: N and ldc must be multiples of 8");
-  if (reinterpret_cast<uintptr_t>(C) % 16 || (bias && reinterpret_cast<uintptr_t>(bias) % 16))
-    throw CudaError("gemm_bf16: C/bias must be 16-byte aligned");
-  int dev = 0;
-  KRB_CUDA(cudaGetDevice(&dev));
-  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
-  EpiArgs ea{};
-  ea.c = C;
-  ea.ldc = ldc;
-  ea.bias = bias;
-  ea.n_out = N;
-  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
-  switch (bn) {
-    case 256: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
-      launch_gemm<256, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
-      break;
-    }
-    case 224: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
-      launch_gemm<224, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
-      break;
-    }
-    case 128: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
-      launch_gemm<128, kEpiStore>(ta, tb, M, N, K, ea, grid_limit, status, stream);
-      break;
-    }
-    default:
-      throw CudaError("gemm_bf16: unsupported bn " + std::to_string(bn));
-  }
+  gemm_store<__nv_bfloat16>(A, lda, B, ldb, C, ldc, bias, M, N, K, bn, grid_limit, status, stream);
 }
 
 void gemm_f16(const __half *A, long lda, const __half *B, long ldb, __half *C, long ldc, int M,
               int N, int K, int bn, uint32_t *status, cudaStream_t stream) {
-  if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_f16: empty shape");
-  if (N % 8 != 0 || ldc % 8 != 0) throw CudaError("gemm_f16: N and ldc must be multiples of 8");
-  if (reinterpret_cast<uintptr_t>(C) % 16) throw CudaError("gemm_f16: C must be 16-byte aligned");
-  int dev = 0;
-  KRB_CUDA(cudaGetDevice(&dev));
-  if (bn <= 0) bn = pick_bn_store(M, N, sm_count(dev));
-  EpiArgs ea{};
-  ea.c = reinterpret_cast<__nv_bfloat16 *>(C);  // 2-byte rows; the F16 epilogue packs fp16
-  ea.ldc = ldc;
-  ea.n_out = N;
-  // TMA moves 2-byte elements without conversion, so the bf16 tensor map serves fp16 too
-  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
-  switch (bn) {
-    case 256: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
-      launch_gemm<256, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    case 224: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
-      launch_gemm<224, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    case 128: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
-      launch_gemm<128, kEpiStoreF16>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    default:
-      throw CudaError("gemm_f16: unsupported bn " + std::to_string(bn));
-  }
+  gemm_store<__half>(A, lda, B, ldb, C, ldc, nullptr, M, N, K, bn, 0, status, stream);
 }
 
-void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb, float *out,
-                 long ld, int M, int N, int K, int bn, uint32_t *status, cudaStream_t stream) {
+template <typename T>
+void gemm_f32out(const T *A, long lda, const T *B, long ldb, float *out, long ld, int M, int N,
+                 int K, int bn, uint32_t *status, cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) throw CudaError("gemm_f32out: empty shape");
   if (N % 4 != 0 || ld % 4 != 0) throw CudaError("gemm_f32out: N and ld must be multiples of 4");
   if (reinterpret_cast<uintptr_t>(out) % 16) throw CudaError("gemm_f32out: out must be 16B aligned");
@@ -244,33 +245,15 @@ void gemm_f32out(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long 
   ea.n_out = N;
   ea.out_f32 = out;
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
-  switch (bn) {
-    case 256: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
-      launch_gemm<256, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    case 224: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 224, kBK);
-      launch_gemm<224, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    case 128: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
-      launch_gemm<128, kEpiStoreF32>(ta, tb, M, N, K, ea, 0, status, stream);
-      break;
-    }
-    default:
-      throw CudaError("gemm_f32out: unsupported bn " + std::to_string(bn));
-  }
+  dispatch_bn<kEpiStoreF32>(bn, ta, B, ldb, M, N, K, ea, 0, status, stream, "gemm_f32out");
 }
 
-void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
-                        __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int K,
-                        int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
-                        const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
-                        const __nv_bfloat16 *kn, float eps, uint32_t *status,
-                        cudaStream_t stream, __half *vt, long ldvt) {
+template <typename T>
+void gemm_qkv_rope(const T *A, long lda, const T *B, long ldb, T *C, long ldc,
+                   const __nv_bfloat16 *bias, int M, int K, int HQ, int HKV, int D,
+                   const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
+                   const __nv_bfloat16 *qn, const __nv_bfloat16 *kn, float eps, uint32_t *status,
+                   cudaStream_t stream, __half *vt, long ldvt) {
   const int N = (HQ + 2 * HKV) * D;
   if (M <= 0 || K <= 0 || HQ <= 0 || HKV <= 0) throw CudaError("gemm_qkv_rope: empty shape");
   if (D != 64 && D != 128) throw CudaError("gemm_qkv_rope: head_dim must be 64 or 128");
@@ -288,7 +271,7 @@ void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B
   };
   const int bn = cost(256) <= cost(128) ? 256 : 128;
   EpiArgs ea{};
-  ea.c = C;
+  ea.c = reinterpret_cast<__nv_bfloat16 *>(C);
   ea.ldc = ldc;
   ea.bias = bias;
   ea.n_out = N;
@@ -304,45 +287,61 @@ void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B
   ea.ldvt = ldvt;
   if (vt && ldvt < M) throw CudaError("gemm_qkv_rope: V^T pitch below the row count");
   const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
-  if (bn == 256) {
-    const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 256, kBK);
-    launch_gemm<256, kEpiQkvRope>(ta, tb, M, N, K, ea, 0, status, stream);
-  } else {
-    const CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, kBK);
-    launch_gemm<128, kEpiQkvRope>(ta, tb, M, N, K, ea, 0, status, stream);
-  }
+  dispatch_bn<kEpiQkvRope>(bn, ta, B, ldb, M, N, K, ea, 0, status, stream, "gemm_qkv_rope");
+}
+
+void gemm_qkv_rope_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *B, long ldb,
+                        __nv_bfloat16 *C, long ldc, const __nv_bfloat16 *bias, int M, int K,
+                        int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
+                        const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *qn,
+                        const __nv_bfloat16 *kn, float eps, uint32_t *status,
+                        cudaStream_t stream, __half *vt, long ldvt) {
+  gemm_qkv_rope<__nv_bfloat16>(A, lda, B, ldb, C, ldc, bias, M, K, HQ, HKV, D, cos_tab, sin_tab,
+                               qn, kn, eps, status, stream, vt, ldvt);
+}
+
+template <typename T>
+void gemm_silu(const T *A, long lda, const T *Bgu, long ldb, T *act, long ldact, int M,
+               int n_out, int K, int bn, int grid_limit, uint32_t *status, cudaStream_t stream) {
+  if (M <= 0 || n_out <= 0 || K <= 0) throw CudaError("gemm_silu: empty shape");
+  if (n_out % 8 != 0 || ldact % 8 != 0) throw CudaError("gemm_silu: n_out % 8 != 0");
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  if (bn <= 0) bn = pick_bn_silu(M, n_out, sm_count(dev));
+  if (bn != 256 && bn != 128) throw CudaError("gemm_silu: unsupported bn " + std::to_string(bn));
+  const int half = bn / 2;
+  const int nblk = (n_out + half - 1) / half;
+  const int n_b_rows = nblk * bn;
+  EpiArgs ea{};
+  ea.c = reinterpret_cast<__nv_bfloat16 *>(act);
+  ea.ldc = ldact;
+  ea.n_out = n_out;
+  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
+  dispatch_bn<kEpiSiluMul>(bn, ta, Bgu, ldb, M, n_b_rows, K, ea, grid_limit, status, stream,
+                           "gemm_silu");
 }
 
 void gemm_silu_bf16(const __nv_bfloat16 *A, long lda, const __nv_bfloat16 *Bgu, long ldb,
                     __nv_bfloat16 *act, long ldact, int M, int n_out, int K, int bn,
                     int grid_limit, uint32_t *status, cudaStream_t stream) {
-  if (M <= 0 || n_out <= 0 || K <= 0) throw CudaError("gemm_silu_bf16: empty shape");
-  if (n_out % 8 != 0 || ldact % 8 != 0) throw CudaError("gemm_silu_bf16: n_out % 8 != 0");
-  int dev = 0;
-  KRB_CUDA(cudaGetDevice(&dev));
-  if (bn <= 0) bn = pick_bn_silu(M, n_out, sm_count(dev));
-  const int half = bn / 2;
-  const int nblk = (n_out + half - 1) / half;
-  const int n_b_rows = nblk * bn;
-  EpiArgs ea{};
-  ea.c = act;
-  ea.ldc = ldact;
-  ea.n_out = n_out;
-  const CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, kBM, kBK);
-  switch (bn) {
-    case 256: {
-      const CUtensorMap tb = make_tmap_2d_bf16(Bgu, n_b_rows, K, ldb, 256, kBK);
-      launch_gemm<256, kEpiSiluMul>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
-      break;
-    }
-    case 128: {
-      const CUtensorMap tb = make_tmap_2d_bf16(Bgu, n_b_rows, K, ldb, 128, kBK);
-      launch_gemm<128, kEpiSiluMul>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
-      break;
-    }
-    default:
-      throw CudaError("gemm_silu_bf16: unsupported bn " + std::to_string(bn));
-  }
+  gemm_silu<__nv_bfloat16>(A, lda, Bgu, ldb, act, ldact, M, n_out, K, bn, grid_limit, status,
+                           stream);
 }
+
+template void gemm_store<__half>(const __half *, long, const __half *, long, __half *, long,
+                                 const __nv_bfloat16 *, int, int, int, int, int, uint32_t *,
+                                 cudaStream_t);
+template void gemm_f32out<__nv_bfloat16>(const __nv_bfloat16 *, long, const __nv_bfloat16 *, long,
+                                         float *, long, int, int, int, int, uint32_t *,
+                                         cudaStream_t);
+template void gemm_f32out<__half>(const __half *, long, const __half *, long, float *, long, int,
+                                  int, int, int, uint32_t *, cudaStream_t);
+template void gemm_qkv_rope<__half>(const __half *, long, const __half *, long, __half *, long,
+                                    const __nv_bfloat16 *, int, int, int, int, int,
+                                    const __nv_bfloat16 *, const __nv_bfloat16 *,
+                                    const __nv_bfloat16 *, const __nv_bfloat16 *, float,
+                                    uint32_t *, cudaStream_t, __half *, long);
+template void gemm_silu<__half>(const __half *, long, const __half *, long, __half *, long, int,
+                                int, int, int, int, uint32_t *, cudaStream_t);
 
 }  // namespace krb

@@ -2,15 +2,17 @@
 //
 //   C[M, N] = A[M, K] . B[N, K]^T        (A, B bf16 K-major; fp32 accumulate in TMEM)
 //
-// Roles inside one 192-thread CTA (one CTA per SM, persistent over output tiles):
+// Roles inside one CTA (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles into a
 //               STAGES-deep shared-memory ring (128-byte swizzle).
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN,
 //               K=16) into one of two TMEM accumulators and commits to mbarriers.
 //               Warp 1 also owns the TMEM allocation.
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//               32*(w%4)..+31 = tile rows), apply the epilogue, store to HBM, and
-//               hand the accumulator back so the next tile's MMAs overlap.
+//   warps 2..    epilogue (8 warps in plain GEMMs, 4 in the relay kernel):
+//               tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31 =
+//               tile rows; two warps per quadrant split the columns), apply the
+//               epilogue, store to HBM, and hand the accumulator back so the next
+//               tile's MMAs overlap.
 //
 // Tiles are visited in "band" order: the output rows are cut into bands of
 // `band` 128-row blocks; all tiles of band 0 come first (row blocks fastest),
@@ -26,38 +28,55 @@ namespace krb {
 constexpr int kBM = 128;        // UMMA M (cta_group::1)
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row of bf16
 constexpr int kUmmaK = 16;      // K per tcgen05.mma kind::f16
-constexpr int kGemmThreads = 192;
 
 enum EpiMode : int {
   kEpiStore = 0,    // C = bf16(acc [+ bias])
   kEpiSiluMul = 1,  // C[:, j] = bf16(silu(acc[:, g(j)]) * acc[:, u(j)]), interleaved blocks
   kEpiStoreF32 = 2, // out_f32 = acc (fp32, unrounded; consumed by the residual Add+RMSNorm)
   kEpiQkvRope = 3,  // fused QKV: (+bias), per-head QK-RMSNorm (optional) and RoPE on q, k
-  kEpiStoreF16 = 4, // fp16 A, B and C: C = f16(acc)  (the plan executor's matmul)
 };
+// Every mode runs with bf16 or fp16 operands (the kernels' F16 parameter); 2-byte
+// outputs take the operands' format.
 
-// RELAY selects the fused relay kernel's instantiation (same layout today; kept
-// as a separate template parameter so its budget can diverge from plain GEMMs).
-template <int BN, int RELAY = 0>
+// Configuration variants (second template parameter of every helper below):
+//   kCfgPlain    plain GEMM, 8 epilogue warps, 2-byte output staging (bf16 / fp16 outputs)
+//   kCfgRelay    the fused relay kernel: 4 epilogue warps, fp32 staging (its own
+//                budget: relay row buffers sit behind this layout)
+//   kCfgPlainF32 plain GEMM, 8 epilogue warps, fp32 output staging (kEpiStoreF32)
+// Eight epilogue warps (two per TMEM lane quadrant, splitting the tile's columns) halve
+// the epilogue of K = 3584 GEMMs, which otherwise outlasts the tile's MMAs.
+constexpr int kCfgPlain = 0, kCfgRelay = 1, kCfgPlainF32 = 2;
+
+template <int BN, int V = kCfgPlain>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
-  static constexpr int kStages = (BN >= 224) ? 4 : 6;
+  static constexpr int kEpiWarps = V == kCfgRelay ? 4 : 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  // epilogue staging per warp: 32 rows of 32 fp32 padded to 36 (conflict-free
+  // row-wise writes and column-block reads), or 32 rows of 32 2-byte values padded to
+  // 80 bytes (kCfgPlain)
+  static constexpr uint32_t kStageRow = 36;
+  static constexpr uint32_t kStage2Pitch = 80;
+  static constexpr uint32_t kWarpEpiBytes = V == kCfgPlain ? 32 * kStage2Pitch : 32 * kStageRow * 4;
+  static constexpr uint32_t kEpiBytes = kEpiWarps * kWarpEpiBytes;
+  // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
+  // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
+  static constexpr uint32_t kMaxStages = (BN >= 224) ? 4 : 6;
+  static constexpr uint32_t kBarBytesMax = (2 * 6 + 4) * 8 + 16 + 64;
+  static constexpr uint32_t kFit = (232448u - kEpiBytes - kBarBytesMax - 1024u) / kStageBytes;
+  static constexpr uint32_t kStages = V == kCfgRelay ? kMaxStages
+                                                     : (kFit < kMaxStages ? kFit : kMaxStages);
   static constexpr uint32_t kTileBytes = kStages * kStageBytes;
   // TMEM accumulator spacing (power of two) and total allocation.
   static constexpr uint32_t kAccStride = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t kTmemCols = 2 * kAccStride;
-  // epilogue staging: one 32 x 32 fp32 chunk per epilogue warp, rows padded to 36
-  static constexpr uint32_t kStageRow = 36;
-  static constexpr uint32_t kWarpEpiBytes = 32 * kStageRow * 4;
-  static constexpr uint32_t kEpiBytes = 4 * kWarpEpiBytes;
-  // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
-  // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
   static constexpr uint32_t kBarBytes = (2 * kStages + 4) * 8 + 16 + 64;
   static constexpr uint32_t kSmemBytes =
       kTileBytes + kEpiBytes + kBarBytes + 1024;  // +1024 alignment slack
+  static_assert(kStages >= 3, "pipeline depth");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -85,7 +104,7 @@ struct GemmSmemView {
   uint64_t *tempty;
   uint32_t *tmem_slot;
   volatile int *abort;
-  float *epi;  // 4 x [32][kStageRow] fp32 staging chunks (epilogue warps)
+  float *epi;  // kEpiWarps staging chunks of kWarpEpiBytes (epilogue warps)
   float *scratch;  // 16 floats for the relay warps
   __device__ __forceinline__ static GemmSmemView carve(uint8_t *raw) {
     using C = GemmCfg<BN, RELAY>;
@@ -405,12 +424,70 @@ __device__ __forceinline__ void unpack8_f(const uint4 &w, float *f) {
   }
 }
 
-template <int BN, typename RowPtr>
-__device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPtr bf16_row,
-                                             const EpiArgs &ea, int row, bool row_ok, int nb) {
+// 2-byte write-back through the warp's staging block (kCfgPlain): each thread packs
+// its row's 32 values (this 32-column chunk, + bias) into 64 bytes at row pitch 80 B;
+// then lane l stores rows (l % 8) + 8 * it, 16-byte piece l / 8 (a quarter-warp reads
+// 8 rows of one piece: conflict-free, as are the row-wise writes).  row_ptr(r) gives
+// the output row (or null past M); valid = output columns left in this chunk (a
+// multiple of 8 by the callers' checks).
+template <bool F16, typename RowPtr>
+__device__ __forceinline__ void epi2_store(uint8_t *stage2, float *v, const __nv_bfloat16 *bias,
+                                           RowPtr row_ptr, int col0, int valid) {
+  const int lane = threadIdx.x & 31;
+  if (bias) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (q * 8 < valid) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4 *>(bias + col0) + q);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(ws[e]);
+          v[q * 8 + 2 * e] += f.x;
+          v[q * 8 + 2 * e + 1] += f.y;
+        }
+      }
+    }
+  }
+  uint4 *srow = reinterpret_cast<uint4 *>(stage2 + lane * 80);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack2<F16>(v[q * 8 + 0], v[q * 8 + 1]);
+    w.y = pack2<F16>(v[q * 8 + 2], v[q * 8 + 3]);
+    w.z = pack2<F16>(v[q * 8 + 4], v[q * 8 + 5]);
+    w.w = pack2<F16>(v[q * 8 + 6], v[q * 8 + 7]);
+    srow[q] = w;
+  }
+  __syncwarp();
+  const int piece = lane >> 3;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane & 7);
+    const uint4 w = *reinterpret_cast<const uint4 *>(stage2 + r * 80 + piece * 16);
+    __nv_bfloat16 *dst = row_ptr(r);
+    if (dst && piece * 8 < valid) *reinterpret_cast<uint4 *>(dst + col0 + piece * 8) = w;
+  }
+  __syncwarp();
+}
+
+// ---- kEpiQkvRope: fused QKV epilogue (one thread = one output row = one position)
+// For every q / k head of the tile: v = acc + bias; with QK-norm, the head's
+// RMSNorm over D (sum of squares from a first pass over TMEM; the normalised value
+// times the weight is rounded to bf16 as HF's Qwen3 RMSNorm returns bf16, for bf16
+// outputs); then rotate-half RoPE with the bf16 cos / sin tables of this row's position:
+//   out[d] = v[d] cos[d] - v[d + D/2] sin[d],  out[d + D/2] = v[d + D/2] cos[d + D/2] + v[d] sin[d + D/2]
+// (same math as qk_norm_rope_kernel, without rounding q / k before it).
+// v heads only get the bias.  Needs BN % D == 0 (heads never straddle tiles).  The
+// tile's heads are shared between the NG column groups of epilogue warps: group grp
+// takes heads grp, grp + NG, ...
+template <int BN, bool F16, typename RowPtr>
+__device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, uint8_t *stage2, RowPtr out_row,
+                                             const EpiArgs &ea, int row, bool row_ok, int nb,
+                                             int grp, int NG) {
   const int D = ea.D, half = D / 2, nch = D / 32;
 #pragma unroll 1
-  for (int h0 = 0; h0 < BN; h0 += D) {
+  for (int h0 = grp * D; h0 < BN; h0 += NG * D) {
     const int hcol = nb * BN + h0;  // first column of this head
     if (hcol >= ea.n_out) break;    // warp-uniform
     if (hcol >= ea.rope_cols) {
@@ -423,10 +500,9 @@ __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPt
         if (ea.vt && row_ok) {
           __half *dst = ea.vt + static_cast<long>(hcol - ea.rope_cols + c * 32) * ea.ldvt + row;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) dst[static_cast<long>(j) * ea.ldvt] = __float2half_rn(bf16_round(v[j]));
+          for (int j = 0; j < 32; ++j) dst[static_cast<long>(j) * ea.ldvt] = __float2half_rn(round2<F16>(v[j]));
         }
-        epi_stage_put(stage, v);
-        epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + c * 32, ea.n_out - hcol - c * 32);
+        epi2_store<F16>(stage2, v, nullptr, out_row, hcol + c * 32, ea.n_out - hcol - c * 32);
       }
       continue;
     }
@@ -466,32 +542,43 @@ __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, float *stage, RowPt
         for (int e = 0; e < 8; ++e) {
           float a = lo[q * 8 + e], b = hi[q * 8 + e];
           if (nw) {
-            a = bf16_round(a * rn * wl[e]);
-            b = bf16_round(b * rn * wh[e]);
+            // bf16 outputs keep HF Qwen3's bf16 rounding of the normed head; fp16 ones
+            // round once, at the store
+            a = a * rn * wl[e];
+            b = b * rn * wh[e];
+            if constexpr (!F16) {
+              a = bf16_round(a);
+              b = bf16_round(b);
+            }
           }
           lo[q * 8 + e] = a * cl[e] - b * sl[e];
           hi[q * 8 + e] = b * ch[e] + a * sh[e];
         }
       }
-      epi_stage_put(stage, lo);
-      epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + dlo, 32);
-      epi_stage_put(stage, hi);
-      epi_stage_store_bf16(stage, bf16_row, nullptr, hcol + dhi, 32);
+      epi2_store<F16>(stage2, lo, nullptr, out_row, hcol + dlo, 32);
+      epi2_store<F16>(stage2, hi, nullptr, out_row, hcol + dhi, 32);
     }
   }
 }
 
-// ---- warps 2..5: epilogue for kEpiStore / kEpiSiluMul / kEpiStoreF32 / kEpiQkvRope /
-// kEpiStoreF16
-template <int BN, int MODE>
-__device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const TileSched &ts,
+// ---- warps 2..9: the plain GEMM's epilogue (kEpiStore / kEpiSiluMul / kEpiStoreF32 /
+// kEpiQkvRope).  Warp w reads TMEM lane quadrant w % 4 (rows); the two warps of a
+// quadrant split the tile's 32-column chunks (or heads) between them: group
+// (w - 2) / 4 takes chunks grp, grp + 2, ...  F16: fp16 operands and 2-byte outputs in
+// fp16 instead of bf16.
+template <int BN, int V, int MODE, bool F16 = false>
+__device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, const TileSched &ts,
                                               int M, const EpiArgs &ea, uint32_t *status) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, V>;
+  static_assert(C::kEpiWarps == 8, "plain GEMM epilogue: 8 warps");
+  constexpr int NG = C::kEpiWarps / 4;  // column groups
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quad = warp & 3;
+  const int grp = (warp - 2) / 4;
   const uint32_t tmem = *s.tmem_slot;
-  float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
+  uint8_t *stage_raw = reinterpret_cast<uint8_t *>(s.epi) + (warp - 2) * C::kWarpEpiBytes;
+  float *stage = reinterpret_cast<float *>(stage_raw);
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
     int mb, nb;
@@ -506,16 +593,17 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
     tc_fence_after();
     const int row0 = mb * kBM + quad * 32;
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + acc * C::kAccStride;
-    auto bf16_row = [&](int r) -> __nv_bfloat16 * {
+    auto out_row = [&](int r) -> __nv_bfloat16 * {
       return (row0 + r < M) ? ea.c + static_cast<long>(row0 + r) * ea.ldc : nullptr;
     };
     if constexpr (MODE == kEpiQkvRope) {
+      static_assert(V == kCfgPlain, "2-byte staging");
       // rows past M are not stored; clamp their table position
       const int erow = mb * kBM + quad * 32 + lane;
-      epi_qkv_rope<BN>(tbase, stage, bf16_row, ea, min(erow, M - 1), erow < M, nb);
-    } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32 || MODE == kEpiStoreF16) {
+      epi_qkv_rope<BN, F16>(tbase, stage_raw, out_row, ea, min(erow, M - 1), erow < M, nb, grp, NG);
+    } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = grp; c < BN / 32; c += NG) {
         const int col0 = nb * BN + c * 32;
         if (col0 >= ea.n_out) break;  // warp-uniform
         uint32_t r[32];
@@ -524,19 +612,21 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        epi_stage_put(stage, v);
-        if constexpr (MODE == kEpiStore)
-          epi_stage_store_bf16(stage, bf16_row, ea.bias, col0, ea.n_out - col0);
-        else if constexpr (MODE == kEpiStoreF16)
-          epi_stage_store_bf16<true>(stage, bf16_row, nullptr, col0, ea.n_out - col0);
-        else
+        if constexpr (MODE == kEpiStore) {
+          static_assert(V == kCfgPlain, "2-byte staging");
+          epi2_store<F16>(stage_raw, v, ea.bias, out_row, col0, ea.n_out - col0);
+        } else {
+          static_assert(V == kCfgPlainF32, "fp32 staging");
+          epi_stage_put(stage, v);
           epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, ea.n_out - col0);
+        }
       }
     } else {
+      static_assert(V == kCfgPlain, "2-byte staging");
       constexpr int HALF = BN / 2;
       static_assert(HALF % 32 == 0, "silu epilogue needs BN/2 % 32 == 0");
 #pragma unroll 1
-      for (int c = 0; c < HALF / 32; ++c) {
+      for (int c = grp; c < HALF / 32; c += NG) {
         const int col0 = nb * HALF + c * 32;
         if (col0 >= ea.n_out) break;
         uint32_t g[32], u[32];
@@ -547,8 +637,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN> &s, const T
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-        epi_stage_put(stage, v);
-        epi_stage_store_bf16(stage, bf16_row, nullptr, col0, ea.n_out - col0);
+        epi2_store<F16>(stage_raw, v, nullptr, out_row, col0, ea.n_out - col0);
       }
     }
     tc_fence_before();

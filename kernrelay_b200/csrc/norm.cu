@@ -1,8 +1,12 @@
 // Memory-bound kernels of the prefill: embedding gather, RMSNorm, Add+RMSNorm,
 // per-head QK-RMSNorm + rotate-half RoPE, and a tiled transpose used at load time.
 //
-// All of them read/write bf16 with 16-byte vector accesses where the layout
-// allows, reduce in fp32 with warp shuffles and round once on output.
+// Activations are bf16 (the stand-alone op entry points) or fp16 (the engine), read and
+// written with 16-byte vector accesses where the layout allows; reductions run in fp32
+// with warp shuffles and round once on output.  Weights (gamma, norm weights, rope
+// tables) stay bf16.
+#include <algorithm>
+
 #include "common.h"
 #include "ptx.cuh"
 
@@ -101,6 +105,28 @@ __device__ __forceinline__ uint4 pack8(const float *f) {
   return w;
 }
 
+// 8 activations in either 2-byte format
+template <bool F16>
+__device__ __forceinline__ void unpack8a(const uint4 &w, float *f) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float2 t = unpack2<F16>(ws[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+template <bool F16>
+__device__ __forceinline__ uint4 pack8a(const float *f) {
+  uint4 w;
+  w.x = pack2<F16>(f[0], f[1]);
+  w.y = pack2<F16>(f[2], f[3]);
+  w.z = pack2<F16>(f[4], f[5]);
+  w.w = pack2<F16>(f[6], f[7]);
+  return w;
+}
+
 // 8 elements of a residual row as fp32 (from fp32 or bf16 storage)
 __device__ __forceinline__ void load8(const float *p, long v, float *f) {
   const float4 *q = reinterpret_cast<const float4 *>(p) + v * 2;
@@ -110,6 +136,9 @@ __device__ __forceinline__ void load8(const float *p, long v, float *f) {
 }
 __device__ __forceinline__ void load8(const __nv_bfloat16 *p, long v, float *f) {
   unpack8(__ldg(reinterpret_cast<const uint4 *>(p) + v), f);
+}
+__device__ __forceinline__ void load8(const __half *p, long v, float *f) {
+  unpack8a<true>(__ldg(reinterpret_cast<const uint4 *>(p) + v), f);
 }
 __device__ __forceinline__ void store8(float *p, long v, const float *f) {
   float4 *q = reinterpret_cast<float4 *>(p) + v * 2;
@@ -121,12 +150,12 @@ __device__ __forceinline__ void store8(float *p, long v, const float *f) {
 // 8-element vectors, so all of a row's loads are in flight at once (HBM-bound).
 //   s = a (+ b)            a: residual (fp32 or bf16), b: bf16/fp32 delta or null
 //   sum_f <- s (fp32, unrounded)   or   sum_b <- bf16(s) and the norm uses bf16(s)
-//   y = s * rsqrt(mean(s^2) + eps) * gamma  (bf16)
+//   y = s * rsqrt(mean(s^2) + eps) * gamma  (2-byte TY: bf16 or fp16)
 // With a bf16 sum the norm is taken over the rounded value, as the stored
 // bf16 residual is what later layers see (aclnnAddRmsNorm semantics).
 constexpr int kNormVec = 4;
 
-template <typename TA, typename TB>
+template <typename TA, typename TB, typename TY>
 __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restrict__ b,
                                    const uint4 *__restrict__ gamma, uint4 *__restrict__ y,
                                    float *__restrict__ rstd, float *__restrict__ sum_f,
@@ -181,14 +210,14 @@ __global__ void add_rmsnorm_kernel(const TA *__restrict__ a, const TB *__restric
       unpack8(__ldg(gamma + v), g);
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[i][e] = x[i][e] * r * g[e];
-      y[base + v] = pack8(x[i]);
+      y[base + v] = pack8a<ActFmt<TY>::f16>(x[i]);
     }
   }
 }
 
-template <typename TA, typename TB>
+template <typename TA, typename TB, typename TY = __nv_bfloat16>
 static void launch_add_rmsnorm(const TA *a, const TB *b, const __nv_bfloat16 *gamma,
-                               __nv_bfloat16 *y, float *rstd, float *sum_f, __nv_bfloat16 *sum_b,
+                               TY *y, float *rstd, float *sum_f, __nv_bfloat16 *sum_b,
                                int rows, int H, float eps, cudaStream_t stream) {
   if (H % 8) throw CudaError("rmsnorm: H % 8 != 0");
   if (rows <= 0) throw CudaError("rmsnorm: no rows");
@@ -199,8 +228,8 @@ static void launch_add_rmsnorm(const TA *a, const TB *b, const __nv_bfloat16 *ga
   auto *y4 = reinterpret_cast<uint4 *>(y);
   auto *s4 = reinterpret_cast<uint4 *>(sum_b);
   const float inv_h = 1.0f / float(H);
-  add_rmsnorm_kernel<TA, TB><<<rows, warps * 32, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4, hv,
-                                                              inv_h, eps);
+  add_rmsnorm_kernel<TA, TB, TY><<<rows, warps * 32, 0, stream>>>(a, b, g4, y4, rstd, sum_f, s4,
+                                                                  hv, inv_h, eps);
   KRB_CUDA(cudaGetLastError());
 }
 
@@ -217,27 +246,43 @@ void add_rmsnorm_bf16(const __nv_bfloat16 *a, const __nv_bfloat16 *b, const __nv
                                                    eps, stream);
 }
 
-void add_rmsnorm_res_f32(const float *res, const __nv_bfloat16 *delta, const __nv_bfloat16 *gamma,
-                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
-                         cudaStream_t stream) {
-  launch_add_rmsnorm<float, __nv_bfloat16>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H,
-                                           eps, stream);
+template <typename T>
+void rmsnorm_act(const T *x, const __nv_bfloat16 *gamma, T *y, int rows, int H, float eps,
+                 cudaStream_t stream) {
+  launch_add_rmsnorm<T, T, T>(x, static_cast<const T *>(nullptr), gamma, y, nullptr, nullptr,
+                              nullptr, rows, H, eps, stream);
 }
+template void rmsnorm_act<__half>(const __half *, const __nv_bfloat16 *, __half *, int, int, float,
+                                  cudaStream_t);
 
-void add_rmsnorm_res_f32(const float *res, const float *delta, const __nv_bfloat16 *gamma,
-                         __nv_bfloat16 *y, float *sum, int rows, int H, float eps,
-                         cudaStream_t stream) {
-  launch_add_rmsnorm<float, float>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H, eps,
-                                   stream);
+template <typename TD, typename TY>
+void add_rmsnorm_res_f32(const float *res, const TD *delta, const __nv_bfloat16 *gamma, TY *y,
+                         float *sum, int rows, int H, float eps, cudaStream_t stream) {
+  launch_add_rmsnorm<float, TD, TY>(res, delta, gamma, y, nullptr, sum, nullptr, rows, H, eps,
+                                    stream);
 }
+template void add_rmsnorm_res_f32<__nv_bfloat16, __nv_bfloat16>(const float *,
+                                                                const __nv_bfloat16 *,
+                                                                const __nv_bfloat16 *,
+                                                                __nv_bfloat16 *, float *, int, int,
+                                                                float, cudaStream_t);
+template void add_rmsnorm_res_f32<float, __nv_bfloat16>(const float *, const float *,
+                                                        const __nv_bfloat16 *, __nv_bfloat16 *,
+                                                        float *, int, int, float, cudaStream_t);
+template void add_rmsnorm_res_f32<__half, __half>(const float *, const __half *,
+                                                  const __nv_bfloat16 *, __half *, float *, int,
+                                                  int, float, cudaStream_t);
+template void add_rmsnorm_res_f32<float, __half>(const float *, const float *,
+                                                 const __nv_bfloat16 *, __half *, float *, int,
+                                                 int, float, cudaStream_t);
 
 // ------------------------------------------------------------------ QK-norm + RoPE
 // One warp per (position, head) for the HQ query heads and HKV key heads of the
 // fused qkv row.  Optional per-head RMSNorm over D (Qwen3 q_norm/k_norm, applied
 // before RoPE as in HF Qwen3Attention), then rotate-half RoPE with the bf16
 // cos/sin tables of the model directory (export_model.py:70-77 layout [max_pos, D]).
-template <int D>
-__global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int HQ, int HKV,
+template <int D, bool F16>
+__global__ void qk_norm_rope_kernel(uint16_t *__restrict__ qkv, int S, int HQ, int HKV,
                                     const __nv_bfloat16 *__restrict__ cos_tab,
                                     const __nv_bfloat16 *__restrict__ sin_tab,
                                     const __nv_bfloat16 *__restrict__ q_norm,
@@ -254,11 +299,11 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int 
   if (head >= static_cast<long>(S) * nh) return;  // whole heads only: warp-uniform per head
   const int s = static_cast<int>(head / nh);
   const int h = static_cast<int>(head - static_cast<long>(s) * nh);
-  __nv_bfloat16 *p = qkv + (static_cast<long>(s) * (HQ + 2 * HKV) + h) * D;
+  uint16_t *p = qkv + (static_cast<long>(s) * (HQ + 2 * HKV) + h) * D;
   const __nv_bfloat16 *nw = (h < HQ) ? q_norm : k_norm;
   float lo[8], hi[8];
-  unpack8(*reinterpret_cast<const uint4 *>(p + j), lo);
-  unpack8(*reinterpret_cast<const uint4 *>(p + HALF + j), hi);
+  unpack8a<F16>(*reinterpret_cast<const uint4 *>(p + j), lo);
+  unpack8a<F16>(*reinterpret_cast<const uint4 *>(p + HALF + j), hi);
   const long trow = static_cast<long>(s) * D;
   float c0[8], s0[8], c1[8], s1[8];
   unpack8(__ldg(reinterpret_cast<const uint4 *>(cos_tab + trow + j)), c0);
@@ -280,9 +325,14 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int 
     unpack8(__ldg(reinterpret_cast<const uint4 *>(nw + HALF + j)), wh);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      // HF RMSNorm returns bf16 before RoPE: keep that rounding point
-      lo[e] = bf16_round(lo[e] * r * wl[e]);
-      hi[e] = bf16_round(hi[e] * r * wh[e]);
+      // bf16 data: HF RMSNorm returns bf16 before RoPE, keep that rounding point;
+      // fp16 data rounds once, at the store
+      lo[e] = lo[e] * r * wl[e];
+      hi[e] = hi[e] * r * wh[e];
+      if constexpr (!F16) {
+        lo[e] = bf16_round(lo[e]);
+        hi[e] = bf16_round(hi[e]);
+      }
     }
   }
   float olo[8], ohi[8];
@@ -291,25 +341,27 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16 *__restrict__ qkv, int S, int 
     olo[e] = lo[e] * c0[e] - hi[e] * s0[e];
     ohi[e] = hi[e] * c1[e] + lo[e] * s1[e];
   }
-  *reinterpret_cast<uint4 *>(p + j) = pack8(olo);
-  *reinterpret_cast<uint4 *>(p + HALF + j) = pack8(ohi);
+  *reinterpret_cast<uint4 *>(p + j) = pack8a<F16>(olo);
+  *reinterpret_cast<uint4 *>(p + HALF + j) = pack8a<F16>(ohi);
 }
 
-void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
-                       const __nv_bfloat16 *cos_tab, const __nv_bfloat16 *sin_tab,
-                       const __nv_bfloat16 *q_norm, const __nv_bfloat16 *k_norm, float eps,
-                       cudaStream_t stream) {
+template <typename T>
+void qk_norm_rope(T *qkv_t, int S, int HQ, int HKV, int D, const __nv_bfloat16 *cos_tab,
+                  const __nv_bfloat16 *sin_tab, const __nv_bfloat16 *q_norm,
+                  const __nv_bfloat16 *k_norm, float eps, cudaStream_t stream) {
+  constexpr bool F16 = ActFmt<T>::f16;
+  uint16_t *qkv = reinterpret_cast<uint16_t *>(qkv_t);
   const long threads_total = static_cast<long>(S) * (HQ + HKV) * (D / 16);
   const int threads = 256;
   const long blocks = (threads_total + threads - 1) / threads;
   switch (D) {
     case 64:
-      qk_norm_rope_kernel<64><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab, sin_tab,
-                                                              q_norm, k_norm, eps);
+      qk_norm_rope_kernel<64, F16><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab,
+                                                                   sin_tab, q_norm, k_norm, eps);
       break;
     case 128:
-      qk_norm_rope_kernel<128><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab, sin_tab,
-                                                               q_norm, k_norm, eps);
+      qk_norm_rope_kernel<128, F16><<<blocks, threads, 0, stream>>>(qkv, S, HQ, HKV, cos_tab,
+                                                                    sin_tab, q_norm, k_norm, eps);
       break;
     default:
       throw CudaError("qk_norm_rope: head_dim must be 64 or 128");
@@ -317,17 +369,27 @@ void qk_norm_rope_bf16(__nv_bfloat16 *qkv, int S, int HQ, int HKV, int D,
   KRB_CUDA(cudaGetLastError());
 }
 
+template void qk_norm_rope<__nv_bfloat16>(__nv_bfloat16 *, int, int, int, int,
+                                          const __nv_bfloat16 *, const __nv_bfloat16 *,
+                                          const __nv_bfloat16 *, const __nv_bfloat16 *, float,
+                                          cudaStream_t);
+template void qk_norm_rope<__half>(__half *, int, int, int, int, const __nv_bfloat16 *,
+                                   const __nv_bfloat16 *, const __nv_bfloat16 *,
+                                   const __nv_bfloat16 *, float, cudaStream_t);
+
 // ------------------------------------------------------------------ transpose
 __device__ __forceinline__ void store_as(__nv_bfloat16 *p, __nv_bfloat16 v) { *p = v; }
 __device__ __forceinline__ void store_as(__half *p, __nv_bfloat16 v) {
   *p = __float2half_rn(__bfloat162float(v));
 }
+__device__ __forceinline__ void store_as(__half *p, __half v) { *p = v; }
 
-// 32 x 32 tiles through padded shared memory; TD = bf16 (copy) or fp16 (converted)
-template <typename TD>
-__global__ void transpose_kernel(const __nv_bfloat16 *__restrict__ src, long ld_src,
+// 32 x 32 tiles through padded shared memory; TS -> TD: bf16 -> bf16 (copy), bf16 -> fp16
+// (converted), fp16 -> fp16 (copy)
+template <typename TS, typename TD>
+__global__ void transpose_kernel(const TS *__restrict__ src, long ld_src,
                                  TD *__restrict__ dst, long ld_dst, int rows, int cols) {
-  __shared__ __nv_bfloat16 tile[32][33];
+  __shared__ TS tile[32][33];
   const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = r0 + i, c = c0 + threadIdx.x;
@@ -344,7 +406,8 @@ void transpose_bf16(const __nv_bfloat16 *src, long ld_src, __nv_bfloat16 *dst, l
                     int rows, int cols, cudaStream_t stream) {
   dim3 block(32, 8);
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-  transpose_kernel<__nv_bfloat16><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  transpose_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, stream>>>(src, ld_src, dst,
+                                                                             ld_dst, rows, cols);
   KRB_CUDA(cudaGetLastError());
 }
 
@@ -352,7 +415,61 @@ void transpose_bf16_to_f16(const __nv_bfloat16 *src, long ld_src, __half *dst, l
                            int rows, int cols, cudaStream_t stream) {
   dim3 block(32, 8);
   dim3 grid((cols + 31) / 32, (rows + 31) / 32);
-  transpose_kernel<__half><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+  transpose_kernel<__nv_bfloat16, __half><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst,
+                                                                      rows, cols);
+  KRB_CUDA(cudaGetLastError());
+}
+
+void transpose_f16(const __half *src, long ld_src, __half *dst, long ld_dst, int rows, int cols,
+                   cudaStream_t stream) {
+  dim3 block(32, 8);
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose_kernel<__half, __half><<<grid, block, 0, stream>>>(src, ld_src, dst, ld_dst, rows,
+                                                               cols);
+  KRB_CUDA(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ format conversions
+__global__ void bf16_to_f16_kernel(uint4 *__restrict__ data, size_t nvec) {
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec;
+       i += size_t(gridDim.x) * blockDim.x) {
+    float f[8];
+    unpack8(data[i], f);
+    data[i] = pack8a<true>(f);
+  }
+}
+
+__global__ void bf16_to_f16_tail_kernel(uint16_t *__restrict__ data, size_t from, size_t n) {
+  const size_t i = from + size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float f = __bfloat162float(*reinterpret_cast<const __nv_bfloat16 *>(data + i));
+    const __half h = __float2half_rn(f);
+    data[i] = *reinterpret_cast<const uint16_t *>(&h);
+  }
+}
+
+void bf16_to_f16_inplace(void *data, size_t n, cudaStream_t stream) {
+  if (reinterpret_cast<uintptr_t>(data) % 16) throw CudaError("bf16_to_f16: unaligned buffer");
+  const size_t nvec = n / 8;
+  if (nvec) {
+    const size_t blocks = std::min<size_t>((nvec + 255) / 256, 148 * 16);
+    bf16_to_f16_kernel<<<unsigned(blocks), 256, 0, stream>>>(static_cast<uint4 *>(data), nvec);
+    KRB_CUDA(cudaGetLastError());
+  }
+  if (n % 8) {
+    bf16_to_f16_tail_kernel<<<1, 8, 0, stream>>>(static_cast<uint16_t *>(data), nvec * 8, n);
+    KRB_CUDA(cudaGetLastError());
+  }
+}
+
+__global__ void f16_to_f32_kernel(const __half *__restrict__ src, float *__restrict__ dst, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    dst[i] = __half2float(src[i]);
+}
+
+void f16_to_f32(const __half *src, float *dst, int n, cudaStream_t stream) {
+  const int blocks = std::min((n + 255) / 256, 1024);
+  f16_to_f32_kernel<<<blocks > 0 ? blocks : 1, 256, 0, stream>>>(src, dst, n);
   KRB_CUDA(cudaGetLastError());
 }
 

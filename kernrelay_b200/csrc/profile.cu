@@ -37,12 +37,11 @@ std::string Engine::profile_many(const std::string &spec_path) {
     const int per = S / k;
     std::function<void(int)> call;  // enqueue slice i
     std::string shape, fused;
-    auto mm = [&](const __nv_bfloat16 *A, int lda, const __nv_bfloat16 *B, __nv_bfloat16 *C, int ldc,
-                  int N, int K) {
+    auto mm = [&](const __half *A, int lda, const __half *B, __half *C, int ldc, int N, int K) {
       shape = "matmul|" + std::to_string(S) + "x" + std::to_string(K) + "x" + std::to_string(N);
       call = [=](int i) {
-        gemm_bf16(A + size_t(i) * per * lda, lda, B, K, C + size_t(i) * per * ldc, ldc, nullptr, per,
-                  N, K, 0, 0, status_, stream_);
+        gemm_store<__half>(A + size_t(i) * per * lda, lda, B, K, C + size_t(i) * per * ldc, ldc,
+                           nullptr, per, N, K, 0, 0, status_, stream_);
       };
     };
     if (op == "matmul_q") {
@@ -62,8 +61,8 @@ std::string Engine::profile_many(const std::string &spec_path) {
       shape = "matmul_silu|" + std::to_string(S) + "x" + std::to_string(H) + "x" +
               std::to_string(2 * Iloc_);
       call = [=](int i) {
-        gemm_silu_bf16(x_ + size_t(i) * per * H, H, w.wgu, H, act_ + size_t(i) * per * Iloc_, Iloc_,
-                       per, Iloc_, H, bn_gu_, 0, status_, stream_);
+        gemm_silu<__half>(x_ + size_t(i) * per * H, H, w.wgu, H, act_ + size_t(i) * per * Iloc_,
+                          Iloc_, per, Iloc_, H, bn_gu_, 0, status_, stream_);
       };
     } else if (op == "matmul_up" || op == "silu" || op == "mul") {
       fused = "matmul_gate";
@@ -72,8 +71,8 @@ std::string Engine::profile_many(const std::string &spec_path) {
     } else if (op == "rmsnorm") {
       shape = "rmsnorm|" + std::to_string(S) + "x" + std::to_string(H);
       call = [=](int i) {
-        rmsnorm_bf16(x_ + size_t(i) * per * H, w.ln1, o_ + size_t(i) * per * H, nullptr, per, H, eps,
-                     stream_);
+        rmsnorm_act<__half>(x_ + size_t(i) * per * H, w.ln1, o_ + size_t(i) * per * H, per, H, eps,
+                            stream_);
       };
     } else if (op == "add_rmsnorm") {
       shape = "add_rmsnorm|" + std::to_string(S) + "x" + std::to_string(H);
@@ -84,9 +83,9 @@ std::string Engine::profile_many(const std::string &spec_path) {
     } else if (op == "rope") {
       shape = "rope|" + std::to_string(S) + "x" + std::to_string(nq + nkv);
       call = [=](int i) {
-        qk_norm_rope_bf16(qkv_ + size_t(i) * per * nqkv_, per, c.HQ, c.HKV, D, cos_ + size_t(i) * per * D,
-                          sin_ + size_t(i) * per * D, c.qk_norm ? w.qn : nullptr,
-                          c.qk_norm ? w.kn : nullptr, eps, stream_);
+        qk_norm_rope<__half>(qkv_ + size_t(i) * per * nqkv_, per, c.HQ, c.HKV, D,
+                             cos_ + size_t(i) * per * D, sin_ + size_t(i) * per * D,
+                             c.qk_norm ? w.qn : nullptr, c.qk_norm ? w.kn : nullptr, eps, stream_);
       };
     } else if (op == "embedding") {
       shape = "embedding|" + std::to_string(S) + "x" + std::to_string(H);
@@ -106,10 +105,10 @@ std::string Engine::profile_many(const std::string &spec_path) {
       call = [=](int g) {
         const int kv_off = kv_div ? g * hkv : g % c.HKV;
         const int group = std::max(1, hq / hkv);
-        attention_vt(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_, kv_off, hkv);
-        attention_tc_bf16(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D,
-                          float(1.0 / std::sqrt(double(D))), status_, stream_, g * hq, hq, kv_off,
-                          group);
+        attention_vt<__half>(qkv_, vt_, ldvt_, S, c.HQ, c.HKV, D, stream_, kv_off, hkv);
+        attention_tc<__half>(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D,
+                             float(1.0 / std::sqrt(double(D))), status_, stream_, g * hq, hq,
+                             kv_off, group);
       };
     } else {
       continue;

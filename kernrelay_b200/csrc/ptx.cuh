@@ -324,4 +324,44 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+__device__ __forceinline__ float2 unpack_f16x2(uint32_t u) {
+  __half2 v = *reinterpret_cast<__half2 *>(&u);
+  return __half22float2(v);
+}
+
+// ---------------------------------------------------------------- 2-byte activations
+// Kernels that move activations are instantiated for both 2-byte formats: bf16 (the
+// stand-alone op entry points) and fp16 (the engine, whose GEMM inputs, q / k / v,
+// attention output and reduction partials are fp16: 8x finer rounding than bf16 at
+// the same tensor-core rate; weights stored as bf16 convert to fp16 exactly).
+template <typename T>
+struct ActFmt;
+template <>
+struct ActFmt<__nv_bfloat16> {
+  static constexpr bool f16 = false;
+};
+template <>
+struct ActFmt<__half> {
+  static constexpr bool f16 = true;
+};
+
+template <bool F16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (F16) return pack_f16x2(lo, hi);
+  else return pack_bf16x2(lo, hi);
+}
+
+template <bool F16>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  if constexpr (F16) return unpack_f16x2(u);
+  else return unpack_bf16x2(u);
+}
+
+// value as the 2-byte format stores it
+template <bool F16>
+__device__ __forceinline__ float round2(float x) {
+  if constexpr (F16) return __half2float(__float2half_rn(x));
+  else return bf16_round(x);
+}
+
 }  // namespace krb

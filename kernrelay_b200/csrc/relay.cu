@@ -77,7 +77,19 @@ __device__ __forceinline__ void acc8_cg(float *acc, const __nv_bfloat16 *p) {
   }
 }
 
-// fp32 accumulate of 8 bf16 held in a 16-byte register vector
+// fp32 accumulate of 8 activations (bf16 or fp16) held in a 16-byte register vector
+template <bool F16>
+__device__ __forceinline__ void acc8_act(float *acc, const uint4 &w) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = unpack2<F16>(ws[e]);
+    acc[2 * e] += f.x;
+    acc[2 * e + 1] += f.y;
+  }
+}
+
+// fp32 accumulate of 8 bf16 held in a 16-byte register vector (weights: gamma)
 __device__ __forceinline__ void acc8_bits(float *acc, const uint4 &w) {
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -88,12 +100,13 @@ __device__ __forceinline__ void acc8_bits(float *acc, const uint4 &w) {
   }
 }
 
+template <bool F16>
 __device__ __forceinline__ uint4 pack8f(const float *f) {
   uint4 w;
-  w.x = pack_bf16x2(f[0], f[1]);
-  w.y = pack_bf16x2(f[2], f[3]);
-  w.z = pack_bf16x2(f[4], f[5]);
-  w.w = pack_bf16x2(f[6], f[7]);
+  w.x = pack2<F16>(f[0], f[1]);
+  w.y = pack2<F16>(f[2], f[3]);
+  w.z = pack2<F16>(f[4], f[5]);
+  w.w = pack2<F16>(f[6], f[7]);
   return w;
 }
 
@@ -102,7 +115,7 @@ __device__ __forceinline__ uint4 pack8f(const float *f) {
 // epilogue can index them by owner rank without a local-memory copy.
 __shared__ uint8_t *g_peer_base[kMaxRanks];
 
-template <int BN>
+template <int BN, bool F16>
 __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s,
                                                     const TileSched &ts, const RelayArgs &ra) {
   using C = GemmCfg<BN, 1>;
@@ -150,7 +163,7 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
         // and the relay warps add the residual in place
         epi_stage_store_f32(stage, ra.sum_out, ra.H, row0, ra.S, col0, ra.H - col0);
       else
-        epi_stage_store_bf16(stage, part_row, nullptr, col0, ra.H - col0);
+        epi_stage_store_bf16<F16>(stage, part_row, nullptr, col0, ra.H - col0);
     }
     tc_fence_before();
     mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
@@ -243,7 +256,7 @@ constexpr int kHalfVec = 8;  // 16-byte vectors per lane per half row: H <= 2*8*
 //   kSrc = 0: delta is one fp32 row; kSrc = 1: delta is one bf16 row;
 //   kSrc >= 2: delta is the sum of the kSrc ranks' bf16 partial rows, rank s's at
 //   g_peer_base[s] + part_off, element offset part_elem (pulled over NVLink)
-template <int kSrc>
+template <int kSrc, bool F16>
 __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void *delta,
                                                  size_t part_off, size_t part_elem, float *sum_out,
                                                  const __nv_bfloat16 *gamma, __nv_bfloat16 *x_out,
@@ -269,14 +282,14 @@ __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void 
         h[i][0] += d0.x; h[i][1] += d0.y; h[i][2] += d0.z; h[i][3] += d0.w;
         h[i][4] += d1.x; h[i][5] += d1.y; h[i][6] += d1.z; h[i][7] += d1.w;
       } else if constexpr (kSrc == 1) {
-        acc8_bits(h[i], __ldcg(reinterpret_cast<const uint4 *>(delta) + v));
+        acc8_act<F16>(h[i], __ldcg(reinterpret_cast<const uint4 *>(delta) + v));
       } else {
         // the partials are summed in fp32 first (same association as the
         // reduce-scatter path), then added to the residual
         float d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int src = 0; src < kSrc; ++src)
-          acc8_bits(d, __ldcg(reinterpret_cast<const uint4 *>(
+          acc8_act<F16>(d, __ldcg(reinterpret_cast<const uint4 *>(
                               reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[src] + part_off) +
                               part_elem) + v));
 #pragma unroll
@@ -309,7 +322,7 @@ __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void 
       acc8_bits(g, __ldg(reinterpret_cast<const uint4 *>(gamma) + v));
 #pragma unroll
       for (int e = 0; e < 8; ++e) h[i][e] = h[i][e] * r * g[e];
-      reinterpret_cast<uint4 *>(x_out)[v] = pack8f(h[i]);
+      reinterpret_cast<uint4 *>(x_out)[v] = pack8f<F16>(h[i]);
     }
   }
 }
@@ -324,7 +337,7 @@ __device__ __forceinline__ void pair_addnorm_row(const float *resid, const void 
 //                       summed first, so every rank forms the same fp32 value)
 // Returns false if the copy did not complete within limit_ns (the row is then
 // left unwritten; the pair still meets at its barriers).
-template <bool kLocalPart>
+template <bool kLocalPart, bool F16>
 __device__ __forceinline__ bool pair_addnorm_row_staged(
     const float *resid, const __nv_bfloat16 *local_part, const uint4 *stage, uint64_t *bar,
     uint32_t phase, uint64_t limit_ns, float *sum_out, const __nv_bfloat16 *gamma,
@@ -354,8 +367,8 @@ __device__ __forceinline__ bool pair_addnorm_row_staged(
     const int v = vbeg + lane + 32 * i;
     if (v < vend) {
       float d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if constexpr (kLocalPart) acc8_bits(d, lp[i]);
-      if (ok) acc8_bits(d, stage[v]);
+      if constexpr (kLocalPart) acc8_act<F16>(d, lp[i]);
+      if (ok) acc8_act<F16>(d, stage[v]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         h[i][e] += d[e];
@@ -384,13 +397,13 @@ __device__ __forceinline__ bool pair_addnorm_row_staged(
       acc8_bits(g, __ldg(reinterpret_cast<const uint4 *>(gamma) + v));
 #pragma unroll
       for (int e = 0; e < 8; ++e) h[i][e] = h[i][e] * r * g[e];
-      reinterpret_cast<uint4 *>(x_out)[v] = pack8f(h[i]);
+      reinterpret_cast<uint4 *>(x_out)[v] = pack8f<F16>(h[i]);
     }
   }
   return pair_ok;
 }
 
-template <int KR>  // number of ranks (compile-time so the partial registers fit)
+template <int KR, bool F16>  // ranks (compile-time so the partial registers fit); fp16 data
 __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int *flag_smem,
                                                float *pair_ss, uint8_t *stage_base) {
   // reduce-scatter units in flight per warp: KR partial vectors each
@@ -447,7 +460,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
       }
       for (int q = gp; q < ra.R; q += GP) {
         const size_t g = size_t(t) * ra.R + q;
-        pair_addnorm_row<0>(ra.resid + g * ra.H, ra.sum_out + g * ra.H, 0, 0, ra.sum_out + g * ra.H,
+        pair_addnorm_row<0, F16>(ra.resid + g * ra.H, ra.sum_out + g * ra.H, 0, 0, ra.sum_out + g * ra.H,
                             ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair,
                             half, pair_ss);
       }
@@ -479,7 +492,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
             mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
             bulk_load(pbuf, theirs + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
           }
-          const bool rok = pair_addnorm_row_staged<true>(
+          const bool rok = pair_addnorm_row_staged<true, F16>(
               ra.resid + g * ra.H, mine + g * ra.H, reinterpret_cast<const uint4 *>(pbuf), pbar,
               phase, ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv,
               inv_h, ra.eps, ra.do_norm != 0, pair, half, pair_ss);
@@ -511,7 +524,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
         }
         for (int q = gp; q < ra.R; q += GP) {
           const size_t g = size_t(t) * ra.R + q;
-          pair_addnorm_row<KR>(ra.resid + g * ra.H, nullptr, ra.part_off, g * ra.H,
+          pair_addnorm_row<KR, F16>(ra.resid + g * ra.H, nullptr, ra.part_off, g * ra.H,
                                ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h,
                                ra.eps, ra.do_norm != 0, pair, half, pair_ss);
         }
@@ -555,8 +568,8 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
           for (int v = tid; v < wv; v += 64) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int src = 0; src < KR; ++src) acc8_bits(acc, sv[src * wv + v]);
-            reinterpret_cast<uint4 *>(red + g * ra.H + size_t(seg) * W)[v] = pack8f(acc);
+            for (int src = 0; src < KR; ++src) acc8_act<F16>(acc, sv[src * wv + v]);
+            reinterpret_cast<uint4 *>(red + g * ra.H + size_t(seg) * W)[v] = pack8f<F16>(acc);
           }
         }
         // pair-uniform outcome, and every thread is done reading the buffer
@@ -594,9 +607,9 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
           if (u < units && col < ra.H) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int src = 0; src < KR; ++src) acc8_bits(acc, part[b][src]);
+            for (int src = 0; src < KR; ++src) acc8_act<F16>(acc, part[b][src]);
             const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
-            *reinterpret_cast<uint4 *>(red + g * ra.H + col) = pack8f(acc);
+            *reinterpret_cast<uint4 *>(red + g * ra.H + col) = pack8f<F16>(acc);
           }
         }
       }
@@ -632,7 +645,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
           mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
           bulk_load(pbuf, g_peer_base[owner] + ra.red_off + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
         }
-        const bool rok = pair_addnorm_row_staged<false>(
+        const bool rok = pair_addnorm_row_staged<false, F16>(
             ra.resid + g * ra.H, nullptr, reinterpret_cast<const uint4 *>(pbuf), pbar, phase,
             ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps,
             ra.do_norm != 0, pair, half, pair_ss);
@@ -651,7 +664,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
       const int owner = q / ra.Rk;
       const __nv_bfloat16 *red_row =
           reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[owner] + ra.red_off) + g * ra.H;
-      pair_addnorm_row<1>(ra.resid + g * ra.H, red_row, 0, 0, ra.sum_out + g * ra.H, ra.gamma,
+      pair_addnorm_row<1, F16>(ra.resid + g * ra.H, red_row, 0, 0, ra.sum_out + g * ra.H, ra.gamma,
                           ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair, half,
                           pair_ss);
     }
@@ -742,7 +755,7 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra) {
   }
 }
 
-template <int BN, int KR>
+template <int BN, int KR, bool F16>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
                       const __grid_constant__ CUtensorMap tb, TileSched ts,
@@ -771,11 +784,12 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   if (warp == 0) {
     if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, ts, ra.K, ra.status);
   } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN, 1>(s, ts, ra.K, ra.status);
+    if (lane == 0) gemm_mma<BN, 1, F16>(s, ts, ra.K, ra.status);
   } else if (warp < kRelayWarp0) {
-    relay_push_epilogue<BN>(s, ts, ra);
+    relay_push_epilogue<BN, F16>(s, ts, ra);
   } else if (warp < kSignalWarp) {
-    relay_consumer<KR>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch, stage_base);
+    relay_consumer<KR, F16>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
+                            stage_base);
   } else if (lane == 0) {
     relay_signal(ra);
   }
@@ -805,11 +819,11 @@ static bool relay_bulk_fits(int H, int k, size_t dyn_limit) {
   return true;
 }
 
-template <int BN, int KR>
-static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, long ldb,
+template <int BN, int KR, bool F16>
+static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
                          TileSched ts, const RelayArgs &ra_in, bool want_bulk, int grid,
                          cudaStream_t stream) {
-  auto kern = relay_down_kernel<BN, KR>;
+  auto kern = relay_down_kernel<BN, KR, F16>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static size_t dyn_limit[64] = {0};
@@ -843,13 +857,17 @@ static void launch_relay(const CUtensorMap &tma, const __nv_bfloat16 *w_down, lo
   KRB_CUDA(cudaLaunchKernelEx(&cfg, kern, tma, tmb, ts, ra));
 }
 
-void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w_down, long ldb,
-                      int bn, const RelayArgs &ra, cudaStream_t stream) {
+template <typename T>
+void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
+                      const RelayArgs &ra, cudaStream_t stream) {
+  constexpr bool F16 = ActFmt<T>::f16;
   if (ra.S % kBM) throw CudaError("relay: seq must be a multiple of 128");
   if (ra.R % kBM) throw CudaError("relay: rows per tile must be a multiple of 128");
   if (ra.H % 8) throw CudaError("relay: hidden must be a multiple of 8");
   if (ra.H > 4096) throw CudaError("relay: hidden must be at most 4096");
   if (ra.k < 1 || ra.k > kMaxRanks || ra.R % ra.k) throw CudaError("relay: bad rank count");
+  // bf16 serves the one-device entry points; the exchange paths are built for fp16
+  if (!F16 && ra.k != 1) throw CudaError("relay: bf16 operands only with one rank");
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   TileSched ts;
@@ -869,13 +887,17 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
       const char *e = std::getenv("KRB_RELAY_BULK");
       return !(e && e[0] == '0');
     }();
-    const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
-    switch (ra.k) {
-      case 1: launch_relay<B, 1>(tma, w_down, ldb, ts, ra, false, grid, stream); break;
-      case 2: launch_relay<B, 2>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
-      case 4: launch_relay<B, 4>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
-      case 8: launch_relay<B, 8>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
-      default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
+    if constexpr (!F16) {
+      launch_relay<B, 1, false>(tma, w_down, ldb, ts, ra, false, grid, stream);
+    } else {
+      const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
+      switch (ra.k) {
+        case 1: launch_relay<B, 1, true>(tma, w_down, ldb, ts, ra, false, grid, stream); break;
+        case 2: launch_relay<B, 2, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+        case 4: launch_relay<B, 4, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+        case 8: launch_relay<B, 8, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+        default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
+      }
     }
   };
   switch (bn) {
@@ -885,6 +907,11 @@ void relay_down_layer(const __nv_bfloat16 *act, long lda, const __nv_bfloat16 *w
     default: throw CudaError("relay: unsupported bn");
   }
 }
+
+template void relay_down_layer<__nv_bfloat16>(const __nv_bfloat16 *, long, const __nv_bfloat16 *,
+                                              long, int, const RelayArgs &, cudaStream_t);
+template void relay_down_layer<__half>(const __half *, long, const __half *, long, int,
+                                       const RelayArgs &, cudaStream_t);
 
 // Expected counter increments for the relay (host helper): owner `rank`
 // receives one rs increment per (n block, 128-row block touching its slice)
