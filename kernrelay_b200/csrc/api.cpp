@@ -664,7 +664,7 @@ KRB_EXPORT int krb_relay_down_single(const void *act, const void *w_down, const 
     ra.rank = 0;
     ra.R = S / tiles;
     ra.Rk = ra.R;
-    krb::relay_expectations(S, H, tiles, 1, 0, dev_bn, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.nseg = (H + 255) / 256;
     ra.peer_base[0] = static_cast<uint8_t *>(scratch);
     ra.local_base = static_cast<uint8_t *>(scratch);
     ra.part_off = L.part_off;
@@ -726,7 +726,7 @@ KRB_EXPORT int krb_relay_down_single_noalloc(const void *act, const void *w_down
     ra.rank = 0;
     ra.R = S / tiles;
     ra.Rk = ra.R;
-    krb::relay_expectations(S, H, tiles, 1, 0, dev_bn, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
+    ra.nseg = (H + 255) / 256;
     ra.peer_base[0] = scratch;
     ra.local_base = scratch;
     ra.part_off = L.part_off;
@@ -788,8 +788,7 @@ KRB_EXPORT int krb_relay_timeout_probe(int S, int H, int K, int tiles, float tim
     ra.rank = 0;
     ra.R = S / tiles;
     ra.Rk = ra.R / k;
-    krb::relay_expectations(S, H, tiles, k, 0, 256, &ra.rs_expect, &ra.ag_expect, &ra.nseg);
-    ra.done_expect = krb::relay_done_expect(S, H, tiles, 256);
+    ra.nseg = (H + 255) / 256;
     ra.peer_base[0] = static_cast<uint8_t *>(mine);
     ra.peer_base[1] = static_cast<uint8_t *>(ghost);
     ra.local_base = static_cast<uint8_t *>(mine);
@@ -841,15 +840,34 @@ KRB_EXPORT int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, 
     if (tiles < 1 || S % tiles || (S / tiles) % 128 || k < 1 || (S / tiles) % k || rank < 0 ||
         rank >= k || (bn != 128 && bn != 224 && bn != 256))
       throw std::runtime_error("relay plan: unsupported shape");
-    uint32_t rs = 0, ag = 0;
-    int nseg = 0;
-    krb::relay_expectations(S, H, tiles, k, rank, bn, &rs, &ag, &nseg);
+    // the SM count of the current device, or B200's 148 where no GPU is visible
+    int grid = 148;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) == cudaSuccess && ndev > 0) {
+      int dev = 0;
+      KRB_CUDA(cudaGetDevice(&dev));
+      grid = krb::sm_count(dev);
+    } else {
+      cudaGetLastError();
+    }
+    const krb::TileSched ts = krb::relay_tile_sched(S, H, tiles, bn, grid);
     const int R = S / tiles, Rk = R / k;
     std::ostringstream os;
-    os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"num_n\":" << (H + bn - 1) / bn
-       << ",\"rs_expect\":" << rs << ",\"ag_expect\":" << ag << ",\"nseg\":" << nseg
-       << ",\"done_expect\":" << krb::relay_done_expect(S, H, tiles, bn)
-       << ",\"blocks\":[";
+    os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"grid\":" << grid << ",\"bn\":" << bn
+       << ",\"bn2\":" << ts.bn2 << ",\"p1\":" << ts.p1 << ",\"total\":" << ts.total()
+       << ",\"nseg\":" << (H + 255) / 256 << ",\"band_tiles\":[";
+    for (int t = 0; t < tiles; ++t) os << (t ? "," : "") << ts.band_tiles(t);
+    // the consumer's targets per run and layer: k = 1 every GEMM tile of row tile t; k > 1
+    // one forwarded signal per (row tile, source) and per (row tile, owner)
+    os << "],\"rs_expect\":[";
+    for (int t = 0; t < tiles; ++t) os << (t ? "," : "") << (k == 1 ? ts.band_tiles(t) : 1);
+    os << "],\"ag_expect\":" << (k == 1 ? 0 : 1) << ",\"tiles\":[";
+    for (int i = 0; i < ts.total(); ++i) {
+      int mb, n0, w;
+      ts.tile(i, mb, n0, w);
+      os << (i ? "," : "") << "[" << mb << "," << n0 << "," << w << "]";
+    }
+    os << "],\"blocks\":[";
     for (int b = 0; b < S / 128; ++b) {
       const krb::RowRoute f = krb::relay_route(b * 128, R, Rk);
       const krb::RowRoute l = krb::relay_route(b * 128 + 127, R, Rk);

@@ -146,39 +146,100 @@ __device__ __forceinline__ Attn2Smem carve2(uint8_t *raw, uint32_t tile_bytes) {
   return a;
 }
 
-// One key block of the two-tile kernel's softmax for one row (thread): row max
-// (pass 1), lazy O rescale, P = 2^(s*scale - m) rounded to bf16 written over S's
-// first 64 columns as fp16 pairs (pass 2; chunk c's P lands on columns already read), and the
-// running max / sum update.  The chunk loops stay rolled (code size).
+__device__ __forceinline__ void tmem_ld_32x32_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// One key block of the two-tile kernel's softmax for one row (thread), in ONE pass over
+// the 128 scores: chunk c (32 scores) is processed while chunk c + 1's TMEM load is in
+// flight.  P = 2^(s*scale - m) with the row's current offset m, rounded to fp16 and
+// written over S's first 64 columns as fp16 pairs (chunk c's P lands on columns already
+// read).  The offset moves only when a chunk's max exceeds it by more than 2^8 (then
+// the P chunks this row already wrote are rescaled in TMEM -- warp-uniformly, rare
+// after the first chunk), so every P stays <= 2^8 in fp16.  Afterwards O (if the offset
+// moved since the previous block: the PV of that block is complete, the commit that
+// released this S covers it) and the running sum follow the offset.  The row sum uses
+// the rounded probabilities that the PV product sees.
 template <bool kMask, int D>
 __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_col, int key0,
                                                     int row, int S, float scale_log2, bool has_o,
                                                     float &m_run, float &l_run) {
-  float m8[8];
+  float m_cur = m_run;  // offset of the P values written so far in this block
+  float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32(s_col, ra);
+  tmem_wait_ld();
 #pragma unroll
-  for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
-#pragma unroll 1
   for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32(s_col + c * 32, r);
-    tmem_wait_ld();
+    uint32_t(&r)[32] = (c & 1) ? rb : ra;
+    if (c + 1 < 4) tmem_ld_32x32(s_col + (c + 1) * 32, (c & 1) ? ra : rb);
+    float m8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m8[e] = -INFINITY;
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       float v = __uint_as_float(r[e]);
       if constexpr (kMask) {
         const int key = key0 + c * 32 + e;
         v = ((key > row) | (key >= S)) ? -INFINITY : v;
+        r[e] = __float_as_uint(v);
       }
       m8[e & 7] = fmaxf(m8[e & 7], v);
     }
+    const float cmax = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
+    const bool grow = cmax - m_cur > kRescaleLog2;  // first chunk of a row: m_cur = -inf
+    if (c > 0 && __any_sync(0xffffffffu, grow)) {
+      // rebase the P chunks 0..c-1 of this row (f = 1 for rows that keep their offset)
+      const float f = grow ? ex2_approx(m_cur - cmax) : 1.f;
+      tmem_wait_st();
+#pragma unroll 1
+      for (int pc = 0; pc < c; ++pc) {
+        uint32_t q[16];
+        tmem_ld_32x32_x16(s_col + pc * 16, q);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float2 pr = unpack_f16x2(q[e]);
+          q[e] = pack_f16x2(pr.x * f, pr.y * f);
+        }
+        tmem_st_32x32_x16(s_col + pc * 16, q);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r8[e] *= f;
+    }
+    if (grow) m_cur = cmax;
+    uint32_t pk[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float s0 = __uint_as_float(r[2 * e]);
+      const float s1 = __uint_as_float(r[2 * e + 1]);
+      // half of the pairs on MUFU.EX2, half on the FMA pipe (balances the two units)
+      const float a0 = fmaf(s0, scale_log2, -m_cur), a1 = fmaf(s1, scale_log2, -m_cur);
+      const float p0 = (e & 1) ? exp2_poly(a0) : ex2_approx(a0);
+      const float p1 = (e & 1) ? exp2_poly(a1) : ex2_approx(a1);
+      // P in fp16 (P <= 2^kRescaleLog2 = 256: far inside its range; 8x finer than bf16)
+      pk[e] = pack_f16x2(p0, p1);
+      const float2 pr = unpack_f16x2(pk[e]);
+      r8[e & 7] += pr.x + pr.y;
+    }
+    tmem_st_32x32_x16(s_col + c * 16, pk);
+    if (c + 1 < 4) tmem_wait_ld();
   }
-  const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                         fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
-  const bool grow = mx - m_run > kRescaleLog2;  // true on the first block (m_run = -inf)
-  const float m_use = grow ? mx : m_run;
-  const float alpha = grow ? ex2_approx(m_run - mx) : 1.f;
-  // PV of the previous block is complete (the commit that released this S covers it)
-  if (has_o && __any_sync(0xffffffffu, grow)) {
+  tmem_wait_st();
+  const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+  // O and l still carry the previous block's offset m_run (-inf before the first block:
+  // alpha = 0, l_run = 0, no O yet)
+  const bool moved = m_cur != m_run;
+  const float alpha = moved ? ex2_approx(m_run - m_cur) : 1.f;
+  if (has_o && __any_sync(0xffffffffu, moved)) {
 #pragma unroll 1
     for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
@@ -188,39 +249,10 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
       for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
       tmem_st_32x32(o_col + c * 32, r);
     }
+    tmem_wait_st();
   }
-  float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32(s_col + c * 32, r);
-    tmem_wait_ld();
-    uint32_t pk[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      float s0 = __uint_as_float(r[2 * e]);
-      float s1 = __uint_as_float(r[2 * e + 1]);
-      if constexpr (kMask) {
-        const int key = key0 + c * 32 + 2 * e;
-        s0 = ((key > row) | (key >= S)) ? -INFINITY : s0;
-        s1 = ((key + 1 > row) | (key + 1 >= S)) ? -INFINITY : s1;
-      }
-      // half of the pairs on MUFU.EX2, half on the FMA pipe (balances the two units)
-      const float a0 = fmaf(s0, scale_log2, -m_use), a1 = fmaf(s1, scale_log2, -m_use);
-      const float p0 = (e & 1) ? exp2_poly(a0) : ex2_approx(a0);
-      const float p1 = (e & 1) ? exp2_poly(a1) : ex2_approx(a1);
-      // P in fp16 (P <= 2^kRescaleLog2 = 256: far inside its range; 8x finer than bf16)
-      pk[e] = pack_f16x2(p0, p1);
-      // the row sum uses the rounded probabilities that the PV product sees
-      const float2 pr = __half22float2(*reinterpret_cast<const __half2 *>(&pk[e]));
-      r8[e & 7] += pr.x + pr.y;
-    }
-    tmem_st_32x32_x16(s_col + c * 16, pk);
-  }
-  tmem_wait_st();
-  const float rs = ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
   l_run = l_run * alpha + rs;
-  m_run = m_use;
+  m_run = m_cur;
 }
 
 }  // namespace

@@ -218,7 +218,7 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
     sym_layout_ = SymLayout::make(S, c.H, T, k);
     KRB_CUDA(cudaMalloc(&sym_, sym_layout_.bytes));
     KRB_CUDA(cudaMemset(sym_, 0, sym_layout_.bytes));
-    relay_expectations(S, c.H, T, k, opts_.rank, bn_down_, &rs_expect_, &ag_expect_, &nseg_);
+    nseg_ = (c.H + 255) / 256;
     // KRB_RELAY=direct|rsag; default: direct all-pull for k <= 2, where it moves the
     // same NVLink bytes as reduce-scatter + all-gather with one sync instead of two
     relay_direct_ = k <= 2 ? 1 : 0;
@@ -612,9 +612,6 @@ void Engine::down_stage(int l, StageTimes *st, const __nv_bfloat16 *gamma, float
     ra.part_off = sym_layout_.part_off;
     ra.red_off = sym_layout_.red_off;
     ra.flag_off = sym_layout_.flag_off;
-    ra.rs_expect = rs_expect_;
-    ra.ag_expect = ag_expect_;
-    ra.done_expect = relay_done_expect(S, H, opts_.tiles, bn_down_);
     ra.direct = relay_direct_;
     ra.ready_order = relay_ready_order_;
     ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch());

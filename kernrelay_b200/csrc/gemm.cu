@@ -11,18 +11,20 @@
 
 namespace krb {
 
-// configuration variant of a plain GEMM: fp32 outputs stage in fp32, the rest in 2 bytes
+// configuration variant of a plain GEMM: fp32 outputs stage in fp32, the rest in 2 bytes;
+// eight epilogue warps for the QKV and fp32-output epilogues, four for the others
 template <int MODE>
 constexpr int plain_cfg() {
-  return MODE == kEpiStoreF32 ? kCfgPlainF32 : kCfgPlain;
+  return MODE == kEpiStoreF32 ? kCfgPlainF32 : MODE == kEpiQkvRope ? kCfgPlain : kCfgPlain4;
 }
 
 // F16: fp16 operands and 2-byte outputs (bf16 otherwise); fp32 accumulation either way.
-// 10 warps: TMA producer, MMA issuer, 8 epilogue warps.
+// Warps: TMA producer, MMA issuer, 4 or 8 epilogue warps.
 template <int BN, int MODE, bool F16>
 __global__ void __launch_bounds__(GemmCfg<BN, plain_cfg<MODE>()>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                TileSched ts, int M, int K, EpiArgs ea, uint32_t *status) {
+                const __grid_constant__ CUtensorMap tb2, TileSched ts, int M, int K, EpiArgs ea,
+                uint32_t *status) {
   constexpr int V = plain_cfg<MODE>();
   using C = GemmCfg<BN, V>;
   extern __shared__ uint8_t smem_raw[];
@@ -32,10 +34,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, plain_cfg<MODE>()>::kThreads, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
+    tma_prefetch_desc(&tb2);
   }
   gemm_setup<BN, V>(s, C::kEpiWarps * 32);
   if (warp == 0) {
-    if (lane == 0) gemm_producer<BN, V>(s, &ta, &tb, ts, K, status);
+    if (lane == 0) gemm_producer<BN, V>(s, &ta, &tb, &tb2, ts, K, status);
   } else if (warp == 1) {
     if (lane == 0) gemm_mma<BN, V, F16>(s, ts, K, status);
   } else {
@@ -145,9 +148,13 @@ static int pick_band(long M, long N, long K, int num_m) {
   return (a_bytes > 48e6 && b_bytes < 24e6) ? 1 : num_m;
 }
 
+// The plain GEMMs with a per-tile column layout (store / fp32 store) take the two-phase
+// tail re-cut (TileSched); the SiLU-gated (B interleaved per BN block) and QKV (heads
+// per tile) epilogues keep one tile width.
 template <int BN, int MODE, bool F16>
-static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int n_b_rows, int K,
-                        const EpiArgs &ea, int grid_limit, uint32_t *status, cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const void *B, long ldb,
+                        int M, int n_b_rows, int K, const EpiArgs &ea, int grid_limit,
+                        uint32_t *status, cudaStream_t stream) {
   using C = GemmCfg<BN, plain_cfg<MODE>()>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
@@ -158,14 +165,14 @@ static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, int M, int
                                   int(C::kSmemBytes)));
     configured[dev & 63] = true;
   }
-  TileSched ts;
-  ts.num_m = (M + kBM - 1) / kBM;
-  ts.num_n = (n_b_rows + BN - 1) / BN;
-  ts.band = pick_band(M, n_b_rows, K, ts.num_m);
-  const int tiles = ts.num_m * ts.num_n;
-  int grid = std::min(tiles, sm_count(dev));
+  const int num_m = (M + kBM - 1) / kBM;
+  const int band = pick_band(M, n_b_rows, K, num_m);
+  int grid = std::min(num_m * ((n_b_rows + BN - 1) / BN), sm_count(dev));
   if (grid_limit > 0) grid = std::min(grid, grid_limit);
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, ts, M, K, ea, status);
+  constexpr bool two_phase = MODE == kEpiStore || MODE == kEpiStoreF32;
+  const TileSched ts = TileSched::make(num_m, n_b_rows, BN, band, grid, two_phase);
+  const CUtensorMap tb2 = ts.bn2 != BN ? make_tmap_2d_bf16(B, n_b_rows, K, ldb, ts.bn2, kBK) : tb;
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tb2, ts, M, K, ea, status);
   KRB_CUDA(cudaGetLastError());
 }
 
@@ -178,20 +185,22 @@ static void dispatch_bn(int bn, const CUtensorMap &ta, const T *B, long ldb, int
   switch (bn) {
     case 256: {
       const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 256, kBK);
-      launch_gemm<256, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+      launch_gemm<256, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
       break;
     }
     case 224:
       if constexpr (MODE != kEpiSiluMul && MODE != kEpiQkvRope) {
         const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 224, kBK);
-        launch_gemm<224, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+        launch_gemm<224, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
+                                    stream);
         break;
       }
       [[fallthrough]];
     case 128:
       if (bn == 128) {
         const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 128, kBK);
-        launch_gemm<128, MODE, F16>(ta, tb, M, n_b_rows, K, ea, grid_limit, status, stream);
+        launch_gemm<128, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
+                                    stream);
         break;
       }
       [[fallthrough]];

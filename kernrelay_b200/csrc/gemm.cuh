@@ -22,6 +22,7 @@
 #pragma once
 
 #include "ptx.cuh"
+#include "tile_sched.h"
 
 namespace krb {
 
@@ -43,14 +44,17 @@ enum EpiMode : int {
 //   kCfgRelay    the fused relay kernel: 4 epilogue warps, fp32 staging (its own
 //                budget: relay row buffers sit behind this layout)
 //   kCfgPlainF32 plain GEMM, 8 epilogue warps, fp32 output staging (kEpiStoreF32)
-// Eight epilogue warps (two per TMEM lane quadrant, splitting the tile's columns) halve
-// the epilogue of K = 3584 GEMMs, which otherwise outlasts the tile's MMAs.
-constexpr int kCfgPlain = 0, kCfgRelay = 1, kCfgPlainF32 = 2;
+//   kCfgPlain4   plain GEMM, 4 epilogue warps, 2-byte output staging
+// Eight epilogue warps (two per TMEM lane quadrant, splitting the tile's columns) cut
+// the exposed epilogue of the last tile of GEMMs with two tiles per SM (QKV with its
+// RoPE epilogue, o_proj's fp32 output: 3-5 % faster on B200); the SiLU-gated and plain
+// stores, with many tiles per SM, ran 1-2 % faster with four.
+constexpr int kCfgPlain = 0, kCfgRelay = 1, kCfgPlainF32 = 2, kCfgPlain4 = 3;
 
 template <int BN, int V = kCfgPlain>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
-  static constexpr int kEpiWarps = V == kCfgRelay ? 4 : 8;
+  static constexpr int kEpiWarps = (V == kCfgRelay || V == kCfgPlain4) ? 4 : 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
@@ -60,7 +64,8 @@ struct GemmCfg {
   // 80 bytes (kCfgPlain)
   static constexpr uint32_t kStageRow = 36;
   static constexpr uint32_t kStage2Pitch = 80;
-  static constexpr uint32_t kWarpEpiBytes = V == kCfgPlain ? 32 * kStage2Pitch : 32 * kStageRow * 4;
+  static constexpr bool kStage2 = V == kCfgPlain || V == kCfgPlain4;
+  static constexpr uint32_t kWarpEpiBytes = kStage2 ? 32 * kStage2Pitch : 32 * kStageRow * 4;
   static constexpr uint32_t kEpiBytes = kEpiWarps * kWarpEpiBytes;
   // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
   // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
@@ -79,20 +84,6 @@ struct GemmCfg {
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
-};
-
-struct TileSched {
-  int num_m;   // 128-row blocks
-  int num_n;   // BN-column blocks
-  int band;    // row blocks per band (num_m % band == 0)
-  __device__ __forceinline__ int total() const { return num_m * num_n; }
-  __device__ __forceinline__ void tile(int idx, int &mb, int &nb) const {
-    const int per_band = band * num_n;
-    const int b = idx / per_band;
-    const int r = idx - b * per_band;
-    nb = r / band;
-    mb = b * band + (r - nb * band);
-  }
 };
 
 template <int BN, int RELAY = 0>
@@ -164,8 +155,8 @@ __device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN, RELAY> &s) 
 // ---- warp 0, one thread: TMA producer
 template <int BN, int RELAY = 0>
 __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, const CUtensorMap *ta,
-                                              const CUtensorMap *tb, const TileSched &ts, int K,
-                                              uint32_t *status) {
+                                              const CUtensorMap *tb, const CUtensorMap *tb2,
+                                              const TileSched &ts, int K, uint32_t *status) {
   using C = GemmCfg<BN, RELAY>;
   const int nkb = (K + kBK - 1) / kBK;
   int stage = 0;
@@ -173,8 +164,10 @@ __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, 
   long issued = 0;
   const uint64_t pol_a = l2_policy_evict_last();
   for (int t = blockIdx.x; t < ts.total() && !*s.abort; t += gridDim.x) {
-    int mb, nb;
-    ts.tile(t, mb, nb);
+    int mb, n0, bn;
+    ts.tile(t, mb, n0, bn);
+    const bool narrow = bn != BN;  // phase-2 tile: B rows through the bn2-row tensor map
+    const uint32_t stage_tx = C::kABytes + uint32_t(bn) * kBK * 2;
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(&s.empty[stage], phase ^ 1, kMbarLimitNs) || *s.abort) {
         report_status(status, kStatusTmaWait);
@@ -184,9 +177,9 @@ __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, 
       {
         uint8_t *a = s.tiles + stage * C::kStageBytes;
         uint8_t *b = a + C::kABytes;
-        mbar_arrive_expect_tx(&s.full[stage], C::kStageBytes);
+        mbar_arrive_expect_tx(&s.full[stage], stage_tx);
         tma_load_2d_hint(a, ta, &s.full[stage], kb * kBK, mb * kBM, pol_a);
-        tma_load_2d(b, tb, &s.full[stage], kb * kBK, nb * BN);
+        tma_load_2d(b, narrow ? tb2 : tb, &s.full[stage], kb * kBK, n0);
       }
       ++issued;
       if (++stage == C::kStages) {
@@ -220,7 +213,8 @@ template <int BN, int RELAY = 0, bool F16 = false>
 __device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const TileSched &ts,
                                          int K, uint32_t *status) {
   using C = GemmCfg<BN, RELAY>;
-  constexpr uint32_t idesc = F16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
+  constexpr uint32_t idesc1 = F16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
+  const uint32_t idesc2 = F16 ? idesc_f16_f32(kBM, ts.bn2) : idesc_bf16_f32(kBM, ts.bn2);
   const uint32_t tmem = *s.tmem_slot;
   const int nkb = (K + kBK - 1) / kBK;
   int stage = 0;
@@ -229,6 +223,7 @@ __device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
+    const uint32_t idesc = t < ts.p1 ? idesc1 : idesc2;
     if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1, kMbarLimitNs) || *s.abort) {
       report_status(status, kStatusMmaWait);
       *s.abort = 1;
@@ -483,12 +478,12 @@ __device__ __forceinline__ void epi2_store(uint8_t *stage2, float *v, const __nv
 // takes heads grp, grp + NG, ...
 template <int BN, bool F16, typename RowPtr>
 __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, uint8_t *stage2, RowPtr out_row,
-                                             const EpiArgs &ea, int row, bool row_ok, int nb,
+                                             const EpiArgs &ea, int row, bool row_ok, int n0,
                                              int grp, int NG) {
   const int D = ea.D, half = D / 2, nch = D / 32;
 #pragma unroll 1
   for (int h0 = grp * D; h0 < BN; h0 += NG * D) {
-    const int hcol = nb * BN + h0;  // first column of this head
+    const int hcol = n0 + h0;  // first column of this head
     if (hcol >= ea.n_out) break;    // warp-uniform
     if (hcol >= ea.rope_cols) {
       // v head: bias only; with ea.vt also transposed (lanes = 32 consecutive rows, so
@@ -561,16 +556,15 @@ __device__ __forceinline__ void epi_qkv_rope(uint32_t tbase, uint8_t *stage2, Ro
   }
 }
 
-// ---- warps 2..9: the plain GEMM's epilogue (kEpiStore / kEpiSiluMul / kEpiStoreF32 /
-// kEpiQkvRope).  Warp w reads TMEM lane quadrant w % 4 (rows); the two warps of a
-// quadrant split the tile's 32-column chunks (or heads) between them: group
+// ---- warps 2..: the plain GEMM's epilogue (kEpiStore / kEpiSiluMul / kEpiStoreF32 /
+// kEpiQkvRope).  Warp w reads TMEM lane quadrant w % 4 (rows); with 8 warps the two
+// warps of a quadrant split the tile's 32-column chunks (or heads) between them: group
 // (w - 2) / 4 takes chunks grp, grp + 2, ...  F16: fp16 operands and 2-byte outputs in
 // fp16 instead of bf16.
 template <int BN, int V, int MODE, bool F16 = false>
 __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, const TileSched &ts,
                                               int M, const EpiArgs &ea, uint32_t *status) {
   using C = GemmCfg<BN, V>;
-  static_assert(C::kEpiWarps == 8, "plain GEMM epilogue: 8 warps");
   constexpr int NG = C::kEpiWarps / 4;  // column groups
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -581,8 +575,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
   float *stage = reinterpret_cast<float *>(stage_raw);
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
-    int mb, nb;
-    ts.tile(t, mb, nb);
+    int mb, n0, bn;
+    ts.tile(t, mb, n0, bn);
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
     if (!mbar_wait(&s.tfull[acc], acc_phase, kMbarLimitNs) || *s.abort) {
@@ -597,15 +591,16 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
       return (row0 + r < M) ? ea.c + static_cast<long>(row0 + r) * ea.ldc : nullptr;
     };
     if constexpr (MODE == kEpiQkvRope) {
-      static_assert(V == kCfgPlain, "2-byte staging");
+      static_assert(C::kStage2, "2-byte staging");
       // rows past M are not stored; clamp their table position
       const int erow = mb * kBM + quad * 32 + lane;
-      epi_qkv_rope<BN, F16>(tbase, stage_raw, out_row, ea, min(erow, M - 1), erow < M, nb, grp, NG);
+      epi_qkv_rope<BN, F16>(tbase, stage_raw, out_row, ea, min(erow, M - 1), erow < M, n0, grp, NG);
     } else if constexpr (MODE == kEpiStore || MODE == kEpiStoreF32) {
 #pragma unroll 1
-      for (int c = grp; c < BN / 32; c += NG) {
-        const int col0 = nb * BN + c * 32;
+      for (int c = grp; c * 32 < bn; c += NG) {
+        const int col0 = n0 + c * 32;
         if (col0 >= ea.n_out) break;  // warp-uniform
+        const int valid = min(bn - c * 32, ea.n_out - col0);
         uint32_t r[32];
         tmem_ld_32x32(tbase + c * 32, r);
         tmem_wait_ld();
@@ -613,21 +608,21 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if constexpr (MODE == kEpiStore) {
-          static_assert(V == kCfgPlain, "2-byte staging");
-          epi2_store<F16>(stage_raw, v, ea.bias, out_row, col0, ea.n_out - col0);
+          static_assert(C::kStage2, "2-byte staging");
+          epi2_store<F16>(stage_raw, v, ea.bias, out_row, col0, valid);
         } else {
           static_assert(V == kCfgPlainF32, "fp32 staging");
           epi_stage_put(stage, v);
-          epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, ea.n_out - col0);
+          epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, valid);
         }
       }
     } else {
-      static_assert(V == kCfgPlain, "2-byte staging");
+      static_assert(C::kStage2, "2-byte staging");
       constexpr int HALF = BN / 2;
       static_assert(HALF % 32 == 0, "silu epilogue needs BN/2 % 32 == 0");
 #pragma unroll 1
       for (int c = grp; c < HALF / 32; c += NG) {
-        const int col0 = nb * HALF + c * 32;
+        const int col0 = n0 / 2 + c * 32;
         if (col0 >= ea.n_out) break;
         uint32_t g[32], u[32];
         tmem_ld_32x32(tbase + c * 32, g);

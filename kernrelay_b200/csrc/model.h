@@ -16,6 +16,7 @@
 
 #include "common.h"
 #include "relay.cuh"
+#include "tile_sched.h"
 
 namespace krb {
 
@@ -228,7 +229,6 @@ class Engine {
   SymLayout sym_layout_{};
   void *sym_ = nullptr;
   std::vector<void *> peers_;
-  uint32_t rs_expect_ = 0, ag_expect_ = 0;
   int relay_direct_ = 0;  // 1: direct all-pull relay, 0: reduce-scatter + all-gather
   int relay_ready_order_ = 1;  // rsag: phases in readiness order (KRB_RELAY_ORDER=pipeline: fixed)
   int nseg_ = 0;
@@ -247,9 +247,8 @@ class Engine {
 template <typename T>
 void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
                       const RelayArgs &ra, cudaStream_t stream);
-uint32_t relay_done_expect(int S, int H, int T, int bn);
-void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
-                        uint32_t *ag_expect, int *nseg);
+// the relay GEMM's tile schedule for `grid` CTAs (row tile t = band t)
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid);
 
 // device-side synthesis / fill (synth.cu)
 void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_, double mean,

@@ -52,6 +52,8 @@
 
 namespace krb {
 
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid);  // bottom of this file
+
 constexpr int kRelayWarp0 = 6;                      // warps 0..5: GEMM roles
 constexpr int kRelayWarps = 8;                      // consumer warps per CTA
 constexpr int kSignalWarp = kRelayWarp0 + kRelayWarps;  // warp 14: system-scope signals
@@ -128,8 +130,8 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
   uint64_t fence_ns = 0, fence_cnt = 0, fence_max = 0;  // trace only
   int it = 0;
   for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
-    int mb, nb;
-    ts.tile(t, mb, nb);
+    int mb, n0, bn;
+    ts.tile(t, mb, n0, bn);
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
     // collective decision: the four epilogue warps meet at named barrier 1 below,
@@ -148,9 +150,10 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
       return part + static_cast<size_t>(row0 + r) * ra.H;
     };
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col0 = nb * BN + c * 32;
+    for (int c = 0; c * 32 < bn; ++c) {
+      const int col0 = n0 + c * 32;
       if (col0 >= ra.H) break;
+      const int valid = min(bn - c * 32, ra.H - col0);
       uint32_t r[32];
       tmem_ld_32x32(tbase + c * 32, r);
       tmem_wait_ld();
@@ -161,9 +164,9 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
       if (ra.k == 1)
         // one rank: nothing to reduce; the fp32 partial goes straight into sum_out
         // and the relay warps add the residual in place
-        epi_stage_store_f32(stage, ra.sum_out, ra.H, row0, ra.S, col0, ra.H - col0);
+        epi_stage_store_f32(stage, ra.sum_out, ra.H, row0, ra.S, col0, valid);
       else
-        epi_stage_store_bf16<F16>(stage, part_row, nullptr, col0, ra.H - col0);
+        epi_stage_store_bf16<F16>(stage, part_row, nullptr, col0, valid);
     }
     tc_fence_before();
     mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
@@ -404,7 +407,8 @@ __device__ __forceinline__ bool pair_addnorm_row_staged(
 }
 
 template <int KR, bool F16>  // ranks (compile-time so the partial registers fit); fp16 data
-__device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int *flag_smem,
+__device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSched &ts,
+                                               volatile int *flag_smem,
                                                float *pair_ss, uint8_t *stage_base) {
   // reduce-scatter units in flight per warp: KR partial vectors each
   constexpr int kRsBatch = KR <= 2 ? 4 : (KR == 4 ? 2 : 1);
@@ -416,8 +420,9 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
   const int gp = blockIdx.x * (kRelayWarps / 2) + pair;
   const int GP = gridDim.x * (kRelayWarps / 2);
   const uint32_t seq = (*ra.epoch - 1u) * uint32_t(ra.L) + uint32_t(ra.layer) + 1u;
-  const uint32_t rs_target = seq * ra.rs_expect;
-  const uint32_t ag_target = seq * ra.ag_expect;
+  // k > 1: one forwarded signal per (row tile, source) and per (row tile, owner) each run
+  const uint32_t rs_target = seq;
+  const uint32_t ag_target = seq;
   const size_t rs_cnt_base = ra.flag_off;
   const size_t ag_cnt_base = ra.flag_off + size_t(ra.T) * ra.k * 128;
   const int units = ra.Rk * ra.nseg;
@@ -452,7 +457,8 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
     // GEMM tiles are released; sum_out = resid + partial in place, then RMSNorm
     for (int t = 0; t < ra.T; ++t) {
       const bool ok =
-          wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusLocalWait, timeout, flag_smem);
+          wait_all_sources(ra, rs_cnt_base, t, seq * uint32_t(ts.band_tiles(t)), kStatusLocalWait,
+                           timeout, flag_smem);
       if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
       if (!ok) {
         timeout = 0;
@@ -727,7 +733,7 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, volatile int
 // rank.  Jobs 0..T-1 forward rs_done[t] to rs_cnt[t][rank]; jobs T..2T-1 (rsag)
 // forward ag_done[t] to ag_cnt[t][rank].  Only 2T threads per GPU pay for a
 // system-scope fence, off the GEMM epilogue and the relay warps.
-__device__ __forceinline__ void relay_signal(const RelayArgs &ra) {
+__device__ __forceinline__ void relay_signal(const RelayArgs &ra, const TileSched &ts) {
   const int j = blockIdx.x;
   const int njobs = ra.direct ? ra.T : 2 * ra.T;
   if (ra.k == 1 || j >= njobs) return;
@@ -738,7 +744,7 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra) {
   const int t = ag ? j - ra.T : j;
   const size_t tk = 2 * size_t(ra.T) * ra.k;
   const size_t done_line = ra.flag_off + (tk + 2 + (ag ? ra.T : 0) + t) * 128;
-  const uint32_t target = seq * (ag ? uint32_t(gridDim.x) : ra.done_expect);
+  const uint32_t target = seq * (ag ? uint32_t(gridDim.x) : uint32_t(ts.band_tiles(t)));
   if (!wait_counter_geq(flag_ptr(ra.local_base, done_line), target, timeout)) {
     report_status(ra.status, kStatusLocalWait);
     return;
@@ -758,7 +764,8 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra) {
 template <int BN, int KR, bool F16>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
-                      const __grid_constant__ CUtensorMap tb, TileSched ts,
+                      const __grid_constant__ CUtensorMap tb,
+                      const __grid_constant__ CUtensorMap tb2, TileSched ts,
                       const __grid_constant__ RelayArgs ra) {
   extern __shared__ uint8_t smem_raw[];
   const GemmSmemView<BN, 1> s = GemmSmemView<BN, 1>::carve(smem_raw);
@@ -767,6 +774,7 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
+    tma_prefetch_desc(&tb2);
   }
   // relay staging: kRelayWarps/2 pair buffers of H bf16, then their mbarriers
   using C = GemmCfg<BN, 1>;
@@ -782,16 +790,16 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   }
   gemm_setup<BN, 1>(s, 128);  // its barrier-init fence and __syncthreads cover the above
   if (warp == 0) {
-    if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, ts, ra.K, ra.status);
+    if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, &tb2, ts, ra.K, ra.status);
   } else if (warp == 1) {
     if (lane == 0) gemm_mma<BN, 1, F16>(s, ts, ra.K, ra.status);
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN, F16>(s, ts, ra);
   } else if (warp < kSignalWarp) {
-    relay_consumer<KR, F16>(ra, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
+    relay_consumer<KR, F16>(ra, ts, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
                             stage_base);
   } else if (lane == 0) {
-    relay_signal(ra);
+    relay_signal(ra, ts);
   }
   gemm_teardown<BN, 1>(s);
 }
@@ -821,8 +829,7 @@ static bool relay_bulk_fits(int H, int k, size_t dyn_limit) {
 
 template <int BN, int KR, bool F16>
 static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
-                         TileSched ts, const RelayArgs &ra_in, bool want_bulk, int grid,
-                         cudaStream_t stream) {
+                         const RelayArgs &ra_in, bool want_bulk, int grid, cudaStream_t stream) {
   auto kern = relay_down_kernel<BN, KR, F16>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
@@ -840,8 +847,9 @@ static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
   ra.bulk = (want_bulk && relay_bulk_fits<BN>(ra.H, ra.k, dyn_limit[dev & 63])) ? 1 : 0;
   const size_t smem = relay_smem_bytes<BN>(ra.H, ra.bulk != 0);
   if (smem > dyn_limit[dev & 63]) throw CudaError("relay: shared memory budget exceeded");
+  const TileSched ts = relay_tile_sched(ra.S, ra.H, ra.T, BN, grid);
   const CUtensorMap tmb = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, BN, kBK);
-  ts.num_n = (ra.H + BN - 1) / BN;
+  const CUtensorMap tmb2 = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, ts.bn2, kBK);
   // cooperative: every CTA must be co-resident, because the relay warps wait
   // for tiles produced by other CTAs of the same grid
   cudaLaunchConfig_t cfg = {};
@@ -854,7 +862,7 @@ static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  KRB_CUDA(cudaLaunchKernelEx(&cfg, kern, tma, tmb, ts, ra));
+  KRB_CUDA(cudaLaunchKernelEx(&cfg, kern, tma, tmb, tmb2, ts, ra));
 }
 
 template <typename T>
@@ -870,10 +878,6 @@ void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
   if (!F16 && ra.k != 1) throw CudaError("relay: bf16 operands only with one rank");
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
-  TileSched ts;
-  ts.num_m = ra.S / kBM;
-  ts.band = ra.R / kBM;
-  ts.num_n = 0;
   const CUtensorMap tma = make_tmap_2d_bf16(act, ra.S, ra.K, lda, kBM, kBK);
   const int grid = sm_count(dev);
   if (ra.k > 1 && 2 * ra.T > grid) throw CudaError("relay: more row tiles than signal jobs");
@@ -888,14 +892,14 @@ void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
       return !(e && e[0] == '0');
     }();
     if constexpr (!F16) {
-      launch_relay<B, 1, false>(tma, w_down, ldb, ts, ra, false, grid, stream);
+      launch_relay<B, 1, false>(tma, w_down, ldb, ra, false, grid, stream);
     } else {
       const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
       switch (ra.k) {
-        case 1: launch_relay<B, 1, true>(tma, w_down, ldb, ts, ra, false, grid, stream); break;
-        case 2: launch_relay<B, 2, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
-        case 4: launch_relay<B, 4, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
-        case 8: launch_relay<B, 8, true>(tma, w_down, ldb, ts, ra, want, grid, stream); break;
+        case 1: launch_relay<B, 1, true>(tma, w_down, ldb, ra, false, grid, stream); break;
+        case 2: launch_relay<B, 2, true>(tma, w_down, ldb, ra, want, grid, stream); break;
+        case 4: launch_relay<B, 4, true>(tma, w_down, ldb, ra, want, grid, stream); break;
+        case 8: launch_relay<B, 8, true>(tma, w_down, ldb, ra, want, grid, stream); break;
         default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
       }
     }
@@ -913,10 +917,6 @@ template void relay_down_layer<__nv_bfloat16>(const __nv_bfloat16 *, long, const
 template void relay_down_layer<__half>(const __half *, long, const __half *, long, int,
                                        const RelayArgs &, cudaStream_t);
 
-// Expected counter increments for the relay (host helper): owner `rank`
-// receives one rs increment per (n block, 128-row block touching its slice)
-// from every source, and one ag increment per reduced 256-column unit of each
-// owner's slice.
 // ------------------------------------------------- allocation-free relay scratch
 // Scratch of krb_relay_down_single_noalloc: the flag counters and the run epoch
 // of a one-device relay (k = 1 needs no partial or reduced-row buffers: the fp32
@@ -943,22 +943,10 @@ uint8_t *relay_noalloc_scratch() {
   return addr[dev];
 }
 
-// GEMM tiles per row tile: (n blocks) x (128-row blocks of the tile).
-uint32_t relay_done_expect(int S, int H, int T, int bn) {
-  return uint32_t(((H + bn - 1) / bn) * ((S / T) / kBM));
-}
-
-void relay_expectations(int S, int H, int T, int k, int rank, int bn, uint32_t *rs_expect,
-                        uint32_t *ag_expect, int *nseg) {
-  (void)rank;
-  *nseg = (H + 255) / 256;
-  if (k == 1) {
-    *rs_expect = relay_done_expect(S, H, T, bn);  // every GEMM tile releases directly
-    *ag_expect = 0;                               // no all-gather
-  } else {
-    *rs_expect = 1;  // one forwarded signal per (tile, source)
-    *ag_expect = 1;  // one forwarded signal per (tile, owner)
-  }
+// The relay GEMM's tile schedule: one band per row tile (row tile t completes before t+1),
+// the two-phase tail re-cut when the tiles need between one and two waves of `grid` CTAs.
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid) {
+  return TileSched::make(S / kBM, H, bn, (S / T) / kBM, grid, true);
 }
 
 }  // namespace krb

@@ -94,15 +94,13 @@ struct RelayArgs {
   uint8_t *local_base;
   size_t part_off, red_off, flag_off;
   // Releases, per layer.  k = 1: every GEMM tile's epilogue adds 1 to rs_cnt[t][0]
-  // (rs_expect = GEMM tiles per row tile).  k > 1, two levels: each GEMM tile's
-  // epilogue adds 1 to the local rs_done[t] at GPU scope (done_expect per row
-  // tile); once it is complete, one signal thread per GPU fences at system scope
-  // and adds 1 to rs_cnt[t][rank] on every rank (rs_expect = 1); likewise every
-  // CTA adds 1 to ag_done[t] after storing its reduced rows (grid per row tile)
-  // and one signal thread forwards 1 to ag_cnt[t][rank] (ag_expect = 1).
-  uint32_t rs_expect;   // increments per (tile, source) per layer on a consumer
-  uint32_t ag_expect;   // increments per (tile, owner) per layer on every rank
-  uint32_t done_expect; // GEMM tiles per row tile (k > 1: local rs_done target)
+  // (target: the GEMM tiles of row tile t, TileSched::band_tiles(t)).  k > 1, two
+  // levels: each GEMM tile's epilogue adds 1 to the local rs_done[t] at GPU scope
+  // (target band_tiles(t)); once it is complete, one signal thread per GPU fences at
+  // system scope and adds 1 to rs_cnt[t][rank] on every rank (target 1); likewise
+  // every CTA adds 1 to ag_done[t] after storing its reduced rows (target: the grid)
+  // and one signal thread forwards 1 to ag_cnt[t][rank] (target 1).  Targets scale
+  // with the run epoch and layer (monotone counters).
   // 1: direct all-pull (every rank sums all k partials of every row inside its
   // Add+RMSNorm; one synchronisation per tile, (k-1) tiles over NVLink per rank);
   // 0: reduce-scatter + all-gather (2(k-1)/k tiles over NVLink, two synchronisations)

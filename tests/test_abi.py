@@ -92,29 +92,48 @@ def test_device_count_never_fails(krlib):
 
 @pytest.mark.parametrize("S,H,T,k,bn", [(2048, 3584, 4, 8, 256), (2048, 3584, 4, 2, 224),
                                         (512, 896, 4, 1, 256), (4096, 4096, 4, 8, 256),
-                                        (2048, 2560, 2, 4, 128)])
+                                        (2048, 2560, 2, 4, 128), (2048, 3584, 4, 1, 224)])
 def test_relay_plan_counts(krlib, S, H, T, k, bn):
-    """Every row tile's GEMM tiles (n blocks x its 128-row blocks) complete the local
-    counter the signal warp waits for (done_expect); for k > 1 each source forwards
-    one signal per tile and owner (rs_expect = ag_expect = 1), for k = 1 the GEMM
-    tiles release the consumer directly (rs_expect = done_expect).  Every rank owns
-    a slice of every row tile, so every rank hears from every source."""
+    """The relay GEMM's tile schedule covers every (128-row block, column) of the output
+    exactly once; row tile t's counter target is the number of GEMM tiles whose rows lie in
+    it (k = 1) or one forwarded signal per source (k > 1); a two-phase schedule runs at most
+    one wave per phase.  Every rank owns a slice of every row tile, so every rank hears
+    from every source."""
     plans = [krlib.relay_plan(S, H, T, k, r, bn) for r in range(k)]
     p0 = plans[0]
-    assert p0["R"] == S // T and p0["Rk"] * k == p0["R"]
-    per_tile, owners = {}, {}
+    R = S // T
+    assert p0["R"] == R and p0["Rk"] * k == R
+    cover = {}
+    per_band = [0] * T
+    for mb, n0, w in p0["tiles"]:
+        assert w % 16 == 0 and 0 <= n0 < H
+        per_band[(mb * 128) // R] += 1
+        for c in range(n0, min(n0 + w, H), 16):
+            cover[(mb, c)] = cover.get((mb, c), 0) + 1
+    assert len(cover) == (S // 128) * len(range(0, H, 16)) and set(cover.values()) == {1}
+    assert per_band == p0["band_tiles"] and p0["total"] == len(p0["tiles"])
+    grid = p0["grid"]
+    if p0["p1"] < p0["total"]:
+        assert p0["p1"] <= grid and p0["total"] - p0["p1"] <= grid and p0["bn2"] < bn
+    for j in range(k):
+        assert plans[j]["rs_expect"] == (p0["band_tiles"] if k == 1 else [1] * T)
+        assert plans[j]["ag_expect"] == (0 if k == 1 else 1)
+    owners = {}
     for b, (tile, j0, j1) in enumerate(p0["blocks"]):
-        assert tile == (b * 128) // p0["R"]
-        per_tile[tile] = per_tile.get(tile, 0) + p0["num_n"]
+        assert tile == (b * 128) // R
         owners.setdefault(tile, set()).update(range(j0, j1 + 1))
     for t in range(T):
-        assert per_tile[t] == p0["done_expect"], t
         assert owners[t] == set(range(k)), t
-    for j in range(k):
-        if k == 1:
-            assert plans[j]["rs_expect"] == p0["done_expect"] and plans[j]["ag_expect"] == 0
-        else:
-            assert plans[j]["rs_expect"] == 1 and plans[j]["ag_expect"] == 1
+
+
+def test_relay_plan_two_phase_on_b200_7b(krlib):
+    """Qwen2.5-7B down_proj at S=2048, T=4, BN=224 on 148 SMs: 256 tiles of 128x224 (1.73
+    waves) become 148 phase-1 tiles plus 140 tiles of width 176 (1 + 176/224 tile times)."""
+    p = krlib.relay_plan(2048, 3584, 4, 2, 0, 224)
+    if p["grid"] != 148:
+        pytest.skip("not a 148-SM device")
+    assert p["p1"] == 148 and p["bn2"] == 176 and p["total"] == 288
+    assert p["band_tiles"] == [64, 64, 20 + 56, 84]
 
 
 def test_relay_plan_rejects_bad_shapes(krlib):

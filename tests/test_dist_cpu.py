@@ -52,7 +52,7 @@ def test_relay_plans_exchanged_between_ranks(krlib, tmp_path):
     p1 = json.loads((tmp_path / "r1.json").read_text())
     assert p0 == p1                                               # both ranks hold both plans
     a, b = p0
-    for key in ("R", "Rk", "num_n", "nseg"):
+    for key in ("R", "Rk", "bn", "bn2", "p1", "total", "tiles", "band_tiles", "nseg"):
         assert a[key] == b[key]                                   # ranks agree on the tiling
     assert a["R"] == 2048 // 4 and a["Rk"] == a["R"] // 2
 
