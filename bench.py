@@ -43,6 +43,19 @@ sys.path.insert(0, str(REPO))
 os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 METRIC = "Qwen2.5-7B prefill tok/s @seq2048 at 1/2/4/8 B200; tp_split vs tp speedup"
+# the other BASELINE configurations (Qwen3-VL text decoders) report the same quantity
+MODEL_NAMES = {
+    "qwen2.5-7b": "Qwen2.5-7B architecture (28 layers, H 3584, I 18944, 28/4 heads, V 152064)",
+    "qwen3-vl-4b": "Qwen3-VL-4B text decoder (36 layers, H 2560, I 9728, 32/8 heads, QK-norm, V 151936 tied)",
+    "qwen3-vl-8b": "Qwen3-VL-8B text decoder (36 layers, H 4096, I 12288, 32/8 heads, QK-norm, V 151936)",
+    "qwen2.5-0.5b": "Qwen2.5-0.5B architecture (24 layers, H 896, I 4864, 14/2 heads, V 151936 tied)",
+}
+
+
+def metric_for(config: str, S: int) -> str:
+    if config == "qwen2.5-7b" and S == 2048:
+        return METRIC
+    return f"{config} prefill tok/s @seq{S} at 1/2/4/8 B200; tp_split vs tp speedup"
 # the reference's published prefill times for this metric (Ascend 910B3, real weights): 146.2 ms
 # single-device and 118.153 ms tp2 at S = 2048 -> tokens/s
 PUBLISHED_TOKS = {1: 2048 / 0.1462, 2: 2048 / 0.118153}
@@ -435,12 +448,13 @@ def run_ours(args, d: Dist):
     base = None
     if not args.no_tp:
         base = run_mode(d, mdir, f"tp{N}", S, 1, args.steps, args.warmup, False, None)
+    pp = run_pp2(d, mdir, S, args) if args.pp2 else None
     if d.rank != 0:
         return None
     toks = S / (split["ms_per_step"] * 1e-3)
     roof, stages = roofline_block(cfg, S, N, 0, split, pk, nvlink_gbs)
     line = {
-        "metric": METRIC,
+        "metric": metric_for(args.config, S),
         "value": round(toks, 1),
         "unit": "tok/s",
         "n_gpus": N,
@@ -449,7 +463,8 @@ def run_ours(args, d: Dist):
         "ms_per_step": round(split["ms_per_step"], 4),
         "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": round(toks / PUBLISHED_TOKS[N], 3) if N in PUBLISHED_TOKS else None,
+        "vs_baseline": (round(toks / PUBLISHED_TOKS[N], 3)
+                        if N in PUBLISHED_TOKS and metric_for(args.config, S) == METRIC else None),
         "dtype": "fp16",
         "precision": ("weights bf16 (the model's dtype) converted exactly to fp16 at load; GEMM and "
                       "attention operands and activations fp16 (8x finer rounding than bf16, same "
@@ -457,7 +472,7 @@ def run_ours(args, d: Dist):
         "data": "synthetic: seeded random-init weights N(0,0.02) (norms 1), uniform random token ids (seed 1234)",
         "config": {"workload": workload_name(args.config, S)
                                + (f" (PROFILING: {cfg.L} layers)" if args.layers else ""),
-                   "model": "Qwen2.5-7B architecture (28 layers, H 3584, I 18944, 28/4 heads, V 152064)",
+                   "model": MODEL_NAMES.get(args.config, args.config),
                    "global_batch": 1, "seq_len": S, "parallelism": f"tp{N} MLP (attention replicated)",
                    "mode": split["mode"], "tiles": args.tiles, "graph": True,
                    "lm_head_rows": S,
@@ -482,7 +497,36 @@ def run_ours(args, d: Dist):
     }
     if N == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg, S, 1)
+    if pp is not None:
+        line["pp2_baseline"] = pp
     return line
+
+
+def run_pp2(d: Dist, mdir: Path, S: int, args):
+    """The PP=2 layer-pipeline baseline (reference RunQwenPP, qwen_main.cpp:1993-2146) on GPUs
+    0 and 1 through kr_qwen_pp_run, one request (the reference's R=1 row), run by rank 0 after
+    the TP measurement while the other ranks wait.  Host-timed wall per prefill, as the
+    reference reports it."""
+    import torch
+    res = None
+    if d.rank == 0:
+        if torch.cuda.device_count() < 2:
+            res = {"unavailable": "needs 2 visible GPUs"}
+        else:
+            from kernrelay_b200 import libapi
+            r = libapi.qwen_pp_run(mdir, mode="pp", seq=S, dev0=0, dev1=1, requests=1,
+                                   warmup=max(1, args.warmup), iters=max(3, args.steps // 4))
+            if r.get("_rc") != 0:
+                res = {"error": r.get("error", "kr_qwen_pp_run failed")}
+            else:
+                best = r["wall_best_us"]
+                res = {"mode": r.get("mode"), "devices": r.get("devices"), "requests": 1,
+                       "layers": r.get("layers"), "wall_best_us": best,
+                       "wall_typical_us": r.get("wall_typical_us"),
+                       "value": round(S / (best * 1e-6), 1), "unit": "tok/s",
+                       "timing": "host wall per prefill (enqueue + device), best of iters"}
+    d.barrier()
+    return res
 
 
 # ------------------------------------------------------------------ micro-DAG workload
@@ -642,12 +686,13 @@ def run_reference(args):
           "sample": cp.describe() + f"; {len(times)} timed prefills, mean"}
     cb.update(cpu_info())
     line = {
-        "metric": METRIC, "impl": "reference", "value": round(toks, 2), "unit": "tok/s",
+        "metric": metric_for(args.config, S), "impl": "reference", "value": round(toks, 2),
+        "unit": "tok/s",
         "n_gpus": N, "steps": len(times), "warmup": len(warm),
         "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic (random weights of the exact shapes)",
         "config": {"workload": workload_name(args.config, S),
-                   "model": "Qwen2.5-7B architecture" if args.config == "qwen2.5-7b" else args.config,
+                   "model": MODEL_NAMES.get(args.config, args.config),
                    "seq_len": S, "global_batch": 1, "parallelism": "none (host CPU)"},
         "cpu_baseline": cb,
         "e2e": {"value": round(toks, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -675,6 +720,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: fewer decoder layers (not a valid benchmark number)")
+    ap.add_argument("--pp2", action="store_true",
+                    help="also time the PP=2 layer-pipeline baseline on GPUs 0 and 1 (rank 0)")
     ap.add_argument("--workload", choices=["prefill", "microdag"], default="prefill",
                     help="prefill: the headline metric; microdag: BASELINE configs[1] (the "
                          "isolated down GEMM -> AllReduce -> AddNorm stage)")
