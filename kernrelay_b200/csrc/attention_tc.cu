@@ -70,8 +70,8 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // 2^x on the FMA pipe, to share the softmax's exponentials with the MUFU unit:
 // Cody-Waite style range reduction x = n + f, n = round(x) (by the 1.5*2^23
 // shift), f in [-1/2, 1/2], and a cubic for 2^f fitted here by weighted least
-// squares for relative error on Chebyshev nodes (max relative error 2.2e-4,
-// a tenth of the bf16 rounding the probabilities get next); n is added to the
+// squares for relative error on Chebyshev nodes (max relative error 2.2e-4, below
+// the fp16 rounding the probabilities get next, 4.9e-4); n is added to the
 // exponent field.  x < -125 gives exactly 0 (masked scores are -inf).
 __device__ __forceinline__ float exp2_poly(float x) {
   const float xc = fmaxf(x, -125.0f);
@@ -165,8 +165,7 @@ __device__ __forceinline__ void tmem_ld_32x32_x16(uint32_t taddr, uint32_t (&r)[
 // the P chunks this row already wrote are rescaled in TMEM -- warp-uniformly, rare
 // after the first chunk), so every P stays <= 2^8 in fp16.  Afterwards O (if the offset
 // moved since the previous block: the PV of that block is complete, the commit that
-// released this S covers it) and the running sum follow the offset.  The row sum uses
-// the rounded probabilities that the PV product sees.
+// released this S covers it) and the running sum follow the offset.
 template <bool kMask, int D>
 __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_col, int key0,
                                                     int row, int S, float scale_log2, bool has_o,
@@ -221,14 +220,17 @@ __device__ __forceinline__ void attn2_softmax_block(uint32_t s_col, uint32_t o_c
     for (int e = 0; e < 16; ++e) {
       const float s0 = __uint_as_float(r[2 * e]);
       const float s1 = __uint_as_float(r[2 * e + 1]);
-      // half of the pairs on MUFU.EX2, half on the FMA pipe (balances the two units)
+      // 13 of 16 pairs on MUFU.EX2 (one issue slot, 8 cycles of its pipe per warp), 3 on the
+      // FMA-pipe cubic (~11 issue slots): with two softmax warps per SM sub-partition this
+      // balances the MUFU pipe against instruction issue (a 50/50 split is issue-bound)
       const float a0 = fmaf(s0, scale_log2, -m_cur), a1 = fmaf(s1, scale_log2, -m_cur);
-      const float p0 = (e & 1) ? exp2_poly(a0) : ex2_approx(a0);
-      const float p1 = (e & 1) ? exp2_poly(a1) : ex2_approx(a1);
-      // P in fp16 (P <= 2^kRescaleLog2 = 256: far inside its range; 8x finer than bf16)
+      const bool poly = (e % 5) == 4;
+      const float p0 = poly ? exp2_poly(a0) : ex2_approx(a0);
+      const float p1 = poly ? exp2_poly(a1) : ex2_approx(a1);
+      // P in fp16 (P <= 2^kRescaleLog2 = 256: far inside its range; 8x finer than bf16);
+      // the row sum takes the fp32 values (one rounding of 2^-11 per term, unbiased)
       pk[e] = pack_f16x2(p0, p1);
-      const float2 pr = unpack_f16x2(pk[e]);
-      r8[e & 7] += pr.x + pr.y;
+      r8[e & 7] += p0 + p1;
     }
     tmem_st_32x32_x16(s_col + c * 16, pk);
     if (c + 1 < 4) tmem_wait_ld();
