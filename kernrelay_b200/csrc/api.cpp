@@ -850,22 +850,25 @@ KRB_EXPORT int krb_relay_plan(int S, int H, int tiles, int k, int rank, int bn, 
     } else {
       cudaGetLastError();
     }
-    const krb::TileSched ts = krb::relay_tile_sched(S, H, tiles, bn, grid);
+    const int cg = krb::relay_uses_pairs(S, tiles, bn) ? 2 : 1;
+    const krb::TileSched ts = krb::relay_tile_sched(S, H, tiles, bn, grid, cg);
     const int R = S / tiles, Rk = R / k;
     std::ostringstream os;
     os << "{\"R\":" << R << ",\"Rk\":" << Rk << ",\"grid\":" << grid << ",\"bn\":" << bn
+       << ",\"cta_group\":" << cg
        << ",\"bn2\":" << ts.bn2 << ",\"p1\":" << ts.p1 << ",\"total\":" << ts.total()
        << ",\"nseg\":" << (H + 255) / 256 << ",\"band_tiles\":[";
     for (int t = 0; t < tiles; ++t) os << (t ? "," : "") << ts.band_tiles(t);
-    // the consumer's targets per run and layer: k = 1 every GEMM tile of row tile t; k > 1
-    // one forwarded signal per (row tile, source) and per (row tile, owner)
+    // the consumer's targets per run and layer: k = 1 every CTA's share of the GEMM tiles of
+    // row tile t; k > 1 one forwarded signal per (row tile, source) and per (row tile, owner)
     os << "],\"rs_expect\":[";
-    for (int t = 0; t < tiles; ++t) os << (t ? "," : "") << (k == 1 ? ts.band_tiles(t) : 1);
+    for (int t = 0; t < tiles; ++t) os << (t ? "," : "") << (k == 1 ? cg * ts.band_tiles(t) : 1);
     os << "],\"ag_expect\":" << (k == 1 ? 0 : 1) << ",\"tiles\":[";
     for (int i = 0; i < ts.total(); ++i) {
       int mb, n0, w;
       ts.tile(i, mb, n0, w);
-      os << (i ? "," : "") << "[" << mb << "," << n0 << "," << w << "]";
+      // [first 128-row block, 128-row blocks, first column, width]
+      os << (i ? "," : "") << "[" << mb * cg << "," << cg << "," << n0 << "," << w << "]";
     }
     os << "],\"blocks\":[";
     for (int b = 0; b < S / 128; ++b) {

@@ -12,20 +12,23 @@
 namespace krb {
 
 // configuration variant of a plain GEMM: fp32 outputs stage in fp32, the rest in 2 bytes;
-// eight epilogue warps for the QKV and fp32-output epilogues, four for the others
-template <int MODE>
+// one-CTA tiles: eight epilogue warps for the QKV and fp32-output epilogues, four for the
+// others; CTA pairs (PAIR): 256-row tiles, eight epilogue warps
+template <int MODE, bool PAIR>
 constexpr int plain_cfg() {
+  if (PAIR) return MODE == kEpiStoreF32 ? kCfgPairF32 : kCfgPair;
   return MODE == kEpiStoreF32 ? kCfgPlainF32 : MODE == kEpiQkvRope ? kCfgPlain : kCfgPlain4;
 }
 
 // F16: fp16 operands and 2-byte outputs (bf16 otherwise); fp32 accumulation either way.
-// Warps: TMA producer, MMA issuer, 4 or 8 epilogue warps.
-template <int BN, int MODE, bool F16>
-__global__ void __launch_bounds__(GemmCfg<BN, plain_cfg<MODE>()>::kThreads, 1)
+// Warps: TMA producer, MMA issuer, 4 or 8 epilogue warps.  PAIR: launched in clusters of
+// two CTAs (cta_group::2 MMAs on 256-row tiles).
+template <int BN, int MODE, bool F16, bool PAIR>
+__global__ void __launch_bounds__(GemmCfg<BN, plain_cfg<MODE, PAIR>()>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                 const __grid_constant__ CUtensorMap tb2, TileSched ts, int M, int K, EpiArgs ea,
                 uint32_t *status) {
-  constexpr int V = plain_cfg<MODE>();
+  constexpr int V = plain_cfg<MODE, PAIR>();
   using C = GemmCfg<BN, V>;
   extern __shared__ uint8_t smem_raw[];
   const GemmSmemView<BN, V> s = GemmSmemView<BN, V>::carve(smem_raw);
@@ -148,18 +151,29 @@ static int pick_band(long M, long N, long K, int num_m) {
   return (a_bytes > 48e6 && b_bytes < 24e6) ? 1 : num_m;
 }
 
+// CTA pairs (cta_group::2) for every plain GEMM whose 128-row blocks pair up (an even
+// count); KRB_GEMM_PAIR=0 keeps one-CTA tiles.
+static bool pairs_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("KRB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // The plain GEMMs with a per-tile column layout (store / fp32 store) take the two-phase
 // tail re-cut (TileSched); the SiLU-gated (B interleaved per BN block) and QKV (heads
 // per tile) epilogues keep one tile width.
-template <int BN, int MODE, bool F16>
-static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const void *B, long ldb,
-                        int M, int n_b_rows, int K, const EpiArgs &ea, int grid_limit,
-                        uint32_t *status, cudaStream_t stream) {
-  using C = GemmCfg<BN, plain_cfg<MODE>()>;
+template <int BN, int MODE, bool F16, bool PAIR>
+static void launch_gemm_cfg(const CUtensorMap &ta, const void *B, long ldb, int M, int n_b_rows,
+                            int K, const EpiArgs &ea, int grid_limit, uint32_t *status,
+                            cudaStream_t stream) {
+  using C = GemmCfg<BN, plain_cfg<MODE, PAIR>()>;
+  constexpr int CG = C::kCG;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static bool configured[64] = {false};
-  auto kern = gemm_kernel<BN, MODE, F16>;
+  auto kern = gemm_kernel<BN, MODE, F16, PAIR>;
   if (!configured[dev & 63]) {
     KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   int(C::kSmemBytes)));
@@ -167,40 +181,63 @@ static void launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const void
   }
   const int num_m = (M + kBM - 1) / kBM;
   const int band = pick_band(M, n_b_rows, K, num_m);
-  int grid = std::min(num_m * ((n_b_rows + BN - 1) / BN), sm_count(dev));
-  if (grid_limit > 0) grid = std::min(grid, grid_limit);
+  // tile rows of CG 128-row blocks; one wave = the CTA groups that fit on the SMs
+  const int rows = num_m / CG, band_rows = std::max(1, band / CG);
+  int groups = std::min(rows * ((n_b_rows + BN - 1) / BN), sm_count(dev) / CG);
+  if (grid_limit > 0) groups = std::min(groups, std::max(1, grid_limit / CG));
   constexpr bool two_phase = MODE == kEpiStore || MODE == kEpiStoreF32;
-  const TileSched ts = TileSched::make(num_m, n_b_rows, BN, band, grid, two_phase);
-  const CUtensorMap tb2 = ts.bn2 != BN ? make_tmap_2d_bf16(B, n_b_rows, K, ldb, ts.bn2, kBK) : tb;
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(ta, tb, tb2, ts, M, K, ea, status);
-  KRB_CUDA(cudaGetLastError());
+  const TileSched ts = TileSched::make(rows, n_b_rows, BN, band_rows, groups, two_phase, 16 * CG);
+  // B boxes: the tile's rows of B, split between the pair's CTAs
+  const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, BN / CG, kBK);
+  const CUtensorMap tb2 =
+      ts.bn2 != BN ? make_tmap_2d_bf16(B, n_b_rows, K, ldb, ts.bn2 / CG, kBK) : tb;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups * CG);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KRB_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, ts, M, K, ea, status));
 }
 
-// B tensor map for one tile width and the launch of MODE for element type T
+template <int BN, int MODE, bool F16>
+static void launch_gemm(const CUtensorMap &ta, const void *B, long ldb, int M, int n_b_rows,
+                        int K, const EpiArgs &ea, int grid_limit, uint32_t *status,
+                        cudaStream_t stream) {
+  const int num_m = (M + kBM - 1) / kBM;
+  if (pairs_enabled() && num_m % 2 == 0 && num_m >= 2)
+    launch_gemm_cfg<BN, MODE, F16, true>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
+                                         stream);
+  else
+    launch_gemm_cfg<BN, MODE, F16, false>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
+                                          stream);
+}
+
+// The launch of MODE for element type T at tile width bn
 template <int MODE, typename T>
 static void dispatch_bn(int bn, const CUtensorMap &ta, const T *B, long ldb, int M, int n_b_rows,
                         int K, const EpiArgs &ea, int grid_limit, uint32_t *status,
                         cudaStream_t stream, const char *what) {
   constexpr bool F16 = ActFmt<T>::f16;
   switch (bn) {
-    case 256: {
-      const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 256, kBK);
-      launch_gemm<256, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
+    case 256:
+      launch_gemm<256, MODE, F16>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
       break;
-    }
     case 224:
       if constexpr (MODE != kEpiSiluMul && MODE != kEpiQkvRope) {
-        const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 224, kBK);
-        launch_gemm<224, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
-                                    stream);
+        launch_gemm<224, MODE, F16>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
         break;
       }
       [[fallthrough]];
     case 128:
       if (bn == 128) {
-        const CUtensorMap tb = make_tmap_2d_bf16(B, n_b_rows, K, ldb, 128, kBK);
-        launch_gemm<128, MODE, F16>(ta, tb, B, ldb, M, n_b_rows, K, ea, grid_limit, status,
-                                    stream);
+        launch_gemm<128, MODE, F16>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
         break;
       }
       [[fallthrough]];

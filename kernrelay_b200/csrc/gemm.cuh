@@ -49,29 +49,43 @@ enum EpiMode : int {
 // the exposed epilogue of the last tile of GEMMs with two tiles per SM (QKV with its
 // RoPE epilogue, o_proj's fp32 output: 3-5 % faster on B200); the SiLU-gated and plain
 // stores, with many tiles per SM, ran 1-2 % faster with four.
-constexpr int kCfgPlain = 0, kCfgRelay = 1, kCfgPlainF32 = 2, kCfgPlain4 = 3;
+//   kCfgPair / kCfgPairF32 / kCfgPairRelay: the same three roles on CTA PAIRS (clusters of
+//                2, cta_group::2): 256-row tiles, each CTA holding 128 rows of A and BN/2
+//                rows of B in its stages, the even CTA issuing the M=256 MMA for both.  Per
+//                SM a k-block then moves A 16 KB + B BN*64 B through shared memory (TMA
+//                write + MMA read) for the same MMA time as a one-CTA 128 x BN tile, which
+//                moves A 16 KB + B BN*128 B: the one-CTA 128x256 tile needs ~190 B/clk of
+//                shared-memory traffic at the full MMA rate, the pair ~125 B/clk.
+constexpr int kCfgPlain = 0, kCfgRelay = 1, kCfgPlainF32 = 2, kCfgPlain4 = 3, kCfgPair = 4,
+              kCfgPairF32 = 5, kCfgPairRelay = 6;
 
 template <int BN, int V = kCfgPlain>
 struct GemmCfg {
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "UMMA N for M=128");
-  static constexpr int kEpiWarps = (V == kCfgRelay || V == kCfgPlain4) ? 4 : 8;
+  static constexpr int kCG = V >= kCfgPair ? 2 : 1;  // CTAs per MMA
+  static constexpr bool kRelay = V == kCfgRelay || V == kCfgPairRelay;
+  static_assert(kCG == 1 || (BN / 2) % 16 == 0, "pair: B halves of whole swizzle atoms");
+  static constexpr int kEpiWarps = (kRelay || V == kCfgPlain4) ? 4 : 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr uint32_t kABytes = kBM * kBK * 2;
-  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kBBytes = (BN / kCG) * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // epilogue staging per warp: 32 rows of 32 fp32 padded to 36 (conflict-free
   // row-wise writes and column-block reads), or 32 rows of 32 2-byte values padded to
   // 80 bytes (kCfgPlain)
   static constexpr uint32_t kStageRow = 36;
   static constexpr uint32_t kStage2Pitch = 80;
-  static constexpr bool kStage2 = V == kCfgPlain || V == kCfgPlain4;
+  static constexpr bool kStage2 = V == kCfgPlain || V == kCfgPlain4 || V == kCfgPair;
   static constexpr uint32_t kWarpEpiBytes = kStage2 ? 32 * kStage2Pitch : 32 * kStageRow * 4;
   static constexpr uint32_t kEpiBytes = kEpiWarps * kWarpEpiBytes;
   // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
   // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
-  static constexpr uint32_t kMaxStages = (BN >= 224) ? 4 : 6;
+  static constexpr uint32_t kMaxStages = (kCG == 2 || BN < 224) ? 6 : 4;
   static constexpr uint32_t kBarBytesMax = (2 * 6 + 4) * 8 + 16 + 64;
-  static constexpr uint32_t kFit = (232448u - kEpiBytes - kBarBytesMax - 1024u) / kStageBytes;
+  // the relay's pair row buffers (up to H = 4096) and their barriers sit behind this layout
+  static constexpr uint32_t kReserve = V == kCfgPairRelay ? 4u * 4096u * 2u + 256u : 0u;
+  static constexpr uint32_t kFit =
+      (232448u - kReserve - kEpiBytes - kBarBytesMax - 1024u) / kStageBytes;
   static constexpr uint32_t kStages = V == kCfgRelay ? kMaxStages
                                                      : (kFit < kMaxStages ? kFit : kMaxStages);
   static constexpr uint32_t kTileBytes = kStages * kStageBytes;
@@ -118,6 +132,9 @@ struct GemmSmemView {
 
 // One-time CTA setup: barriers by thread 0, TMEM by warp 1.  Ends with
 // __syncthreads so every role sees the TMEM base address.
+// Pairs: the leader's tempty counts the epilogue threads of BOTH CTAs, and a cluster
+// barrier makes every barrier initialisation visible to the peer before any remote arrive
+// or TMA completion; warp 1 of both CTAs allocates the pair's TMEM together.
 template <int BN, int RELAY = 0>
 __device__ __forceinline__ void gemm_setup(const GemmSmemView<BN, RELAY> &s, int epi_threads) {
   using C = GemmCfg<BN, RELAY>;
@@ -129,17 +146,23 @@ __device__ __forceinline__ void gemm_setup(const GemmSmemView<BN, RELAY> &s, int
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tfull[i], 1);
-      mbar_init(&s.tempty[i], epi_threads);
+      mbar_init(&s.tempty[i], C::kCG * epi_threads);
     }
     *s.abort = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(s.tmem_slot, C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (C::kCG == 2) {
+      tmem_alloc_pair(s.tmem_slot, C::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(s.tmem_slot, C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (C::kCG == 2) cluster_sync();
   tc_fence_after();
 }
 
@@ -148,9 +171,39 @@ __device__ __forceinline__ void gemm_teardown(const GemmSmemView<BN, RELAY> &s) 
   using C = GemmCfg<BN, RELAY>;
   tc_fence_before();
   __syncthreads();
+  // pairs: neither CTA leaves (or frees TMEM) while the other may still signal its
+  // barriers or the leader's MMAs may still touch its shared memory or TMEM
+  if constexpr (C::kCG == 2) cluster_sync();
   tc_fence_after();
-  if ((threadIdx.x >> 5) == 1) tmem_dealloc(*s.tmem_slot, C::kTmemCols);
+  if ((threadIdx.x >> 5) == 1) {
+    if constexpr (C::kCG == 2)
+      tmem_dealloc_pair(*s.tmem_slot, C::kTmemCols);
+    else
+      tmem_dealloc(*s.tmem_slot, C::kTmemCols);
+  }
 }
+
+// Tile loop of this CTA: one-CTA kernels step over CTAs, pairs over clusters (both CTAs
+// of a cluster take the same tiles).  row_block(mb) = this CTA's 128-row block of tile row
+// mb (tile rows are 256 rows for pairs).
+template <int CG>
+struct TileWalk {
+  int first, step, rank;
+  __device__ __forceinline__ static TileWalk make() {
+    TileWalk w;
+    if constexpr (CG == 2) {
+      w.first = int(cluster_id_x());
+      w.step = int(nclusters_x());
+      w.rank = int(cluster_ctarank());
+    } else {
+      w.first = blockIdx.x;
+      w.step = gridDim.x;
+      w.rank = 0;
+    }
+    return w;
+  }
+  __device__ __forceinline__ int row_block(int mb) const { return CG == 2 ? 2 * mb + rank : mb; }
+};
 
 // ---- warp 0, one thread: TMA producer
 template <int BN, int RELAY = 0>
@@ -163,11 +216,15 @@ __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, 
   uint32_t phase = 0;
   long issued = 0;
   const uint64_t pol_a = l2_policy_evict_last();
-  for (int t = blockIdx.x; t < ts.total() && !*s.abort; t += gridDim.x) {
+  const TileWalk<C::kCG> w = TileWalk<C::kCG>::make();
+  // pairs: every load of both CTAs completes on the leader's full[stage]
+  const uint32_t leader_full = C::kCG == 2 ? mapa_shared(&s.full[0], 0) : 0u;
+  for (int t = w.first; t < ts.total() && !*s.abort; t += w.step) {
     int mb, n0, bn;
     ts.tile(t, mb, n0, bn);
     const bool narrow = bn != BN;  // phase-2 tile: B rows through the bn2-row tensor map
-    const uint32_t stage_tx = C::kABytes + uint32_t(bn) * kBK * 2;
+    // bytes of one stage: this CTA's A rows and B rows (pairs: both CTAs' on the leader)
+    const uint32_t stage_tx = C::kCG * (C::kABytes + uint32_t(bn / C::kCG) * kBK * 2);
     for (int kb = 0; kb < nkb; ++kb) {
       if (!mbar_wait(&s.empty[stage], phase ^ 1, kMbarLimitNs) || *s.abort) {
         report_status(status, kStatusTmaWait);
@@ -177,9 +234,17 @@ __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, 
       {
         uint8_t *a = s.tiles + stage * C::kStageBytes;
         uint8_t *b = a + C::kABytes;
-        mbar_arrive_expect_tx(&s.full[stage], stage_tx);
-        tma_load_2d_hint(a, ta, &s.full[stage], kb * kBK, mb * kBM, pol_a);
-        tma_load_2d(b, narrow ? tb2 : tb, &s.full[stage], kb * kBK, n0);
+        if constexpr (C::kCG == 2) {
+          if (w.rank == 0) mbar_arrive_expect_tx(&s.full[stage], stage_tx);
+          const uint32_t bar = leader_full + 8u * uint32_t(stage);
+          tma_load_2d_pair(a, ta, bar, kb * kBK, w.row_block(mb) * kBM, pol_a);
+          tma_load_2d_pair(b, narrow ? tb2 : tb, bar, kb * kBK, n0 + w.rank * (bn / 2),
+                           l2_policy_evict_first());
+        } else {
+          mbar_arrive_expect_tx(&s.full[stage], stage_tx);
+          tma_load_2d_hint(a, ta, &s.full[stage], kb * kBK, mb * kBM, pol_a);
+          tma_load_2d(b, narrow ? tb2 : tb, &s.full[stage], kb * kBK, n0);
+        }
       }
       ++issued;
       if (++stage == C::kStages) {
@@ -190,7 +255,10 @@ __device__ __forceinline__ void gemm_producer(const GemmSmemView<BN, RELAY> &s, 
   }
 drain:
   // Make sure no TMA write is still in flight into this CTA's shared memory
-  // before the CTA can exit: wait on the last phase armed for each stage.
+  // before the CTA can exit: wait on the last phase armed for each stage.  (Pairs: the
+  // leader's full barriers count both CTAs' bytes, so the leader waits for both; the
+  // peer is held at the teardown's cluster barrier until then.)
+  if (C::kCG == 2 && w.rank != 0) return;
   {
     const long n = issued < C::kStages ? issued : C::kStages;
     int st = stage;
@@ -213,14 +281,17 @@ template <int BN, int RELAY = 0, bool F16 = false>
 __device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const TileSched &ts,
                                          int K, uint32_t *status) {
   using C = GemmCfg<BN, RELAY>;
-  constexpr uint32_t idesc1 = F16 ? idesc_f16_f32(kBM, BN) : idesc_bf16_f32(kBM, BN);
-  const uint32_t idesc2 = F16 ? idesc_f16_f32(kBM, ts.bn2) : idesc_bf16_f32(kBM, ts.bn2);
+  constexpr int kM = kBM * C::kCG;  // pairs: one M = 256 MMA for both CTAs
+  constexpr uint32_t idesc1 = F16 ? idesc_f16_f32(kM, BN) : idesc_bf16_f32(kM, BN);
+  const uint32_t idesc2 = F16 ? idesc_f16_f32(kM, ts.bn2) : idesc_bf16_f32(kM, ts.bn2);
   const uint32_t tmem = *s.tmem_slot;
   const int nkb = (K + kBK - 1) / kBK;
   int stage = 0;
   uint32_t phase = 0;
   int it = 0;
-  for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
+  const TileWalk<C::kCG> w = TileWalk<C::kCG>::make();
+  if (w.rank != 0) return;  // pairs: the leader issues every MMA
+  for (int t = w.first; t < ts.total(); t += w.step, ++it) {
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
     const uint32_t idesc = t < ts.p1 ? idesc1 : idesc2;
@@ -244,16 +315,27 @@ __device__ __forceinline__ void gemm_mma(const GemmSmemView<BN, RELAY> &s, const
       const uint32_t b = a + C::kABytes;
 #pragma unroll
       for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
-        umma_bf16(d, sdesc_kmajor_sw128(a + kk * kUmmaK * 2),
-                  sdesc_kmajor_sw128(b + kk * kUmmaK * 2), idesc, (kb | kk) != 0);
+        if constexpr (C::kCG == 2)
+          umma_pair(d, sdesc_kmajor_sw128(a + kk * kUmmaK * 2),
+                    sdesc_kmajor_sw128(b + kk * kUmmaK * 2), idesc, (kb | kk) != 0);
+        else
+          umma_bf16(d, sdesc_kmajor_sw128(a + kk * kUmmaK * 2),
+                    sdesc_kmajor_sw128(b + kk * kUmmaK * 2), idesc, (kb | kk) != 0);
       }
-      umma_commit(&s.empty[stage]);
+      // pairs: the stage is free in both CTAs once these MMAs completed
+      if constexpr (C::kCG == 2)
+        umma_commit_pair(&s.empty[stage], 0x3);
+      else
+        umma_commit(&s.empty[stage]);
       if (++stage == C::kStages) {
         stage = 0;
         phase ^= 1;
       }
     }
-    umma_commit(&s.tfull[acc]);
+    if constexpr (C::kCG == 2)
+      umma_commit_pair(&s.tfull[acc], 0x3);  // both CTAs' epilogues
+    else
+      umma_commit(&s.tfull[acc]);
     if (!ok) break;
   }
 }
@@ -574,9 +656,14 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
   uint8_t *stage_raw = reinterpret_cast<uint8_t *>(s.epi) + (warp - 2) * C::kWarpEpiBytes;
   float *stage = reinterpret_cast<float *>(stage_raw);
   int it = 0;
-  for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
+  const TileWalk<C::kCG> w = TileWalk<C::kCG>::make();
+  // the accumulator is handed back to the MMA issuer: the leader's tempty (pairs: both
+  // CTAs' epilogue threads arrive there)
+  const uint32_t leader_tempty = C::kCG == 2 ? mapa_shared(&s.tempty[0], 0) : 0u;
+  for (int t = w.first; t < ts.total(); t += w.step, ++it) {
     int mb, n0, bn;
     ts.tile(t, mb, n0, bn);
+    mb = w.row_block(mb);
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
     if (!mbar_wait(&s.tfull[acc], acc_phase, kMbarLimitNs) || *s.abort) {
@@ -611,7 +698,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
           static_assert(C::kStage2, "2-byte staging");
           epi2_store<F16>(stage_raw, v, ea.bias, out_row, col0, valid);
         } else {
-          static_assert(V == kCfgPlainF32, "fp32 staging");
+          static_assert(!C::kStage2, "fp32 staging");
           epi_stage_put(stage, v);
           epi_stage_store_f32(stage, ea.out_f32, ea.ldc, row0, M, col0, valid);
         }
@@ -636,7 +723,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmSmemView<BN, V> &s, cons
       }
     }
     tc_fence_before();
-    mbar_arrive(&s.tempty[acc]);
+    if constexpr (C::kCG == 2)
+      mbar_arrive_cluster(leader_tempty + 8u * uint32_t(acc));
+    else
+      mbar_arrive(&s.tempty[acc]);
   }
 }
 

@@ -247,8 +247,10 @@ class Engine {
 template <typename T>
 void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
                       const RelayArgs &ra, cudaStream_t stream);
-// the relay GEMM's tile schedule for `grid` CTAs (row tile t = band t)
-TileSched relay_tile_sched(int S, int H, int T, int bn, int grid);
+// the relay GEMM's tile schedule for `grid` CTAs (row tile t = band t; cta_group 2: CTA
+// pairs on 256-row tiles), and whether the relay runs its GEMM on CTA pairs
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid, int cta_group);
+bool relay_uses_pairs(int S, int T, int bn);
 
 // device-side synthesis / fill (synth.cu)
 void synth_normal_device(__nv_bfloat16 *dst, size_t n, uint64_t key, double std_, double mean,

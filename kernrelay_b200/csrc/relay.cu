@@ -52,7 +52,8 @@
 
 namespace krb {
 
-TileSched relay_tile_sched(int S, int H, int T, int bn, int grid);  // bottom of this file
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid,
+                           int cta_group);  // bottom of this file
 
 constexpr int kRelayWarp0 = 6;                      // warps 0..5: GEMM roles
 constexpr int kRelayWarps = 8;                      // consumer warps per CTA
@@ -117,10 +118,10 @@ __device__ __forceinline__ uint4 pack8f(const float *f) {
 // epilogue can index them by owner rank without a local-memory copy.
 __shared__ uint8_t *g_peer_base[kMaxRanks];
 
-template <int BN, bool F16>
-__device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s,
+template <int BN, int V, bool F16>
+__device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, V> &s,
                                                     const TileSched &ts, const RelayArgs &ra) {
-  using C = GemmCfg<BN, 1>;
+  using C = GemmCfg<BN, V>;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int quad = warp & 3;
@@ -129,9 +130,12 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
   float *stage = s.epi + (warp - 2) * 32 * C::kStageRow;
   uint64_t fence_ns = 0, fence_cnt = 0, fence_max = 0;  // trace only
   int it = 0;
-  for (int t = blockIdx.x; t < ts.total(); t += gridDim.x, ++it) {
+  const TileWalk<C::kCG> w = TileWalk<C::kCG>::make();
+  const uint32_t leader_tempty = C::kCG == 2 ? mapa_shared(&s.tempty[0], 0) : 0u;
+  for (int t = w.first; t < ts.total(); t += w.step, ++it) {
     int mb, n0, bn;
     ts.tile(t, mb, n0, bn);
+    mb = w.row_block(mb);  // this CTA's 128 rows of the tile
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
     // collective decision: the four epilogue warps meet at named barrier 1 below,
@@ -169,7 +173,11 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, 1> &s
         epi_stage_store_bf16<F16>(stage, part_row, nullptr, col0, valid);
     }
     tc_fence_before();
-    mbar_arrive(&s.tempty[acc]);  // accumulator free for the next tile
+    // accumulator free for the next tile (pairs: on the leader, for both CTAs)
+    if constexpr (C::kCG == 2)
+      mbar_arrive_cluster(leader_tempty + 8u * uint32_t(acc));
+    else
+      mbar_arrive(&s.tempty[acc]);
     named_bar_sync(1, 128);       // all four epilogue warps' stores are issued
     if (warp == 2 && lane == 0) {
       const uint64_t f0 = ra.trace ? globaltimer_ns() : 0;
@@ -457,7 +465,8 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
     // GEMM tiles are released; sum_out = resid + partial in place, then RMSNorm
     for (int t = 0; t < ra.T; ++t) {
       const bool ok =
-          wait_all_sources(ra, rs_cnt_base, t, seq * uint32_t(ts.band_tiles(t)), kStatusLocalWait,
+          wait_all_sources(ra, rs_cnt_base, t, seq * uint32_t(ra.cta_group * ts.band_tiles(t)),
+                           kStatusLocalWait,
                            timeout, flag_smem);
       if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
       if (!ok) {
@@ -744,7 +753,8 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra, const TileSche
   const int t = ag ? j - ra.T : j;
   const size_t tk = 2 * size_t(ra.T) * ra.k;
   const size_t done_line = ra.flag_off + (tk + 2 + (ag ? ra.T : 0) + t) * 128;
-  const uint32_t target = seq * (ag ? uint32_t(gridDim.x) : uint32_t(ts.band_tiles(t)));
+  const uint32_t target =
+      seq * (ag ? uint32_t(gridDim.x) : uint32_t(ra.cta_group * ts.band_tiles(t)));
   if (!wait_counter_geq(flag_ptr(ra.local_base, done_line), target, timeout)) {
     report_status(ra.status, kStatusLocalWait);
     return;
@@ -761,14 +771,14 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra, const TileSche
   }
 }
 
-template <int BN, int KR, bool F16>
+template <int BN, int KR, bool F16, int V>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
                       const __grid_constant__ CUtensorMap tb,
                       const __grid_constant__ CUtensorMap tb2, TileSched ts,
                       const __grid_constant__ RelayArgs ra) {
   extern __shared__ uint8_t smem_raw[];
-  const GemmSmemView<BN, 1> s = GemmSmemView<BN, 1>::carve(smem_raw);
+  const GemmSmemView<BN, V> s = GemmSmemView<BN, V>::carve(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -777,7 +787,7 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
     tma_prefetch_desc(&tb2);
   }
   // relay staging: kRelayWarps/2 pair buffers of H bf16, then their mbarriers
-  using C = GemmCfg<BN, 1>;
+  using C = GemmCfg<BN, V>;
   uint8_t *stage_base = s.tiles + ((C::kTileBytes + C::kEpiBytes + C::kBarBytes + 127) & ~127u);
   if (threadIdx.x == 0) {
 #pragma unroll
@@ -788,29 +798,29 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
       for (int i = 0; i < kRelayWarps / 2; ++i) mbar_init(&bars[i], 1);
     }
   }
-  gemm_setup<BN, 1>(s, 128);  // its barrier-init fence and __syncthreads cover the above
+  gemm_setup<BN, V>(s, 128);  // its barrier-init fence and __syncthreads cover the above
   if (warp == 0) {
-    if (lane == 0) gemm_producer<BN, 1>(s, &ta, &tb, &tb2, ts, ra.K, ra.status);
+    if (lane == 0) gemm_producer<BN, V>(s, &ta, &tb, &tb2, ts, ra.K, ra.status);
   } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN, 1, F16>(s, ts, ra.K, ra.status);
+    if (lane == 0) gemm_mma<BN, V, F16>(s, ts, ra.K, ra.status);
   } else if (warp < kRelayWarp0) {
-    relay_push_epilogue<BN, F16>(s, ts, ra);
+    relay_push_epilogue<BN, V, F16>(s, ts, ra);
   } else if (warp < kSignalWarp) {
     relay_consumer<KR, F16>(ra, ts, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
                             stage_base);
   } else if (lane == 0) {
     relay_signal(ra, ts);
   }
-  gemm_teardown<BN, 1>(s);
+  gemm_teardown<BN, V>(s);
 }
 
 // ------------------------------------------------------------------ host side
 
 // dynamic shared memory of the relay kernel: the GEMM pipeline, plus (bulk) the
 // pair row buffers and their mbarriers behind it
-template <int BN>
+template <int BN, int V>
 static size_t relay_smem_bytes(int H, bool bulk) {
-  using C = GemmCfg<BN, 1>;
+  using C = GemmCfg<BN, V>;
   if (!bulk) return C::kSmemBytes;
   return C::kSmemBytes + 128 + size_t(kRelayWarps / 2) * H * 2 + (kRelayWarps / 2) * 8;
 }
@@ -819,18 +829,30 @@ static size_t relay_smem_bytes(int H, bool bulk) {
 // opt-in dynamic shared memory left beside the kernel's static shared memory) and
 // every copy to be 16-byte aligned: rows (H bf16) and, for the reduce-scatter
 // units, segments of H/k columns.
-template <int BN>
+template <int BN, int V>
 static bool relay_bulk_fits(int H, int k, size_t dyn_limit) {
-  if (relay_smem_bytes<BN>(H, true) > dyn_limit) return false;
+  if (relay_smem_bytes<BN, V>(H, true) > dyn_limit) return false;
   if ((H * 2) % 16) return false;
   if (k > 1 && (H % k || (H / k) % 8)) return false;
   return true;
 }
 
-template <int BN, int KR, bool F16>
+// The down GEMM runs on CTA pairs (256-row tiles, cta_group::2) when every row tile is a
+// whole number of 256-row blocks and the tile width splits into two B halves of whole
+// 16-row UMMA blocks; KRB_GEMM_PAIR=0 keeps one-CTA tiles.
+bool relay_uses_pairs(int S, int T, int bn) {
+  static const bool on = [] {
+    const char *e = std::getenv("KRB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on && (bn == 256 || bn == 224) && (S / T) % 256 == 0;
+}
+
+template <int BN, int KR, bool F16, int V>
 static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
                          const RelayArgs &ra_in, bool want_bulk, int grid, cudaStream_t stream) {
-  auto kern = relay_down_kernel<BN, KR, F16>;
+  using C = GemmCfg<BN, V>;
+  auto kern = relay_down_kernel<BN, KR, F16, V>;
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   static size_t dyn_limit[64] = {0};
@@ -844,24 +866,30 @@ static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
     dyn_limit[dev & 63] = lim;
   }
   RelayArgs ra = ra_in;
-  ra.bulk = (want_bulk && relay_bulk_fits<BN>(ra.H, ra.k, dyn_limit[dev & 63])) ? 1 : 0;
-  const size_t smem = relay_smem_bytes<BN>(ra.H, ra.bulk != 0);
+  ra.cta_group = C::kCG;
+  ra.bulk = (want_bulk && relay_bulk_fits<BN, V>(ra.H, ra.k, dyn_limit[dev & 63])) ? 1 : 0;
+  const size_t smem = relay_smem_bytes<BN, V>(ra.H, ra.bulk != 0);
   if (smem > dyn_limit[dev & 63]) throw CudaError("relay: shared memory budget exceeded");
-  const TileSched ts = relay_tile_sched(ra.S, ra.H, ra.T, BN, grid);
-  const CUtensorMap tmb = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, BN, kBK);
-  const CUtensorMap tmb2 = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, ts.bn2, kBK);
+  const TileSched ts = relay_tile_sched(ra.S, ra.H, ra.T, BN, grid, C::kCG);
+  // B boxes: the tile's rows of W_down, split between the pair's CTAs
+  const CUtensorMap tmb = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, BN / C::kCG, kBK);
+  const CUtensorMap tmb2 = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, ts.bn2 / C::kCG, kBK);
   // cooperative: every CTA must be co-resident, because the relay warps wait
-  // for tiles produced by other CTAs of the same grid
+  // for tiles produced by other CTAs of the same grid; pairs: clusters of two
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kRelayThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = C::kCG;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = C::kCG == 2 ? 2 : 1;
   KRB_CUDA(cudaLaunchKernelEx(&cfg, kern, tma, tmb, tmb2, ts, ra));
 }
 
@@ -891,18 +919,28 @@ void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
       const char *e = std::getenv("KRB_RELAY_BULK");
       return !(e && e[0] == '0');
     }();
-    if constexpr (!F16) {
-      launch_relay<B, 1, false>(tma, w_down, ldb, ra, false, grid, stream);
-    } else {
-      const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
-      switch (ra.k) {
-        case 1: launch_relay<B, 1, true>(tma, w_down, ldb, ra, false, grid, stream); break;
-        case 2: launch_relay<B, 2, true>(tma, w_down, ldb, ra, want, grid, stream); break;
-        case 4: launch_relay<B, 4, true>(tma, w_down, ldb, ra, want, grid, stream); break;
-        case 8: launch_relay<B, 8, true>(tma, w_down, ldb, ra, want, grid, stream); break;
-        default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
+    auto with_cfg = [&](auto v_tag) {
+      constexpr int V = decltype(v_tag)::value;
+      if constexpr (!F16) {
+        launch_relay<B, 1, false, V>(tma, w_down, ldb, ra, false, grid, stream);
+      } else {
+        const bool want = bulk_env && ra.k > 1 && (!ra.direct || ra.k == 2);
+        switch (ra.k) {
+          case 1: launch_relay<B, 1, true, V>(tma, w_down, ldb, ra, false, grid, stream); break;
+          case 2: launch_relay<B, 2, true, V>(tma, w_down, ldb, ra, want, grid, stream); break;
+          case 4: launch_relay<B, 4, true, V>(tma, w_down, ldb, ra, want, grid, stream); break;
+          case 8: launch_relay<B, 8, true, V>(tma, w_down, ldb, ra, want, grid, stream); break;
+          default: throw CudaError("relay: rank count must be 1, 2, 4 or 8");
+        }
+      }
+    };
+    if constexpr (B == 256 || B == 224) {
+      if (relay_uses_pairs(ra.S, ra.T, B)) {
+        with_cfg(std::integral_constant<int, kCfgPairRelay>{});
+        return;
       }
     }
+    with_cfg(std::integral_constant<int, kCfgRelay>{});
   };
   switch (bn) {
     case 256: by_ranks(std::integral_constant<int, 256>{}); break;
@@ -945,8 +983,10 @@ uint8_t *relay_noalloc_scratch() {
 
 // The relay GEMM's tile schedule: one band per row tile (row tile t completes before t+1),
 // the two-phase tail re-cut when the tiles need between one and two waves of `grid` CTAs.
-TileSched relay_tile_sched(int S, int H, int T, int bn, int grid) {
-  return TileSched::make(S / kBM, H, bn, (S / T) / kBM, grid, true);
+// cta_group 2: tile rows of 256 over grid / 2 CTA pairs.
+TileSched relay_tile_sched(int S, int H, int T, int bn, int grid, int cta_group) {
+  const int rows = kBM * cta_group;
+  return TileSched::make(S / rows, H, bn, (S / T) / rows, grid / cta_group, true, 16 * cta_group);
 }
 
 }  // namespace krb

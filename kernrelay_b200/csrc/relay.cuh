@@ -101,6 +101,9 @@ struct RelayArgs {
   // every CTA adds 1 to ag_done[t] after storing its reduced rows (target: the grid)
   // and one signal thread forwards 1 to ag_cnt[t][rank] (target 1).  Targets scale
   // with the run epoch and layer (monotone counters).
+  // CTAs per GEMM tile (2: the down GEMM runs on CTA pairs with 256-row tiles; every CTA
+  // releases its 128 rows, so a row tile's target is cta_group x its GEMM tiles)
+  int cta_group;
   // 1: direct all-pull (every rank sums all k partials of every row inside its
   // Add+RMSNorm; one synchronisation per tile, (k-1) tiles over NVLink per rank);
   // 0: reduce-scatter + all-gather (2(k-1)/k tiles over NVLink, two synchronisations)

@@ -39,7 +39,10 @@ struct TileSched {
   static int cdiv(int a, int b) { return (a + b - 1) / b; }
 
   // host: one phase, or two when that shortens the GEMM
-  static TileSched make(int num_m, int N, int BN, int band, int grid, bool two_phase) {
+  // step: granularity of the phase-2 width (16; 32 for CTA pairs, whose B halves are
+  // whole 16-row UMMA blocks)
+  static TileSched make(int num_m, int N, int BN, int band, int grid, bool two_phase,
+                        int step = 16) {
     TileSched t{};
     t.num_m = num_m;
     t.N = N;
@@ -60,7 +63,7 @@ struct TileSched {
     const int b1 = p1 / per_band;
     const int c1 = ((p1 - b1 * per_band) / band) * BN;
     const int later = num_m / band - b1 - 1;
-    for (int w = 64; w < BN; w += 16) {
+    for (int w = 64; w < BN; w += step) {
       const int a = (b1 < num_m / band) ? cdiv(N - c1, w) * band : 0;
       const int b = cdiv(N, w) * band;
       if (a + later * b <= grid) {

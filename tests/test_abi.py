@@ -105,18 +105,20 @@ def test_relay_plan_counts(krlib, S, H, T, k, bn):
     assert p0["R"] == R and p0["Rk"] * k == R
     cover = {}
     per_band = [0] * T
-    for mb, n0, w in p0["tiles"]:
-        assert w % 16 == 0 and 0 <= n0 < H
+    cg = p0["cta_group"]
+    for mb, nblk, n0, w in p0["tiles"]:
+        assert w % (16 * cg) == 0 and 0 <= n0 < H and nblk == cg
         per_band[(mb * 128) // R] += 1
-        for c in range(n0, min(n0 + w, H), 16):
-            cover[(mb, c)] = cover.get((mb, c), 0) + 1
+        for b in range(mb, mb + nblk):
+            for c in range(n0, min(n0 + w, H), 16):
+                cover[(b, c)] = cover.get((b, c), 0) + 1
     assert len(cover) == (S // 128) * len(range(0, H, 16)) and set(cover.values()) == {1}
     assert per_band == p0["band_tiles"] and p0["total"] == len(p0["tiles"])
-    grid = p0["grid"]
+    groups = p0["grid"] // cg
     if p0["p1"] < p0["total"]:
-        assert p0["p1"] <= grid and p0["total"] - p0["p1"] <= grid and p0["bn2"] < bn
+        assert p0["p1"] <= groups and p0["total"] - p0["p1"] <= groups and p0["bn2"] < bn
     for j in range(k):
-        assert plans[j]["rs_expect"] == (p0["band_tiles"] if k == 1 else [1] * T)
+        assert plans[j]["rs_expect"] == ([cg * n for n in p0["band_tiles"]] if k == 1 else [1] * T)
         assert plans[j]["ag_expect"] == (0 if k == 1 else 1)
     owners = {}
     for b, (tile, j0, j1) in enumerate(p0["blocks"]):
@@ -126,14 +128,17 @@ def test_relay_plan_counts(krlib, S, H, T, k, bn):
         assert owners[t] == set(range(k)), t
 
 
-def test_relay_plan_two_phase_on_b200_7b(krlib):
-    """Qwen2.5-7B down_proj at S=2048, T=4, BN=224 on 148 SMs: 256 tiles of 128x224 (1.73
-    waves) become 148 phase-1 tiles plus 140 tiles of width 176 (1 + 176/224 tile times)."""
+def test_relay_plan_two_phase_on_b200_7b(krlib, monkeypatch):
+    """Qwen2.5-7B down_proj at S=2048, T=4, BN=224 on 148 SMs.  CTA pairs: 128 tiles of
+    256x224 on 74 pairs (1.73 waves) become 74 phase-1 tiles plus 64 of width 192.  One-CTA
+    tiles (KRB_GEMM_PAIR=0, read by a fresh library process): 256 tiles of 128x224 become
+    148 plus 140 of width 176."""
     p = krlib.relay_plan(2048, 3584, 4, 2, 0, 224)
     if p["grid"] != 148:
         pytest.skip("not a 148-SM device")
-    assert p["p1"] == 148 and p["bn2"] == 176 and p["total"] == 288
-    assert p["band_tiles"] == [64, 64, 20 + 56, 84]
+    assert p["cta_group"] == 2
+    assert p["p1"] == 74 and p["bn2"] == 192 and p["total"] == 138
+    assert p["band_tiles"] == [32, 32, 10 + 26, 38]
 
 
 def test_relay_plan_rejects_bad_shapes(krlib):
