@@ -81,6 +81,7 @@ class Dist:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
         self.backend = "nccl"
+        self.nvlink = None   # peer-copy measurement (rank 0's, shared after init)
 
     def init(self, backend: str | None = None, timeout_s: float | None = None):
         """One process group per job: NCCL on GPUs (the driver's contract); gloo is
@@ -128,6 +129,12 @@ class Dist:
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
+
+
+def pickle_bcast(d: Dist, obj):
+    """rank 0's object on every rank (json over the byte broadcast)"""
+    b = d.bcast_bytes(json.dumps(obj).encode() if d.rank == 0 else None)
+    return json.loads(b.decode())
 
 
 # ------------------------------------------------------------------ clocks
@@ -230,11 +237,12 @@ def relay_roofline_s(cfg, S, k, pk, nvlink_gbs):
 
 def measure_peer_gbs(d: Dist, nbytes: int = 1 << 30, reps: int = 8):
     """Peer-copy bandwidth GPU 0 -> GPU 1 and back (copy engines over NVLink), per
-    direction, measured by rank 0 before any engine exists (the other ranks wait at a
-    barrier).  Device events on the copying stream, after one warm-up copy."""
+    direction, measured by rank 0 before the process group exists (the other ranks are
+    still in its rendezvous, with no kernel of theirs on a GPU).  Device events on the
+    copying stream, after one warm-up copy; the best of two rounds per direction."""
     import torch
     gbs = None
-    if d.rank == 0 and torch.cuda.device_count() >= 2:
+    if d.rank == 0 and d.world > 1 and torch.cuda.device_count() >= 2:
         res = []
         for a, b in ((0, 1), (1, 0)):
             src = torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{a}")
@@ -242,22 +250,25 @@ def measure_peer_gbs(d: Dist, nbytes: int = 1 << 30, reps: int = 8):
             with torch.cuda.device(b):
                 s = torch.cuda.current_stream()
                 dst.copy_(src)
-                torch.cuda.synchronize(a)
-                torch.cuda.synchronize(b)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                for _ in range(reps):
-                    dst.copy_(src, non_blocking=True)
-                e1.record(s)
-                e1.synchronize()
-                res.append(nbytes * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+                best = 0.0
+                for _ in range(2):
+                    torch.cuda.synchronize(a)
+                    torch.cuda.synchronize(b)
+                    e0, e1 = (torch.cuda.Event(enable_timing=True),
+                              torch.cuda.Event(enable_timing=True))
+                    e0.record(s)
+                    for _ in range(reps):
+                        dst.copy_(src, non_blocking=True)
+                    e1.record(s)
+                    e1.synchronize()
+                    best = max(best, nbytes * reps / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+                res.append(best)
             torch.cuda.synchronize(a)
             del src, dst
         torch.cuda.empty_cache()
         gbs = {"gpu0_to_gpu1_gbs": round(res[0], 1), "gpu1_to_gpu0_gbs": round(res[1], 1),
                "per_direction_gbs": round(min(res), 1), "spec_gbs": NVLINK_SPEC_GBS,
-               "how": f"torch peer copy of {nbytes >> 20} MiB x {reps}, CUDA events"}
-    d.barrier()
+               "how": f"torch peer copy of {nbytes >> 20} MiB x {reps}, CUDA events, best of 2"}
     return gbs
 
 
@@ -441,7 +452,7 @@ def run_ours(args, d: Dist):
     S, N = args.seq, d.world
     mdir = model_dir(args.config, S, args.seed, d, args.layers)
     pk = peaks()
-    nvlink = measure_peer_gbs(d) if N > 1 else None
+    nvlink = d.nvlink if N > 1 else None
     nvlink_gbs = nvlink["per_direction_gbs"] if nvlink else NVLINK_FALLBACK_GBS
     clocks = Clocks(d.local) if d.rank == 0 else None
     split = run_mode(d, mdir, f"tp{N}_split", S, args.tiles, args.steps, args.warmup, True, clocks)
@@ -549,10 +560,12 @@ def _microdag_engine(d: Dist, mode: str, S: int, H: int, I: int, tiles: int, see
 
 
 def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
-    """K graph replays of one micro-DAG step, each bracketed by its own CUDA events on the
-    engine stream with an L2 flush (a 512 MiB device write) before it, outside the
-    bracket: at k >= 4 a rank's inputs and outputs fit in the 126 MB L2.  Returns the
-    mean over steps of the per-step maximum over ranks (ms)."""
+    """K steps of [L2 flush (a 512 MiB device write; at k >= 4 a rank's operands fit in the
+    126 MB L2), one micro-DAG step (graph replay)] back to back on the engine stream, timed
+    by CUDA events around the whole loop, minus K flushes alone timed the same way.  The
+    ranks stay in step without a host barrier per step (every relay step waits for its
+    peers), so a per-step flush does not shift the ranks against each other.  Returns the
+    per-step time, max over ranks (ms)."""
     import torch
     eng.run()
     eng.sync()
@@ -562,23 +575,31 @@ def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
     for _ in range(W):
         eng.run()
     eng.sync()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(K)]
-    torch.cuda.synchronize()
-    d.barrier()
-    if clocks:
-        clocks.start()
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     with torch.cuda.stream(stream):
+        # flush alone
+        torch.cuda.synchronize()
+        e[0].record(stream)
         for i in range(K):
             flush.fill_(i & 0xFF)
-            ev[i][0].record(stream)
+        e[1].record(stream)
+        torch.cuda.synchronize()
+        d.barrier()
+        if clocks:
+            clocks.start()
+        torch.cuda.synchronize()
+        d.barrier()
+        e[2].record(stream)
+        for i in range(K):
+            flush.fill_(i & 0xFF)
             eng.run()
-            ev[i][1].record(stream)
+        e[3].record(stream)
     eng.sync()
     torch.cuda.synchronize()
     d.barrier()
     ck = clocks.stop() if clocks else None
-    per = [d.max(a.elapsed_time(b)) for a, b in ev]
+    flush_ms = e[0].elapsed_time(e[1]) / K
+    step_ms = d.max(e[2].elapsed_time(e[3]) / K - flush_ms)
     st = eng.status()
     if st:
         raise RuntimeError(f"micro-DAG: device status {st}")
@@ -586,7 +607,7 @@ def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
     for _ in range(3):
         t = eng.stage_times()["stage_us"]
         stages = t if stages is None else {k: stages[k] + t[k] for k in t}
-    return statistics.mean(per), ck, {k: v / 3 for k, v in stages.items()}
+    return step_ms, ck, {k: v / 3 for k, v in stages.items()}, flush_ms
 
 
 def run_microdag(args, d: Dist):
@@ -599,7 +620,7 @@ def run_microdag(args, d: Dist):
     cfg = model_gen.CONFIGS[args.config]
     S, H, I, N = args.seq, cfg.H, cfg.I, d.world
     pk = peaks()
-    nvlink = measure_peer_gbs(d) if N > 1 else None
+    nvlink = d.nvlink if N > 1 else None
     nvlink_gbs = nvlink["per_direction_gbs"] if nvlink else NVLINK_FALLBACK_GBS
     clocks = Clocks(d.local) if d.rank == 0 else None
     res = {}
@@ -608,9 +629,9 @@ def run_microdag(args, d: Dist):
             continue
         eng = _microdag_engine(d, mode, S, H, I, args.tiles, args.seed)
         try:
-            ms, ck, st = time_microdag(d, eng, args.steps, args.warmup,
-                                       clocks if "split" in mode else None)
-            res[mode] = {"ms": ms, "clocks": ck, "stage_us": st,
+            ms, ck, st, fl = time_microdag(d, eng, args.steps, args.warmup,
+                                           clocks if "split" in mode else None)
+            res[mode] = {"ms": ms, "clocks": ck, "stage_us": st, "flush_ms": fl,
                          "launches": eng.info()["launches_per_run"]}
         finally:
             eng.close()
@@ -631,7 +652,9 @@ def run_microdag(args, d: Dist):
         "config": {"workload": f"microdag S={S} H={H} I={I}/k T={args.tiles}",
                    "model": "isolated TP-MLP micro-DAG (BASELINE configs[1])", "seq_len": S,
                    "global_batch": 1, "parallelism": f"tp{N}", "graph": True,
-                   "l2": "flushed before every step (512 MiB write outside the timed bracket)"},
+                   "l2": ("flushed before every step: a 512 MiB write; the same loop of writes "
+                          "alone is timed and subtracted (flush_us)"),
+                   "flush_us": round(split["flush_ms"] * 1e3, 2)},
         "roofline": {"stage": "down GEMM + reduction + Add+RMSNorm", "roofline_us": round(roof_s * 1e6, 2),
                      "gemm_us_at_peak": round(gemm_s * 1e6, 2), "nvlink_us": round(comm_s * 1e6, 2),
                      "bound": "tensor" if gemm_s >= comm_s else "nvlink",
@@ -734,7 +757,10 @@ def main():
         return 0
     if d.world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={d.world}")
+    d.nvlink = measure_peer_gbs(d)   # rank 0, before any collective exists
     d.init()
+    if d.world > 1:
+        d.nvlink = pickle_bcast(d, d.nvlink)
     try:
         line = run_microdag(args, d) if args.workload == "microdag" else run_ours(args, d)
         if line is not None:
