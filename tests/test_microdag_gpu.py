@@ -43,6 +43,8 @@ def _check(eng, h_ref, x_ref, label):
     x = eng.final_x()
     eh = float(np.abs(h - h_ref).max())
     ex = float(np.abs(x - x_ref).max())
+    print(f"\n{label}: h max abs err {eh:.3e} (max|h| {np.abs(h_ref).max():.3g}), "
+          f"x max abs err {ex:.3e} (max|x| {np.abs(x_ref).max():.3g})")
     assert eh <= 1e-3 * np.abs(h_ref).max() + 1e-2, f"{label}: h max abs err {eh:.4g}"
     assert ex <= 1e-2 * np.abs(x_ref).max(), f"{label}: x max abs err {ex:.4g}"
 

@@ -81,10 +81,13 @@ def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
             _run_all(engines, lambda e: (e.run(), e.sync()))
         for e in engines:
             assert e.status() == 0, f"rank {e.rank} status {e.status()}"
-        for l in range(cfg.L):
-            err = _maxrel(engines[0].layer_hidden(l), ref["hidden"][l].numpy())
-            assert err <= TOL, f"{mode} layer {l}: {err:.3g}"
+        errs = [_maxrel(engines[0].layer_hidden(l), ref["hidden"][l].numpy()) for l in range(cfg.L)]
         logits = engines[0].last_logits()
+        print(f"\n{mode} ({variant}): per-layer max rel err "
+              f"{' '.join(f'{e:.2e}' for e in errs)}; argmax {int(np.argmax(logits))} "
+              f"oracle {int(np.argmax(ref['logits_last']))}")
+        for l, err in enumerate(errs):
+            assert err <= TOL, f"{mode} layer {l}: {err:.3g}"
         assert int(np.argmax(logits)) == int(np.argmax(ref["logits_last"]))
     finally:
         for e in engines:
