@@ -66,7 +66,7 @@ int krb_gemm_f32out(const void *A, long lda, const void *B, long ldb, float *out
 
 /* act[M, n_out] = silu(A.Bg^T) * (A.Bu^T) where Bgu interleaves gate and up
  * rows in blocks of bn: rows [b*bn, b*bn+bn/2) = gate rows [b*bn/2, (b+1)*bn/2),
- * rows [b*bn+bn/2, (b+1)*bn) = the matching up rows (bn = 128 or 256).
+ * rows [b*bn+bn/2, (b+1)*bn) = the matching up rows (bn = 128, 192 or 256).
  * Replaces the gate/up aclnnMatmul + aclnnSilu + aclnnMul, qwen_main.cpp:1267-1271. */
 int krb_gemm_silu_bf16(const void *A, long lda, const void *Bgu, long ldb, void *act, long ldact,
                        int M, int n_out, int K, int bn, void *stream);

@@ -560,7 +560,8 @@ KRB_EXPORT int krb_gemm_qkv_rope_bf16(const void *A, long lda, const void *B, lo
 KRB_EXPORT int krb_gemm_silu_bf16(const void *A, long lda, const void *Bgu, long ldb, void *act,
                                   long ldact, int M, int n_out, int K, int bn, void *stream) {
   KRB_OP_BEGIN
-  if (bn != 128 && bn != 256) throw std::runtime_error("gemm_silu: bn must be 128 or 256");
+  if (bn != 128 && bn != 192 && bn != 256)
+    throw std::runtime_error("gemm_silu: bn must be 128, 192 or 256");
   krb::gemm_silu_bf16(static_cast<const bf *>(A), lda, static_cast<const bf *>(Bgu), ldb,
                       static_cast<bf *>(act), ldact, M, n_out, K, bn, 0, nullptr, as_stream(stream));
   KRB_OP_END

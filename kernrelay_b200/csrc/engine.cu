@@ -228,7 +228,10 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
       else throw std::runtime_error("KRB_RELAY must be direct or rsag");
     }
     if (relay_direct_ && k > 4) throw std::runtime_error("direct relay supports up to 4 ranks");
-    relay_ready_order_ = 1;  // rsag phases in readiness order (KRB_RELAY_ORDER=pipeline: fixed)
+    // rsag phase order: the fixed pipeline rs(t+1) before ag(t) (measured ~2 % faster at
+    // k = 4 than readiness order: every peer's all-gather waits on the reduce-scatters);
+    // KRB_RELAY_ORDER=ready takes whichever phase is ready, in runs of ready tiles
+    relay_ready_order_ = 0;
     if (const char *e = std::getenv("KRB_RELAY_ORDER")) {
       if (!std::strcmp(e, "ready")) relay_ready_order_ = 1;
       else if (!std::strcmp(e, "pipeline")) relay_ready_order_ = 0;

@@ -122,14 +122,20 @@ int pick_bn_store(int M, int N, int sms) {
 
 int pick_bn_silu(int M, int n_out, int sms) {
   const long mblk = (M + kBM - 1) / kBM;
-  const int cands[2] = {256, 128};
+  const int cands[3] = {256, 192, 128};
+  // relative throughput of one tile (CTA pairs): per 64-deep k-block a pair's SM moves
+  // A 16 KB + its half of B in through TMA and out to the MMA; 256-wide tiles stay within
+  // the SM's shared-memory bandwidth, 192-wide ones exceed it by ~15 %, 128-wide ones by
+  // ~50 % (measured ~0.65 of the 256-wide rate)
+  const double tile_eff[3] = {1.0, 0.87, 0.65};
   int best = 256;
   double best_score = -1;
-  for (int bn : cands) {
+  for (int i = 0; i < 3; ++i) {
+    const int bn = cands[i];
     const int half = bn / 2;
     const long nblk = (n_out + half - 1) / half;
     const double col_util = double(n_out) / double(nblk * half);
-    const double score = wave_eff(mblk * nblk, sms) * col_util * (1.0 + 0.02 * (bn / 32));
+    const double score = wave_eff(mblk * nblk, sms) * col_util * tile_eff[i];
     if (score > best_score + 1e-9) {
       best_score = score;
       best = bn;
@@ -235,6 +241,14 @@ static void dispatch_bn(int bn, const CUtensorMap &ta, const T *B, long ldb, int
       if constexpr (MODE != kEpiSiluMul && MODE != kEpiQkvRope) {
         launch_gemm<224, MODE, F16>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
         break;
+      }
+      [[fallthrough]];
+    case 192:
+      if constexpr (MODE == kEpiSiluMul) {
+        if (bn == 192) {
+          launch_gemm<192, MODE, F16>(ta, B, ldb, M, n_b_rows, K, ea, grid_limit, status, stream);
+          break;
+        }
       }
       [[fallthrough]];
     case 128:
@@ -356,7 +370,8 @@ void gemm_silu(const T *A, long lda, const T *Bgu, long ldb, T *act, long ldact,
   int dev = 0;
   KRB_CUDA(cudaGetDevice(&dev));
   if (bn <= 0) bn = pick_bn_silu(M, n_out, sm_count(dev));
-  if (bn != 256 && bn != 128) throw CudaError("gemm_silu: unsupported bn " + std::to_string(bn));
+  if (bn != 256 && bn != 192 && bn != 128)
+    throw CudaError("gemm_silu: unsupported bn " + std::to_string(bn));
   const int half = bn / 2;
   const int nblk = (n_out + half - 1) / half;
   const int n_b_rows = nblk * bn;

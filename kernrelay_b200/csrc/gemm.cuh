@@ -79,7 +79,7 @@ struct GemmCfg {
   static constexpr uint32_t kWarpEpiBytes = kStage2 ? 32 * kStage2Pitch : 32 * kStageRow * 4;
   static constexpr uint32_t kEpiBytes = kEpiWarps * kWarpEpiBytes;
   // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem slot + abort flag
-  // ... + 16 bytes (tmem slot, abort, flag) + 64 bytes of relay scratch (pair sums)
+  // ... + 16 bytes (tmem slot, abort, flag, relay GEMM-done) + 64 bytes of relay scratch (pair sums)
   static constexpr uint32_t kMaxStages = (kCG == 2 || BN < 224) ? 6 : 4;
   static constexpr uint32_t kBarBytesMax = (2 * 6 + 4) * 8 + 16 + 64;
   // the relay's pair row buffers (up to H = 4096) and their barriers sit behind this layout
@@ -148,7 +148,8 @@ __device__ __forceinline__ void gemm_setup(const GemmSmemView<BN, RELAY> &s, int
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], C::kCG * epi_threads);
     }
-    *s.abort = 0;
+    s.abort[0] = 0;
+    s.abort[2] = 0;  // relay kernel: "this CTA's GEMM is done" (the pipeline buffers are free)
     fence_mbar_init();
   }
   if (warp == 1) {

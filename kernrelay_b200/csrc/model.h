@@ -230,7 +230,7 @@ class Engine {
   void *sym_ = nullptr;
   std::vector<void *> peers_;
   int relay_direct_ = 0;  // 1: direct all-pull relay, 0: reduce-scatter + all-gather
-  int relay_ready_order_ = 1;  // rsag: phases in readiness order (KRB_RELAY_ORDER=pipeline: fixed)
+  int relay_ready_order_ = 0;  // rsag: fixed pipeline order (KRB_RELAY_ORDER=ready: readiness)
   int nseg_ = 0;
   uint64_t flag_timeout_ns_ = 2000000000ull;
   unsigned long long *trace_ = nullptr;  // relay phase trace (KRB_RELAY_TRACE=1)

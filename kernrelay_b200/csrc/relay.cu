@@ -57,6 +57,7 @@ TileSched relay_tile_sched(int S, int H, int T, int bn, int grid,
 
 constexpr int kRelayWarp0 = 6;                      // warps 0..5: GEMM roles
 constexpr int kRelayWarps = 8;                      // consumer warps per CTA
+constexpr int kRelaySlots = 8;                      // staging slots (mbarriers) per warp pair
 constexpr int kSignalWarp = kRelayWarp0 + kRelayWarps;  // warp 14: system-scope signals
 constexpr int kRelayThreads = (kSignalWarp + 1) * 32;
 
@@ -132,6 +133,7 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, V> &s
   int it = 0;
   const TileWalk<C::kCG> w = TileWalk<C::kCG>::make();
   const uint32_t leader_tempty = C::kCG == 2 ? mapa_shared(&s.tempty[0], 0) : 0u;
+  bool clean = true;
   for (int t = w.first; t < ts.total(); t += w.step, ++it) {
     int mb, n0, bn;
     ts.tile(t, mb, n0, bn);
@@ -145,6 +147,7 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, V> &s
     if (!ok) {
       report_status(ra.status, kStatusEpiWait);
       *s.abort = 1;
+      clean = false;
       break;
     }
     tc_fence_after();
@@ -198,6 +201,13 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, V> &s
     }
   }
   if (warp == 2 && lane == 0) {
+    // Every accumulator of this CTA has been drained, so every MMA (and, before it,
+    // every TMA load) that used the pipeline buffers is complete: the relay warps may
+    // stage copies there from now on.
+    if (clean) {
+      __threadfence_block();
+      s.abort[2] = 1;
+    }
     trace_mark(ra, 1);
     if (ra.trace) {
       unsigned long long *tr = ra.trace + size_t(blockIdx.x) * kTraceSlots;
@@ -209,44 +219,56 @@ __device__ __forceinline__ void relay_push_epilogue(const GemmSmemView<BN, V> &s
 }
 
 // ---------------------------------------------------------------- relay warps
-// One thread per CTA polls the k counters of tile t (bounded); the relay warps
-// then meet at named barrier 2 and every thread performs its own acquire load
-// (already satisfied, no spinning) so its later loads are ordered after the
-// peers' releases.  Returns false (all threads) if the wait expired.
-__device__ __forceinline__ bool wait_all_sources(const RelayArgs &ra, size_t cnt_base, int t,
-                                                 uint32_t target, uint32_t code,
-                                                 uint64_t timeout_ns, volatile int *flag_smem) {
-  if (threadIdx.x == kRelayWarp0 * 32) {
-    int ok = 1;
-    for (int src = 0; src < ra.k; ++src) {
-      const uint32_t *p = flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128);
-      if (!wait_counter_geq(p, target, timeout_ns)) {
-        report_status(ra.status, code);
-        ok = 0;
-        break;
-      }
+// The first relay warp polls the k counters of tile t, lane s the counter of source s
+// (bounded, all k round trips in flight at once); the relay warps then meet at named
+// barrier 2, which orders every lane's acquire before the other relay threads' loads.
+// Returns 0 (all threads) if the wait expired, else 1, plus 2 when `gemm_done` (this
+// CTA's GEMM has finished, read once by the poller so every thread sees the same) is set,
+// plus e << 8: once the GEMM is done, tiles t+1 .. e-1 (e <= extend_limit) were found
+// complete too (non-blocking checks), so the caller may take [t, e) as one run.
+__device__ __forceinline__ bool sources_ready(const RelayArgs &ra, size_t cnt_base, int t,
+                                              uint32_t target);
+__device__ __forceinline__ int wait_all_sources(const RelayArgs &ra, size_t cnt_base, int t,
+                                                uint32_t target, uint32_t code,
+                                                uint64_t timeout_ns, volatile int *flag_smem,
+                                                const volatile int *gemm_done = nullptr,
+                                                int extend_limit = 0) {
+  if ((threadIdx.x >> 5) == kRelayWarp0) {
+    const int src = threadIdx.x & 31;
+    bool ok = true;
+    if (src < ra.k)
+      ok = wait_counter_geq(flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128),
+                            target, timeout_ns);
+    ok = __all_sync(0xffffffffu, ok);
+    const bool done = gemm_done && *gemm_done;
+    int e = t + 1;
+    if (ok && done)
+      while (e < extend_limit && sources_ready(ra, cnt_base, e, target)) ++e;
+    if (src == 0) {
+      if (!ok) report_status(ra.status, code);
+      *flag_smem = ok ? 1 | (done ? 2 : 0) | (e << 8) : 0;
     }
-    *flag_smem = ok;
   }
-  // The poller's acquire loads observed every source's release; the CTA barrier
-  // orders them before the other relay threads' loads (cumulativity through the
-  // barrier, the same pattern as a cooperative grid sync).  Payload loads go to
+  // Cumulativity through the barrier (the same pattern as a cooperative grid sync)
+  // makes every source's release visible to all relay threads.  Payload loads go to
   // L2 (ld.global.cg), so no stale L1 line can be hit.
   named_bar_sync(2, kRelayWarps * 32);
-  const bool ok = *flag_smem != 0;
+  const int w = *flag_smem;
   named_bar_sync(2, kRelayWarps * 32);  // flag_smem may be rewritten by the next wait
-  return ok;
+  return w;
 }
 
-// Non-blocking: true when every source's counter of tile t has reached target (one
-// acquire load each; called by a single thread, which then publishes the result).
+// Non-blocking, called by the whole first relay warp: true in every lane when each
+// source's counter of tile t has reached target (lane s loads source s's counter).
 __device__ __forceinline__ bool sources_ready(const RelayArgs &ra, size_t cnt_base, int t,
                                               uint32_t target) {
-  for (int src = 0; src < ra.k; ++src) {
-    const uint32_t *p = flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128);
-    if (static_cast<int32_t>(ld_acquire_sys(p) - target) < 0) return false;
-  }
-  return true;
+  const int src = threadIdx.x & 31;
+  bool r = true;
+  if (src < ra.k)
+    r = static_cast<int32_t>(
+            ld_acquire_sys(flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128)) -
+            target) >= 0;
+  return __all_sync(0xffffffffu, r);
 }
 
 __device__ __forceinline__ float warp_allsum(float v) {
@@ -414,10 +436,14 @@ __device__ __forceinline__ bool pair_addnorm_row_staged(
   return pair_ok;
 }
 
-template <int KR, bool F16>  // ranks (compile-time so the partial registers fit); fp16 data
+// KR: ranks (compile-time so the partial registers fit); F16: fp16 data; BULK: staged bulk
+// copies (each form is its own kernel, so the register-heavy forms do not share one
+// register allocation)
+template <int KR, bool F16, bool BULK>
 __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSched &ts,
-                                               volatile int *flag_smem,
-                                               float *pair_ss, uint8_t *stage_base) {
+                                               volatile int *flag_smem, float *pair_ss,
+                                               uint8_t *stage_base, uint8_t *big_base,
+                                               int big_slots, const volatile int *gemm_done) {
   // reduce-scatter units in flight per warp: KR partial vectors each
   constexpr int kRsBatch = KR <= 2 ? 4 : (KR == 4 ? 2 : 1);
   const int lane = threadIdx.x & 31;
@@ -427,6 +453,13 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
   const int pair = wl >> 1, half = wl & 1;
   const int gp = blockIdx.x * (kRelayWarps / 2) + pair;
   const int GP = gridDim.x * (kRelayWarps / 2);
+  // Exchange pairs (bulk forms): with quiet_signals the CTAs that run signal jobs (the
+  // first T, or 2T for rsag) take no rows, so the system-scope fence of a signal job
+  // does not wait behind its own CTA's NVLink loads; xgp < 0: no exchange rows here.
+  const int nsig0 = (KR > 1 && ra.quiet_signals) ? (ra.direct ? ra.T : 2 * ra.T) : 0;
+  const int nsig = (GP - nsig0 * (kRelayWarps / 2) >= GP / 2) ? nsig0 : 0;
+  const int xgp = gp - nsig * (kRelayWarps / 2);
+  const int XGP = GP - nsig * (kRelayWarps / 2);
   const uint32_t seq = (*ra.epoch - 1u) * uint32_t(ra.L) + uint32_t(ra.layer) + 1u;
   // k > 1: one forwarded signal per (row tile, source) and per (row tile, owner) each run
   const uint32_t rs_target = seq;
@@ -439,25 +472,36 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
   // after any earlier failure (status word set) do not wait again: give up fast
   uint64_t timeout = ra.timeout_ns;
   if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) timeout = 0;
-  // bulk staging (ra.bulk): one H-element bf16 row buffer and one mbarrier per pair;
+  // bulk staging (BULK): one H-element bf16 row buffer and one mbarrier per pair;
   // the pair's leader issues the copies, all 64 threads wait on the mbarrier
   const bool leader = half == 0 && lane == 0;
-  uint8_t *pbuf = ra.bulk ? stage_base + size_t(pair) * ra.H * 2 : nullptr;
-  uint64_t *pbar =
-      ra.bulk ? reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) * ra.H * 2) + pair
-              : nullptr;
-  uint32_t phase = 0;
+  uint8_t *pbuf = BULK ? stage_base + size_t(pair) * ra.H * 2 : nullptr;
+  uint64_t *pbar = BULK ? reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) *
+                                                                          ra.H * 2) +
+                                 pair * kRelaySlots
+                           : nullptr;
   bool stuck = false;  // a copy did not complete in time: no new copies, drain at exit
   auto stage_fail = [&]() {
     if (!stuck) report_status(ra.status, kStatusRsWait);
     stuck = true;
     timeout = 0;
   };
-  auto drain = [&]() {
-    // no bulk copy may still be writing this CTA's shared memory when it exits; if the
-    // copy does not land within another timeout the CTA leaves anyway and says so
-    if (ra.bulk && stuck && leader && !mbar_wait(pbar, phase, ra.timeout_ns))
-      report_status(ra.status, kStatusCopyDrain);
+  // Staging slots (bulk): while this CTA's GEMM runs, one H-element slot per pair (the
+  // reserve behind the GEMM layout); once the GEMM is done here (the epilogue drained the
+  // last accumulator, so no TMA load or MMA touches the pipeline buffers again),
+  // `big_slots` slots per pair in the pipeline buffers, one copy in flight per slot.
+  uint32_t parity = 0;    // bit i: the parity slot i's barrier completes next
+  uint32_t inflight = 0;  // bit i: slot i holds a copy not yet waited for
+  auto slot_ptr = [&](bool big, int i) -> uint8_t * {
+    return big ? big_base + (size_t(pair) * big_slots + i) * ra.H * 2 : pbuf;
+  };
+  auto drain_slots = [&]() {
+    // no bulk copy may still be writing this CTA's shared memory when it exits; a copy
+    // that does not land within another timeout is reported and the CTA leaves anyway
+    for (int i = 0; i < kRelaySlots; ++i)
+      if (((inflight >> i) & 1u) && !mbar_wait(&pbar[i], (parity >> i) & 1u, ra.timeout_ns)) {
+        if (leader) report_status(ra.status, kStatusCopyDrain);
+      }
   };
 
   if constexpr (KR == 1) {
@@ -485,47 +529,75 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
     return;
   }
 
-  if constexpr (KR == 2) {
-    if (ra.direct && ra.bulk) {
-      // direct all-pull with bulk staging: the peer's partial row arrives by one
-      // bulk copy while the pair loads the residual and this rank's partial
+  if constexpr (KR == 2 && BULK) {
+    if (ra.direct) {
+      // direct all-pull with bulk staging, over runs of row tiles found complete
+      // together: each slot receives the peer's partial row by one bulk copy while the
+      // pair loads the residual and this rank's own partial
       const int peer = 1 - ra.rank;
       const __nv_bfloat16 *mine = reinterpret_cast<const __nv_bfloat16 *>(ra.local_base + ra.part_off);
       const uint8_t *theirs = g_peer_base[peer] + ra.part_off;
-      for (int t = 0; t < ra.T; ++t) {
-        const bool ok =
-            wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
-        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
-        if (!ok || stuck) {
+      const int per = (xgp >= 0 && ra.R > xgp) ? (ra.R - xgp + XGP - 1) / XGP : 0;  // rows per tile
+      int t0 = 0;
+      while (t0 < ra.T) {
+        const int w = wait_all_sources(ra, rs_cnt_base, t0, rs_target, kStatusRsWait, timeout,
+                                       flag_smem, gemm_done, ra.T);
+        const int t1 = w ? (w >> 8) : t0 + 1;
+        for (int t = t0; t < t1; ++t)
+          if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
+        if (w == 0) {
+          stuck = true;
           timeout = 0;
-          continue;
         }
-        if (leader) fence_proxy_async_global();
-        for (int q = gp; q < ra.R; q += GP) {
-          const size_t g = size_t(t) * ra.R + q;
-          if (leader) {
-            mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
-            bulk_load(pbuf, theirs + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
+        if (!stuck) {
+          const bool big = (w & 2) && big_slots > 1;
+          const int n = per * (t1 - t0);
+          const int ns = big ? big_slots : 1;
+          auto row_of = [&](int i) -> size_t {
+            const int t = t0 + i / per;
+            return size_t(t) * ra.R + xgp + size_t(i - (t - t0) * per) * XGP;
+          };
+          auto issue = [&](int i) {
+            const int sl = i % ns;
+            inflight |= 1u << sl;
+            if (!leader) return;
+            mbar_arrive_expect_tx(&pbar[sl], uint32_t(ra.H) * 2);
+            bulk_load(slot_ptr(big, sl), theirs + row_of(i) * ra.H * 2, uint32_t(ra.H) * 2,
+                      &pbar[sl]);
+          };
+          if (leader && n > 0) {
+            fence_proxy_async_global();
+            if (big) fence_proxy_async_shared();
           }
-          const bool rok = pair_addnorm_row_staged<true, F16>(
-              ra.resid + g * ra.H, mine + g * ra.H, reinterpret_cast<const uint4 *>(pbuf), pbar,
-              phase, ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv,
-              inv_h, ra.eps, ra.do_norm != 0, pair, half, pair_ss);
-          if (!rok) {
-            stage_fail();
-            break;
+          for (int i = 0; i < n && i < ns; ++i) issue(i);
+          for (int i = 0; i < n; ++i) {
+            const int sl = i % ns;
+            const size_t g = row_of(i);
+            const bool rok = pair_addnorm_row_staged<true, F16>(
+                ra.resid + g * ra.H, mine + g * ra.H,
+                reinterpret_cast<const uint4 *>(slot_ptr(big, sl)), &pbar[sl], (parity >> sl) & 1u,
+                ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h,
+                ra.eps, ra.do_norm != 0, pair, half, pair_ss);
+            if (!rok) {
+              stage_fail();
+              break;
+            }
+            parity ^= 1u << sl;
+            inflight &= ~(1u << sl);
+            if (i + ns < n) issue(i + ns);
           }
-          phase ^= 1;
         }
-        if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+        for (int t = t0; t < t1; ++t)
+          if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
+        t0 = t1;
       }
       if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
-      drain();
+      drain_slots();
       return;
     }
   }
 
-  if constexpr (KR <= 4) {  // direct all-pull is offered up to 4 ranks
+  if constexpr (KR <= 4 && !BULK) {  // direct all-pull is offered up to 4 ranks
     if (ra.direct) {
       // direct all-pull: once every rank released tile t, each pair of warps sums
       // the k partial rows (local + NVLink loads) inside its Add+RMSNorm
@@ -550,36 +622,74 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
     }
   }
 
-  // reduce-scatter step of tile t: wait for every source's partial of my slice,
-  // sum in fp32, round once, push the reduced rows to every rank, release ag_cnt
-  auto rs_phase = [&](int t) -> bool {
-    const bool rs_ok =
-        wait_all_sources(ra, rs_cnt_base, t, rs_target, kStatusRsWait, timeout, flag_smem);
-    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
-    if (rs_ok && ra.bulk && !stuck) {
-      // unit = (owned row i, column segment seg of W = H/k columns): the leader
-      // stages the k sources' segments (k bulk copies, source order) in the pair
-      // buffer; the pair sums them in fp32 in that order and stores the bf16 row
-      __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
+  // ---- rsag: reduce-scatter, then all-gather, over runs of row tiles [t0, t1).
+  // Row tiles that become ready together (the GEMM completes them in the same wave) are
+  // exchanged as ONE phase: one wait and one CTA barrier per phase instead of per tile,
+  // and more copies in flight per pair.
+  // one wait on slot i: every thread of the pair tracks the same parity / inflight bits
+  auto slot_wait = [&](int i) -> bool {
+    const bool ok = mbar_wait(&pbar[i], (parity >> i) & 1u, ra.timeout_ns);
+    if (ok) {
+      parity ^= 1u << i;
+      inflight &= ~(1u << i);
+    }
+    return ok;
+  };
+  __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
+
+  // reduce-scatter of tiles [t0, t1): sum the k sources' partials of the rows this rank
+  // owns in fp32 (source order), round once, store into the local `red` buffer, then
+  // release ag_done[t] for each tile (the signal warp forwards it to every rank)
+  auto rs_phase = [&](int t0, int t1, bool big) {
+    for (int t = t0; t < t1; ++t)
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 3 + 4 * t);
+    if (BULK && !stuck) {
+      // unit = (owned row i, column segment seg of W = H/k columns): the leader stages
+      // the k sources' segments (k bulk copies, source order) in one slot; the pair
+      // sums them in fp32 in that order and stores the row segment
       const int W = ra.H / KR;
       const uint32_t seg_bytes = uint32_t(W) * 2;
       const int wv = W / 8;
       const int tid = half * 32 + lane;
-      const int nunits = ra.Rk * KR;
-      if (leader) fence_proxy_async_global();
-      for (int u = gp; u < nunits; u += GP) {
-        const int i = u / KR, seg = u - i * KR;
-        const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
+      const int upt = ra.Rk * KR;                                  // units per tile
+      const int mine = (xgp >= 0 && upt > xgp) ? (upt - xgp + XGP - 1) / XGP : 0;  // per tile
+      const int n = mine * (t1 - t0);
+      const int ns = big ? big_slots : 1;
+      auto unit_at = [&](int i, size_t &g, int &seg) {
+        const int t = t0 + i / mine;
+        const int u = xgp + (i - (t - t0) * mine) * XGP;
+        const int row = u / KR;
+        seg = u - row * KR;
+        g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + row;
+      };
+      auto issue = [&](int i) {
+        const int sl = i % ns;
+        inflight |= 1u << sl;
+        if (!leader) return;
+        size_t g;
+        int seg;
+        unit_at(i, g, seg);
         const size_t off = (g * ra.H + size_t(seg) * W) * 2;
-        if (leader) {
-          mbar_arrive_expect_tx(pbar, seg_bytes * KR);
+        uint8_t *dst = slot_ptr(big, sl);
+        mbar_arrive_expect_tx(&pbar[sl], seg_bytes * KR);
 #pragma unroll
-          for (int src = 0; src < KR; ++src)
-            bulk_load(pbuf + src * seg_bytes, g_peer_base[src] + ra.part_off + off, seg_bytes, pbar);
-        }
-        const bool uok = mbar_wait(pbar, phase, ra.timeout_ns);
+        for (int src = 0; src < KR; ++src)
+          bulk_load(dst + src * seg_bytes, g_peer_base[src] + ra.part_off + off, seg_bytes,
+                    &pbar[sl]);
+      };
+      if (leader && n > 0) {
+        fence_proxy_async_global();
+        if (big) fence_proxy_async_shared();
+      }
+      for (int i = 0; i < n && i < ns; ++i) issue(i);
+      for (int i = 0; i < n; ++i) {
+        const int sl = i % ns;
+        const bool uok = slot_wait(sl);
         if (uok) {
-          const uint4 *sv = reinterpret_cast<const uint4 *>(pbuf);
+          size_t g;
+          int seg;
+          unit_at(i, g, seg);
+          const uint4 *sv = reinterpret_cast<const uint4 *>(slot_ptr(big, sl));
           for (int v = tid; v < wv; v += 64) {
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -587,151 +697,197 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
             reinterpret_cast<uint4 *>(red + g * ra.H + size_t(seg) * W)[v] = pack8f<F16>(acc);
           }
         }
-        // pair-uniform outcome, and every thread is done reading the buffer
-        const bool all_ok = named_bar_and(3 + pair, 64, uok);
-        if (!all_ok) {
+        // pair-uniform outcome, and every thread is done reading the slot
+        if (!named_bar_and(3 + pair, 64, uok)) {
           stage_fail();
           break;
         }
-        phase ^= 1;
+        if (i + ns < n) issue(i + ns);
       }
-    } else if (rs_ok) {
-      __nv_bfloat16 *red = reinterpret_cast<__nv_bfloat16 *>(ra.local_base + ra.red_off);
-      for (int u0 = gw * kRsBatch; u0 < units; u0 += GW * kRsBatch) {
-        uint4 part[kRsBatch][KR];
+    } else if (!BULK && !stuck) {
+      for (int t = t0; t < t1; ++t)
+        for (int u0 = gw * kRsBatch; u0 < units; u0 += GW * kRsBatch) {
+          uint4 part[kRsBatch][KR];
 #pragma unroll
-        for (int b = 0; b < kRsBatch; ++b) {
-          const int u = u0 + b;
-          const int i = u / ra.nseg;
-          const int col = (u - i * ra.nseg) * 256 + lane * 8;
-          const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
-          if (u < units && col < ra.H) {
-            // pull: every source's partial row g (remote for src != rank)
-#pragma unroll
-            for (int src = 0; src < KR; ++src)
-              part[b][src] = __ldcg(reinterpret_cast<const uint4 *>(
-                  reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[src] + ra.part_off) +
-                  g * ra.H + col));
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kRsBatch; ++b) {
-          const int u = u0 + b;
-          const int i = u / ra.nseg;
-          const int col = (u - i * ra.nseg) * 256 + lane * 8;
-          if (u < units && col < ra.H) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int src = 0; src < KR; ++src) acc8_act<F16>(acc, part[b][src]);
+          for (int b = 0; b < kRsBatch; ++b) {
+            const int u = u0 + b;
+            const int i = u / ra.nseg;
+            const int col = (u - i * ra.nseg) * 256 + lane * 8;
             const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
-            *reinterpret_cast<uint4 *>(red + g * ra.H + col) = pack8f<F16>(acc);
+            if (u < units && col < ra.H) {
+              // pull: every source's partial row g (remote for src != rank)
+#pragma unroll
+              for (int src = 0; src < KR; ++src)
+                part[b][src] = __ldcg(reinterpret_cast<const uint4 *>(
+                    reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[src] + ra.part_off) +
+                    g * ra.H + col));
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < kRsBatch; ++b) {
+            const int u = u0 + b;
+            const int i = u / ra.nseg;
+            const int col = (u - i * ra.nseg) * 256 + lane * 8;
+            if (u < units && col < ra.H) {
+              float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int src = 0; src < KR; ++src) acc8_act<F16>(acc, part[b][src]);
+              const size_t g = size_t(t) * ra.R + size_t(ra.rank) * ra.Rk + i;
+              *reinterpret_cast<uint4 *>(red + g * ra.H + col) = pack8f<F16>(acc);
+            }
           }
         }
+    }
+    // release of my reduced rows: one GPU-scope add per CTA and tile to the local
+    // ag_done[t] by one thread after the CTA barrier (cumulative over the relay
+    // threads' stores); the signal warp forwards each completed tile to every rank
+    named_bar_sync(2, kRelayWarps * 32);
+    for (int t = t0; t < t1; ++t) {
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 4 + 4 * t);
+      if (threadIdx.x == kRelayWarp0 * 32 && !stuck) {
+        red_add_release_gpu(
+            flag_ptr(ra.local_base, ra.flag_off + (2 * size_t(ra.T) * KR + 2 + ra.T + t) * 128), 1u);
+        if (t < 8) trace_mark(ra, 35 + t);
       }
     }
-    // release of my reduced rows: one GPU-scope add per CTA to the local ag_done[t]
-    // by one thread after the CTA barrier (cumulative over the relay threads'
-    // stores); the signal warp forwards the completed tile to every rank
-    named_bar_sync(2, kRelayWarps * 32);
-    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 4 + 4 * t);
-    if (threadIdx.x == kRelayWarp0 * 32 && rs_ok && !stuck) {
-      red_add_release_gpu(
-          flag_ptr(ra.local_base, ra.flag_off + (2 * size_t(ra.T) * KR + 2 + ra.T + t) * 128), 1u);
-      if (t < 8) trace_mark(ra, 35 + t);
-    }
-    if (!rs_ok) timeout = 0;
-    return rs_ok;
   };
 
-  // ---- all-gather step of tile t: wait for every owner's reduced slice, then Add+RMSNorm
-  auto ag_phase = [&](int t, bool rs_ok) {
-    const bool ag_ok =
-        wait_all_sources(ra, ag_cnt_base, t, ag_target, kStatusAgWait, timeout, flag_smem);
-    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 5 + 4 * t);
-    if (!rs_ok || !ag_ok) timeout = 0;
-    if (!ag_ok) return;
-    if (ra.bulk) {
-      if (stuck) return;
-      if (leader) fence_proxy_async_global();
-      for (int q = gp; q < ra.R; q += GP) {
-        const size_t g = size_t(t) * ra.R + q;
-        const int owner = q / ra.Rk;
-        if (leader) {
-          mbar_arrive_expect_tx(pbar, uint32_t(ra.H) * 2);
-          bulk_load(pbuf, g_peer_base[owner] + ra.red_off + g * ra.H * 2, uint32_t(ra.H) * 2, pbar);
-        }
+  // all-gather of tiles [t0, t1): the reduced rows pulled from each row's owner, then
+  // Add+RMSNorm
+  auto ag_phase = [&](int t0, int t1, bool big) {
+    for (int t = t0; t < t1; ++t)
+      if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 5 + 4 * t);
+    if (BULK && !stuck) {
+      const int mine = (xgp >= 0 && ra.R > xgp) ? (ra.R - xgp + XGP - 1) / XGP : 0;  // rows per tile
+      const int n = mine * (t1 - t0);
+      const int ns = big ? big_slots : 1;
+      auto row_at = [&](int i, size_t &g, int &q) {
+        const int t = t0 + i / mine;
+        q = xgp + (i - (t - t0) * mine) * XGP;
+        g = size_t(t) * ra.R + q;
+      };
+      auto issue = [&](int i) {
+        const int sl = i % ns;
+        inflight |= 1u << sl;
+        if (!leader) return;
+        size_t g;
+        int q;
+        row_at(i, g, q);
+        mbar_arrive_expect_tx(&pbar[sl], uint32_t(ra.H) * 2);
+        bulk_load(slot_ptr(big, sl), g_peer_base[q / ra.Rk] + ra.red_off + g * ra.H * 2,
+                  uint32_t(ra.H) * 2, &pbar[sl]);
+      };
+      if (leader && n > 0) {
+        fence_proxy_async_global();
+        if (big) fence_proxy_async_shared();
+      }
+      for (int i = 0; i < n && i < ns; ++i) issue(i);
+      for (int i = 0; i < n; ++i) {
+        const int sl = i % ns;
+        size_t g;
+        int q;
+        row_at(i, g, q);
         const bool rok = pair_addnorm_row_staged<false, F16>(
-            ra.resid + g * ra.H, nullptr, reinterpret_cast<const uint4 *>(pbuf), pbar, phase,
-            ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps,
-            ra.do_norm != 0, pair, half, pair_ss);
+            ra.resid + g * ra.H, nullptr, reinterpret_cast<const uint4 *>(slot_ptr(big, sl)),
+            &pbar[sl], (parity >> sl) & 1u, ra.timeout_ns, ra.sum_out + g * ra.H, ra.gamma,
+            ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair, half, pair_ss);
         if (!rok) {
           stage_fail();
           break;
         }
-        phase ^= 1;
+        parity ^= 1u << sl;
+        inflight &= ~(1u << sl);
+        if (i + ns < n) issue(i + ns);
       }
+    } else if (!BULK && !stuck) {
+      for (int t = t0; t < t1; ++t)
+        for (int q = gp; q < ra.R; q += GP) {
+          const size_t g = size_t(t) * ra.R + q;
+          // reduced row g lives in its owner's `red` buffer (pulled over NVLink)
+          const __nv_bfloat16 *red_row =
+              reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[q / ra.Rk] + ra.red_off) + g * ra.H;
+          pair_addnorm_row<1, F16>(ra.resid + g * ra.H, red_row, 0, 0, ra.sum_out + g * ra.H,
+                                   ra.gamma, ra.x_out + g * ra.H, hv, inv_h, ra.eps,
+                                   ra.do_norm != 0, pair, half, pair_ss);
+        }
+    }
+    for (int t = t0; t < t1; ++t)
       if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
-      return;
-    }
-    for (int q = gp; q < ra.R; q += GP) {
-      const size_t g = size_t(t) * ra.R + q;
-      // reduced row g lives in its owner's `red` buffer (pulled over NVLink)
-      const int owner = q / ra.Rk;
-      const __nv_bfloat16 *red_row =
-          reinterpret_cast<const __nv_bfloat16 *>(g_peer_base[owner] + ra.red_off) + g * ra.H;
-      pair_addnorm_row<1, F16>(ra.resid + g * ra.H, red_row, 0, 0, ra.sum_out + g * ra.H, ra.gamma,
-                          ra.x_out + g * ra.H, hv, inv_h, ra.eps, ra.do_norm != 0, pair, half,
-                          pair_ss);
-    }
-    if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 6 + 4 * t);
   };
 
-  // Phase order over the row tiles (one call site per phase keeps register pressure
-  // down).  Default: the software pipeline rs(0), rs(1), ag(0), rs(2), ag(1), ...: the
-  // reduce-scatter of tile t+1 runs while the all-gather of tile t is still in flight
-  // on the other ranks.  ra.ready_order: once the reduce-scatter is ahead, take
-  // whichever of rs(next_rs) and ag(next_ag) is ready first (reduce-scatter when both
-  // are: the peers' all-gathers wait on it) instead of blocking ag(t) behind the
-  // partials of tile t+1.  An all-gather never runs before its own reduce-scatter.
-  uint32_t rs_failed = 0;  // bit t: the reduce-scatter of tile t failed (T <= 32, host-checked)
+  // Phase order.  ra.ready_order (default): the first relay warp polls both counter sets
+  // and takes whichever is ready -- the reduce-scatter when both are (the peers'
+  // all-gathers wait on it) -- extended over every following tile that is ready too,
+  // and publishes the choice; an all-gather never runs before its own reduce-scatter.
+  // Otherwise the fixed software pipeline rs(0), rs(1), ag(0), rs(2), ag(1), ..., one
+  // tile per phase, each behind a blocking wait.
   int next_rs = 0, next_ag = 0;
   while (next_ag < ra.T) {
-    bool do_rs = next_rs < ra.T;
-    if (do_rs && next_rs > next_ag) {
-      if (!ra.ready_order) {
-        do_rs = next_rs == next_ag + 1;
-      } else {
-        // one thread polls both counter sets and publishes a uniform choice:
-        // 1 reduce-scatter ready, 2 all-gather ready, 3 limit reached (the blocking
-        // all-gather wait then reports it)
-        const uint64_t t0 = globaltimer_ns();
-        int choice = 0;
-        while (choice == 0) {
-          if (threadIdx.x == kRelayWarp0 * 32) {
-            int c = 0;
-            if (sources_ready(ra, rs_cnt_base, next_rs, rs_target)) c = 1;
-            else if (sources_ready(ra, ag_cnt_base, next_ag, ag_target)) c = 2;
-            else if (globaltimer_ns() - t0 > timeout) c = 3;
-            *flag_smem = c;
+    int choice = 0, t1 = 0;
+    bool big = false;
+    if (ra.ready_order) {
+      // every decision below is the poller's, published through shared memory: the
+      // relay threads' own `timeout` / `stuck` may differ by pair after a failure
+      const uint64_t t0 = globaltimer_ns();
+      while (choice == 0) {
+        if ((threadIdx.x >> 5) == kRelayWarp0) {
+          // runs only once the GEMM is done here: before that a pair has one slot and a
+          // run would only delay the first tile's all-gather
+          const bool done = *gemm_done != 0;
+          int c = 0, e = 0;
+          if (next_rs < ra.T && sources_ready(ra, rs_cnt_base, next_rs, rs_target)) {
+            c = 1;
+            e = next_rs + 1;
+            while (done && e < ra.T && sources_ready(ra, rs_cnt_base, e, rs_target)) ++e;
+          } else if (next_ag < next_rs && sources_ready(ra, ag_cnt_base, next_ag, ag_target)) {
+            c = 2;
+            e = next_ag + 1;
+            while (done && e < next_rs && sources_ready(ra, ag_cnt_base, e, ag_target)) ++e;
+          } else if (timeout == 0 || globaltimer_ns() - t0 > timeout) {
+            c = 3;
           }
-          named_bar_sync(2, kRelayWarps * 32);
-          choice = *flag_smem;
-          named_bar_sync(2, kRelayWarps * 32);
-          if (choice == 0) __nanosleep(64);
+          if (lane == 0) flag_smem[0] = c | (e << 8) | (int(done) << 16);
         }
-        do_rs = choice == 1;
+        // the lanes' acquire loads are ordered before every relay thread's later loads
+        named_bar_sync(2, kRelayWarps * 32);
+        const int w = flag_smem[0];
+        named_bar_sync(2, kRelayWarps * 32);
+        choice = w & 0xff;
+        t1 = (w >> 8) & 0xff;
+        big = ((w >> 16) & 1) && big_slots > 1;
+        if (choice == 0) __nanosleep(64);
       }
-    }
-    if (do_rs) {
-      if (!rs_phase(next_rs)) rs_failed |= 1u << next_rs;
-      ++next_rs;
     } else {
-      ag_phase(next_ag, ((rs_failed >> next_ag) & 1u) == 0);
-      ++next_ag;
+      choice = 3;
+    }
+    if (choice == 3) {
+      // fixed order, or a poll that ran out of time: one tile behind a blocking wait
+      // (which reports an expiry).  Fixed order: rs(t+1) goes before ag(t).
+      const bool rs_now = ra.ready_order ? next_rs == next_ag
+                                         : next_rs < ra.T && next_rs <= next_ag + 1;
+      const int t = rs_now ? next_rs : next_ag;
+      const int w = wait_all_sources(ra, rs_now ? rs_cnt_base : ag_cnt_base, t,
+                                     rs_now ? rs_target : ag_target,
+                                     rs_now ? kStatusRsWait : kStatusAgWait, timeout, flag_smem,
+                                     gemm_done);
+      if (w == 0) {
+        stuck = true;
+        timeout = 0;
+      }
+      choice = rs_now ? 1 : 2;
+      t1 = t + 1;
+      big = (w & 2) && big_slots > 1;
+    }
+    if (choice == 1) {
+      rs_phase(next_rs, t1, big);
+      next_rs = t1;
+    } else {
+      ag_phase(next_ag, t1, big);
+      next_ag = t1;
     }
   }
   if (threadIdx.x == kRelayWarp0 * 32) trace_mark(ra, 2);
-  drain();
+  drain_slots();
 }
 
 // ---------------------------------------------------------------- signal warp
@@ -771,7 +927,7 @@ __device__ __forceinline__ void relay_signal(const RelayArgs &ra, const TileSche
   }
 }
 
-template <int BN, int KR, bool F16, int V>
+template <int BN, int KR, bool F16, int V, bool BULK>
 __global__ void __launch_bounds__(kRelayThreads, 1)
     relay_down_kernel(const __grid_constant__ CUtensorMap ta,
                       const __grid_constant__ CUtensorMap tb,
@@ -793,9 +949,9 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
 #pragma unroll
     for (int i = 0; i < kMaxRanks; ++i) g_peer_base[i] = ra.peer_base[i];
     trace_mark(ra, 0);
-    if (ra.bulk) {
+    if (BULK) {
       uint64_t *bars = reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) * ra.H * 2);
-      for (int i = 0; i < kRelayWarps / 2; ++i) mbar_init(&bars[i], 1);
+      for (int i = 0; i < (kRelayWarps / 2) * kRelaySlots; ++i) mbar_init(&bars[i], 1);
     }
   }
   gemm_setup<BN, V>(s, 128);  // its barrier-init fence and __syncthreads cover the above
@@ -806,8 +962,12 @@ __global__ void __launch_bounds__(kRelayThreads, 1)
   } else if (warp < kRelayWarp0) {
     relay_push_epilogue<BN, V, F16>(s, ts, ra);
   } else if (warp < kSignalWarp) {
-    relay_consumer<KR, F16>(ra, ts, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
-                            stage_base);
+    // once this CTA's GEMM is done, its pipeline buffers hold big_slots row slots per pair
+    const int big_slots =
+        min(kRelaySlots, int(C::kTileBytes / (uint32_t(kRelayWarps / 2) * uint32_t(ra.H) * 2u)));
+    relay_consumer<KR, F16, BULK>(ra, ts, reinterpret_cast<volatile int *>(s.abort) + 1, s.scratch,
+                            stage_base, s.tiles, big_slots,
+                            reinterpret_cast<volatile int *>(s.abort) + 2);
   } else if (lane == 0) {
     relay_signal(ra, ts);
   }
@@ -822,7 +982,7 @@ template <int BN, int V>
 static size_t relay_smem_bytes(int H, bool bulk) {
   using C = GemmCfg<BN, V>;
   if (!bulk) return C::kSmemBytes;
-  return C::kSmemBytes + 128 + size_t(kRelayWarps / 2) * H * 2 + (kRelayWarps / 2) * 8;
+  return C::kSmemBytes + 128 + size_t(kRelayWarps / 2) * H * 2 + (kRelayWarps / 2) * kRelaySlots * 8;
 }
 
 // Bulk staging needs the row buffers to fit next to the GEMM pipeline (within the
@@ -848,28 +1008,49 @@ bool relay_uses_pairs(int S, int T, int bn) {
   return on && (bn == 256 || bn == 224) && (S / T) % 256 == 0;
 }
 
-template <int BN, int KR, bool F16, int V>
-static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
-                         const RelayArgs &ra_in, bool want_bulk, int grid, cudaStream_t stream) {
-  using C = GemmCfg<BN, V>;
-  auto kern = relay_down_kernel<BN, KR, F16, V>;
-  int dev = 0;
-  KRB_CUDA(cudaGetDevice(&dev));
-  static size_t dyn_limit[64] = {0};
-  if (!dyn_limit[dev & 63]) {
+// the opt-in dynamic shared memory left beside a relay kernel's static shared memory
+// (set once per kernel and device)
+template <int BN, int KR, bool F16, int V, bool BULK>
+static size_t relay_dyn_limit(int dev) {
+  static size_t lim[64] = {0};
+  if (!lim[dev & 63]) {
+    auto kern = relay_down_kernel<BN, KR, F16, V, BULK>;
     int optin = 0;
     KRB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
     cudaFuncAttributes fa{};
     KRB_CUDA(cudaFuncGetAttributes(&fa, kern));
-    const size_t lim = size_t(optin) - fa.sharedSizeBytes;
-    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(lim)));
-    dyn_limit[dev & 63] = lim;
+    const size_t l = size_t(optin) - fa.sharedSizeBytes;
+    KRB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(l)));
+    lim[dev & 63] = l;
   }
+  return lim[dev & 63];
+}
+
+template <int BN, int KR, bool F16, int V>
+static void launch_relay(const CUtensorMap &tma, const void *w_down, long ldb,
+                         const RelayArgs &ra_in, bool want_bulk, int grid, cudaStream_t stream) {
+  using C = GemmCfg<BN, V>;
+  int dev = 0;
+  KRB_CUDA(cudaGetDevice(&dev));
+  // k = 1 has no exchange; the direct form stages in bulk only at k = 2
+  constexpr bool kBulkForm = KR > 1;
+  static const bool quiet_env = [] {
+    const char *e = std::getenv("KRB_RELAY_QUIET_SIGNALS");
+    return !(e && e[0] == '0');
+  }();
   RelayArgs ra = ra_in;
   ra.cta_group = C::kCG;
-  ra.bulk = (want_bulk && relay_bulk_fits<BN, V>(ra.H, ra.k, dyn_limit[dev & 63])) ? 1 : 0;
+  ra.quiet_signals = quiet_env ? 1 : 0;
+  ra.bulk = (kBulkForm && want_bulk && (!ra.direct || ra.k == 2) &&
+             relay_bulk_fits<BN, V>(ra.H, ra.k, relay_dyn_limit<BN, KR, F16, V, kBulkForm>(dev)))
+                ? 1
+                : 0;
+  auto kern = ra.bulk ? relay_down_kernel<BN, KR, F16, V, kBulkForm>
+                      : relay_down_kernel<BN, KR, F16, V, false>;
+  const size_t lim = ra.bulk ? relay_dyn_limit<BN, KR, F16, V, kBulkForm>(dev)
+                             : relay_dyn_limit<BN, KR, F16, V, false>(dev);
   const size_t smem = relay_smem_bytes<BN, V>(ra.H, ra.bulk != 0);
-  if (smem > dyn_limit[dev & 63]) throw CudaError("relay: shared memory budget exceeded");
+  if (smem > lim) throw CudaError("relay: shared memory budget exceeded");
   const TileSched ts = relay_tile_sched(ra.S, ra.H, ra.T, BN, grid, C::kCG);
   // B boxes: the tile's rows of W_down, split between the pair's CTAs
   const CUtensorMap tmb = make_tmap_2d_bf16(w_down, ra.H, ra.K, ldb, BN / C::kCG, kBK);
@@ -909,7 +1090,8 @@ void relay_down_layer(const T *act, long lda, const T *w_down, long ldb, int bn,
   const CUtensorMap tma = make_tmap_2d_bf16(act, ra.S, ra.K, lda, kBM, kBK);
   const int grid = sm_count(dev);
   if (ra.k > 1 && 2 * ra.T > grid) throw CudaError("relay: more row tiles than signal jobs");
-  // the reduce-scatter failure mask of the consumer holds one bit per row tile
+  // the consumer publishes its choice of a run of row tiles with tile indexes in 8-bit
+  // fields; 32 row tiles stay well inside them
   if (ra.k > 1 && ra.T > 32) throw CudaError("relay: at most 32 row tiles with more than one rank");
   auto by_ranks = [&](auto bn_tag) {
     constexpr int B = decltype(bn_tag)::value;

@@ -111,9 +111,14 @@ struct RelayArgs {
   // 1: the relay warps stage remote rows in shared memory with bulk copies (set
   // by the launcher when the shared-memory budget and the alignment allow it)
   int bulk;
-  // reduce-scatter + all-gather form only: 1 = take whichever phase is ready first
-  // (default), 0 = reduce-scatter of tile t+1 before all-gather of t (KRB_RELAY_ORDER=pipeline)
+  // reduce-scatter + all-gather form only: 0 = reduce-scatter of tile t+1 before the
+  // all-gather of t (default), 1 = take whichever phase is ready first, in runs of ready
+  // tiles once the GEMM is done (KRB_RELAY_ORDER=ready)
   int ready_order;
+  // 1 (default): the CTAs that run signal jobs take no exchange rows, so their
+  // system-scope fences do not wait behind their own NVLink loads (set by the launcher;
+  // KRB_RELAY_QUIET_SIGNALS=0 spreads the rows over every CTA)
+  int quiet_signals;
   const uint32_t *epoch;  // local run counter (bumped once per prefill)
   int layer, L;
   const float *resid;          // h1 [S, H] fp32 residual stream

@@ -7,7 +7,9 @@ exchange and the Add+RMSNorm finished, and the NVLink bytes per second that impl
 Runs a tp{k}_split prefill of a random-init model (all k ranks as threads of this process,
 devices 0..k-1) with KRB_RELAY_TRACE=1, so every relay CTA stamps %globaltimer at its phase
 boundaries (slot meanings in csrc/relay.cuh, kTraceSlots).  The last layer's relay launch is
-reported, times relative to the earliest CTA start on that rank (medians over CTAs):
+reported, times relative to the earliest CTA start on that rank (medians over CTAs, the
+latest CTA in brackets), with the signal jobs that forward each tile's completion to the
+peers (when the local completion counter filled; the system-scope fence and k remote adds):
 
 * direct (each rank pulls every peer's partial rows of tile t): NVLink bytes per rank per
   tile = (k-1) * R * H * 2, over the interval from "partials arrived" to "norm done";
@@ -64,13 +66,28 @@ def summarise(tr, k, T, R, H, kind):
         v = v[v > 0]
         return float(np.median(v - t0) / 1e3) if v.size else None
 
-    out = {"gemm_done_us": med(1), "relay_end_us": med(2), "tiles": []}
+    def mx(c):
+        v = t[:, c]
+        v = v[v > 0]
+        return float((v.max() - t0) / 1e3) if v.size else None
+
+    out = {"t0_ns": int(t0), "gemm_done_us": med(1), "gemm_done_max_us": mx(1),
+           "relay_end_us": med(2), "relay_end_max_us": mx(2), "tiles": [], "signals": []}
+    # signal jobs (CTA j < T forwards the partials of row tile j, T <= j < 2T the reduced
+    # rows of tile j - T): when the local counter completed, and the fence + remote adds
+    for j in range(min(2 * T, t.shape[0])):
+        end, fence = int(t[j, 46]), int(t[j, 47])
+        if end > 0:
+            out["signals"].append({"job": j, "tile": j % T, "kind": "ag" if j >= T else "rs",
+                                   "local_done_us": (end - fence - t0) / 1e3,
+                                   "forwarded_us": (end - t0) / 1e3, "fence_us": fence / 1e3})
     part_bytes = (k - 1) * R * H * 2
     slice_bytes = (k - 1) * (R // max(k, 1)) * H * 2
     for tt in range(min(T, 8)):
         arr, stored, ag, norm = med(3 + 4 * tt), med(4 + 4 * tt), med(5 + 4 * tt), med(6 + 4 * tt)
         row = {"tile": tt, "partials_arrived_us": arr, "reduced_stored_us": stored,
-               "reduced_arrived_us": ag, "norm_done_us": norm}
+               "reduced_arrived_us": ag, "norm_done_us": norm,
+               "max_us": [mx(3 + 4 * tt), mx(4 + 4 * tt), mx(5 + 4 * tt), mx(6 + 4 * tt)]}
         if k > 1 and arr is not None and norm is not None:
             if kind == "direct":
                 row["nvlink_gbs"] = part_bytes / max(norm - arr, 1e-3) / 1e3
@@ -91,6 +108,7 @@ def main():
     ap.add_argument("--tiles", type=int, default=4)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--out")
+    ap.add_argument("--raw", help="also save every CTA's raw trace slots (.npz, one array per rank)")
     args = ap.parse_args()
     traces, status, kind, stages, cfg = run(args.k, args.layers, args.relay, args.config, args.seq,
                                             args.tiles, args.iters)
@@ -111,9 +129,16 @@ def main():
             fmt = lambda v: "   -  " if v is None else f"{v:6.1f}"
             print(f"  tile {row['tile']}: partials {fmt(row['partials_arrived_us'])}  stored "
                   f"{fmt(row['reduced_stored_us'])}  reduced {fmt(row['reduced_arrived_us'])}  norm "
-                  f"{fmt(row['norm_done_us'])}{extra}")
+                  f"{fmt(row['norm_done_us'])}{extra}  (latest CTA: "
+                  + " ".join(fmt(v) for v in row["max_us"]) + ")")
+        for sg in s["signals"]:
+            print(f"  signal {sg['kind']} tile {sg['tile']}: local counter complete "
+                  f"{sg['local_done_us']:6.1f}, forwarded {sg['forwarded_us']:6.1f} "
+                  f"(fence + {args.k} adds {sg['fence_us']:.1f} us)")
     if args.out:
         Path(args.out).write_text(json.dumps(res, indent=1), encoding="utf-8")
+    if args.raw:
+        np.savez_compressed(args.raw, **{f"rank{r}": tr for r, tr in enumerate(traces)})
     if any(status):
         raise SystemExit(f"device status {status}")
 

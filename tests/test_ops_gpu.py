@@ -73,8 +73,11 @@ def test_gemm_bias_and_pitch(cuda, krlib):
 
 
 @pytest.mark.parametrize("M,I,K,bn", [(256, 512, 512, 256), (256, 320, 384, 128),
-                                      (512, 2368, 896, 256)])
+                                      (512, 2368, 896, 256), (512, 2368, 896, 192),
+                                      (384, 1216, 640, 192)])
 def test_gemm_silu(cuda, krlib, M, I, K, bn):
+    """bn 192: the 7B / Qwen3-VL-4B tp8 gate/up widths (2368, 1216 per rank); M = 384 has
+    an odd number of 128-row blocks, so it runs on one-CTA tiles instead of CTA pairs."""
     import torch
     g = torch.Generator().manual_seed(I + K)
     A = _bf(torch.randn(M, K, generator=g)).to(cuda)

@@ -5,9 +5,10 @@ It mirrors kernrelay_b200/csrc/relay.cu: the GEMM epilogues add to the local rs_
 one signal job per (tile, counter) forwards a completed rs_done[t] / ag_done[t] to
 rs_cnt[t][rank] / ag_cnt[t][rank] on every rank; the consumer's phase loop takes
 reduce-scatter(next_rs) or all-gather(next_ag) by the kernel's rule -- the fixed pipeline
-(rs(t+1) before ag(t)) or the readiness order (when the reduce-scatter is ahead, whichever
-of the two is ready, reduce-scatter first) -- and an all-gather never precedes its own
-reduce-scatter.  Each reduce-scatter completion adds to ag_done[t].  Checked for k in
+(rs(t+1) before ag(t), one tile per phase) or the readiness order (whichever of the two is
+ready, reduce-scatter first, each merged with the following tiles that are ready too) --
+and an all-gather never precedes its own reduce-scatter.  Each reduce-scatter completion
+adds to ag_done[t] of every tile it covered.  Checked for k in
 {2, 4, 8}, T in {1, 2, 4, 8}, both orders and several layers (monotone counters with
 per-layer targets): every rank finishes every layer (no deadlock), and a rank's all-gather
 of tile t starts only after every owner finished its reduce-scatter of tile t.
@@ -67,29 +68,35 @@ def simulate(k, T, layers, ready_order, seed):
             start_layer(r, st["layer"])
             return
         nr, na = st["next_rs"], st["next_ag"]
-        do_rs = nr < T
-        if do_rs and nr > na:
-            if not ready_order:
-                do_rs = nr == na + 1
-            else:
-                if ready(r, rs_cnt, nr, target):
-                    do_rs = True
-                elif ready(r, ag_cnt, na, target):
-                    do_rs = False
-                else:
-                    return                     # poll again when a counter changes
-        if do_rs:
-            if not ready(r, rs_cnt, nr, target):
+        if not ready_order:
+            # fixed pipeline: rs(t+1) before ag(t), one tile per phase, blocking waits
+            do_rs = nr < T and nr <= na + 1
+            t0 = nr if do_rs else na
+            if not ready(r, rs_cnt if do_rs else ag_cnt, t0, target):
                 return                         # blocking wait: resumed on a counter change
-            st["busy"] = True
-            push(rng.uniform(0.2, 1.0), "rs_end", (r, nr, l))
+            t1 = t0 + 1
         else:
-            if not ready(r, ag_cnt, na, target):
-                return
-            # invariant: every owner finished its reduce-scatter of tile na in layer l
-            assert rs_finished[l][na] == set(range(k)), (l, na, rs_finished[l][na])
-            st["busy"] = True
-            push(rng.uniform(0.2, 1.0), "ag_end", (r, na, l))
+            # readiness order: the reduce-scatter when ready, else the all-gather (only
+            # behind its own reduce-scatter), each extended over the following tiles that
+            # are ready too (one merged phase)
+            if nr < T and ready(r, rs_cnt, nr, target):
+                do_rs, t0, t1 = True, nr, nr + 1
+                while t1 < T and ready(r, rs_cnt, t1, target):
+                    t1 += 1
+            elif na < nr and ready(r, ag_cnt, na, target):
+                do_rs, t0, t1 = False, na, na + 1
+                while t1 < nr and ready(r, ag_cnt, t1, target):
+                    t1 += 1
+            else:
+                return                         # poll again when a counter changes
+        st["busy"] = True
+        if do_rs:
+            push(rng.uniform(0.2, 1.0) * (t1 - t0), "rs_end", (r, t0, t1, l))
+        else:
+            for t in range(t0, t1):
+                # invariant: every owner finished its reduce-scatter of tile t in layer l
+                assert rs_finished[l][t] == set(range(k)), (l, t, rs_finished[l][t])
+            push(rng.uniform(0.2, 1.0) * (t1 - t0), "ag_end", (r, t0, t1, l))
 
     for r in range(k):
         start_layer(r, 0)
@@ -110,22 +117,23 @@ def simulate(k, T, layers, ready_order, seed):
             for dst in range(k):
                 rs_cnt[dst][t][r] += 1
         elif kind == "rs_end":
-            r, t, l = p
-            rs_finished[l][t].add(r)
+            r, t0, t1, l = p
             state[r]["busy"] = False
-            state[r]["next_rs"] += 1
-            ag_done[r][t] += 1
-            while ag_done[r][t] >= forwarded_ag[r][t] + 1:
-                forwarded_ag[r][t] += 1
-                push(rng.uniform(0.1, 0.5), "fwd_ag", (r, t))
+            state[r]["next_rs"] = t1
+            for t in range(t0, t1):
+                rs_finished[l][t].add(r)
+                ag_done[r][t] += 1
+                while ag_done[r][t] >= forwarded_ag[r][t] + 1:
+                    forwarded_ag[r][t] += 1
+                    push(rng.uniform(0.1, 0.5), "fwd_ag", (r, t))
         elif kind == "fwd_ag":
             r, t = p
             for dst in range(k):
                 ag_cnt[dst][t][r] += 1
         elif kind == "ag_end":
-            r, t, l = p
+            r, t0, t1, l = p
             state[r]["busy"] = False
-            state[r]["next_ag"] += 1
+            state[r]["next_ag"] = t1
         for r in range(k):
             for _ in range(3):
                 before = (state[r]["busy"], state[r]["layer"], state[r]["next_ag"])

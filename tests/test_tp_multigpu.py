@@ -51,11 +51,12 @@ def _run_all(engines, fn):
 
 
 @pytest.mark.parametrize("k", [2, 4, 8])
-@pytest.mark.parametrize("variant", ["direct", "rsag", "rsag_pipeline", "nccl"])
+@pytest.mark.parametrize("variant", ["direct", "rsag", "rsag_ready", "nccl"])
 def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     """variant: the split relay's direct all-pull or reduce-scatter + all-gather
-    form (KRB_RELAY, read at engine creation; rsag runs its phases in readiness order,
-    rsag_pipeline in the fixed order, KRB_RELAY_ORDER=pipeline), or the NCCL tp baseline."""
+    form (KRB_RELAY, read at engine creation; rsag runs its phases in the fixed pipeline
+    order, rsag_ready in readiness order with runs of ready tiles, KRB_RELAY_ORDER=ready),
+    or the NCCL tp baseline."""
     if _ngpu() < k:
         pytest.skip(f"needs {k} GPUs")
     if variant == "direct" and k > 4:
@@ -66,8 +67,8 @@ def test_tp_engines_match_oracle(cuda, krlib, tiny, k, variant, monkeypatch):
     relay = variant.split("_")[0]
     if split:
         monkeypatch.setenv("KRB_RELAY", relay)
-    if variant == "rsag_pipeline":
-        monkeypatch.setenv("KRB_RELAY_ORDER", "pipeline")
+    if variant == "rsag_ready":
+        monkeypatch.setenv("KRB_RELAY_ORDER", "ready")
     engines = [krlib.Engine(d, mode, 512, rank=r, world=k, device=r, tiles=4) for r in range(k)]
     try:
         if split:
@@ -143,3 +144,61 @@ def test_kr_qwen_pp_run_abi(cuda, tiny, mode):
     assert s1["argmax"] == s1["ref_argmax"] == int(np.argmax(ref["logits_last"]))
     assert s1["maxdiff"] <= 2 * TOL * float(np.abs(ref["logits_last"]).max())
     assert s1["flag_timeouts"] == 0 and r["stages"][0]["flag_timeouts"] == 0
+
+
+@pytest.fixture(scope="module")
+def q7b(tmp_path_factory, krlib):
+    """The headline model: Qwen2.5-7B architecture, 28 layers, S=2048,
+    seed 1234 (the bench's model); one fp32 oracle pass streamed layer by layer, kept as the
+    per-layer residual streams and the last-row logits."""
+    if _ngpu() < 2:
+        pytest.skip("needs 2 GPUs")
+    import time
+    cfg = model_gen.CONFIGS["qwen2.5-7b"]
+    d = model_gen.write_model(tmp_path_factory.mktemp("q7b") / "q7b", cfg, 2048, seed=1234,
+                              materialize=False)
+    synth = lambda name, seed, std, n, mean: krlib.synth_normal(name, seed, std, n, mean=mean)  # noqa: E731
+    m = qwen_ref.Model(d, synth=synth)
+    t0 = time.time()
+    hs, x_final = [], None
+    for ev in qwen_ref.prefill_layers(m):
+        if ev[0] == "layer":
+            hs.append(ev[2].numpy())
+        else:
+            x_final = ev[1]
+    logits = qwen_ref.lm_head(m, x_final[-1:])[0].numpy()
+    print(f"\nqwen2.5-7b S=2048 oracle: {time.time() - t0:.0f} s")
+    return d, cfg, hs, logits
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("k", [2, 4, 8])
+def test_qwen25_7b_tp_split_parity(cuda, krlib, q7b, k):
+    """The headline configuration on k GPUs: tp{k}_split (the fused relay, its default form
+    for k) with 4 row tiles, every layer's residual stream on rank 0 against the fp32 oracle
+    (the ranks' partials are rounded to fp16 before the exchange; the oracle sums exact fp32
+    partials).  Bar: per-layer max rel err <= 1e-2 and the same last-row argmax."""
+    if _ngpu() < k:
+        pytest.skip(f"needs {k} GPUs")
+    d, cfg, hs, ref_logits = q7b
+    engines = [krlib.Engine(d, f"tp{k}_split", 2048, rank=r, world=k, device=r, tiles=4)
+               for r in range(k)]
+    try:
+        krlib.Engine.link(engines)
+        engines[0].layer_dump(True)
+        for _ in range(2):
+            _run_all(engines, lambda e: (e.run(), e.sync()))
+        for e in engines:
+            assert e.status() == 0, f"rank {e.rank} status {e.status()}"
+        errs = [_maxrel(engines[0].layer_hidden(l), hs[l]) for l in range(cfg.L)]
+        logits = engines[0].last_logits()
+        top = np.sort(ref_logits.astype(np.float64))[::-1]
+        print(f"\nqwen2.5-7b S=2048 tp{k}_split ({engines[0].info()['relay']}): per-layer max rel "
+              f"err {' '.join(f'{e:.2e}' for e in errs)}; max {max(errs):.3e}; argmax gpu "
+              f"{int(np.argmax(logits))} oracle {int(np.argmax(ref_logits))}; oracle top-2 margin "
+              f"{top[0] - top[1]:.4g}; logits max rel err {_maxrel(logits, ref_logits):.3e}")
+        assert max(errs) <= TOL, errs
+        assert int(np.argmax(logits)) == int(np.argmax(ref_logits))
+    finally:
+        for e in engines:
+            e.close()
