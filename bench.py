@@ -354,7 +354,8 @@ def run_mode(d: Dist, mdir: Path, mode: str, S: int, tiles: int, K: int, W: int,
         eng.close()
 
 
-def roofline_block(cfg, S, k, rank, split_res, pk, nvlink_gbs=NVLINK_FALLBACK_GBS):
+def roofline_block(cfg, S, k, rank, split_res, pk, nvlink_gbs=NVLINK_FALLBACK_GBS,
+                   config_name="qwen2.5-7b"):
     st = split_res["stage_us"]
     work = stage_work(cfg, S, k, rank)
     stages = {}
@@ -401,15 +402,16 @@ def roofline_block(cfg, S, k, rank, split_res, pk, nvlink_gbs=NVLINK_FALLBACK_GB
             roof = {"kernel": name, "bound": "hbm", "achieved": round(per / (launch_us * 1e-6) / 1e9, 1),
                     "peak": pk["hbm_gbs"], "unit": "GB/s"}
     roof["frac"] = round(roof["achieved"] / roof["peak"], 3)
-    roof["traffic"] = traffic_for(name, k)
+    roof["traffic"] = traffic_for(config_name, S, name, k)
     roof["peak_source"] = f"{pk['source']} ({'sustained bf16' if roof['unit'] == 'TFLOP/s' else 'HBM copy'})"
     roof["launch_us"] = round(launch_us, 2)
     return roof, stages
 
 
-def traffic_for(stage: str, k: int):
-    """DRAM bytes (read + write) per launch of `stage` at tp degree k from the committed
-    ncu summary (profiles/traffic.txt, lines `stage@k = bytes`), or None if not captured."""
+def traffic_for(config: str, S: int, stage: str, k: int):
+    """DRAM bytes (read + write) per launch of `stage` at tp degree k for model `config` at
+    sequence length S, from the committed ncu summary (profiles/traffic.txt, lines
+    `config/S/stage@k = bytes`), or None if that case was not captured."""
     p = REPO / "profiles" / "traffic.txt"
     if not p.exists():
         return None
@@ -417,7 +419,7 @@ def traffic_for(stage: str, k: int):
         if line.startswith("#") or not line.strip():
             continue
         name, _, val = line.partition("=")
-        if name.strip() == f"{stage}@{k}":
+        if name.strip() == f"{config}/{S}/{stage}@{k}":
             try:
                 return float(val.split()[0])
             except ValueError:
@@ -463,7 +465,7 @@ def run_ours(args, d: Dist):
     if d.rank != 0:
         return None
     toks = S / (split["ms_per_step"] * 1e-3)
-    roof, stages = roofline_block(cfg, S, N, 0, split, pk, nvlink_gbs)
+    roof, stages = roofline_block(cfg, S, N, 0, split, pk, nvlink_gbs, args.config)
     line = {
         "metric": metric_for(args.config, S),
         "value": round(toks, 1),
@@ -562,7 +564,8 @@ def _microdag_engine(d: Dist, mode: str, S: int, H: int, I: int, tiles: int, see
 def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
     """K steps of [L2 flush (a 512 MiB device write; at k >= 4 a rank's operands fit in the
     126 MB L2), one micro-DAG step (graph replay)] back to back on the engine stream, timed
-    by CUDA events around the whole loop, minus K flushes alone timed the same way.  The
+    by CUDA events around the whole loop, minus K flushes alone timed the same way right
+    after (W warm-up steps in the same pattern first touch the flush buffer).  The
     ranks stay in step without a host barrier per step (every relay step waits for its
     peers), so a per-step flush does not shift the ranks against each other.  Returns the
     per-step time, max over ranks (ms)."""
@@ -572,17 +575,13 @@ def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
     eng.capture()
     stream = torch.cuda.ExternalStream(eng.stream_ptr(), device=d.local)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=f"cuda:{d.local}")
-    for _ in range(W):
-        eng.run()
-    eng.sync()
     e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     with torch.cuda.stream(stream):
-        # flush alone
-        torch.cuda.synchronize()
-        e[0].record(stream)
-        for i in range(K):
+        # warm-up: the flush buffer's first writes and W steps in the timed pattern
+        for i in range(W):
             flush.fill_(i & 0xFF)
-        e[1].record(stream)
+            eng.run()
+        eng.sync()
         torch.cuda.synchronize()
         d.barrier()
         if clocks:
@@ -594,12 +593,23 @@ def time_microdag(d: Dist, eng, K: int, W: int, clocks: Clocks | None):
             flush.fill_(i & 0xFF)
             eng.run()
         e[3].record(stream)
+        eng.sync()
+        torch.cuda.synchronize()
+        d.barrier()
+        # the same K flushes alone, right after (same clocks and memory state)
+        e[0].record(stream)
+        for i in range(K):
+            flush.fill_(i & 0xFF)
+        e[1].record(stream)
     eng.sync()
     torch.cuda.synchronize()
     d.barrier()
     ck = clocks.stop() if clocks else None
     flush_ms = e[0].elapsed_time(e[1]) / K
     step_ms = d.max(e[2].elapsed_time(e[3]) / K - flush_ms)
+    if step_ms <= 0:
+        raise RuntimeError(f"micro-DAG: step time {step_ms:.4f} ms after subtracting the flush "
+                           f"({flush_ms:.4f} ms): timing is not usable")
     st = eng.status()
     if st:
         raise RuntimeError(f"micro-DAG: device status {st}")
