@@ -472,8 +472,8 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
   // after any earlier failure (status word set) do not wait again: give up fast
   uint64_t timeout = ra.timeout_ns;
   if (ra.status && *reinterpret_cast<volatile uint32_t *>(ra.status) != 0) timeout = 0;
-  // bulk staging (BULK): one H-element bf16 row buffer and one mbarrier per pair;
-  // the pair's leader issues the copies, all 64 threads wait on the mbarrier
+  // bulk staging (BULK): one H-element row buffer and kRelaySlots mbarriers per pair (one
+  // per staging slot); the pair's leader issues the copies, all 64 threads wait on them
   const bool leader = half == 0 && lane == 0;
   uint8_t *pbuf = BULK ? stage_base + size_t(pair) * ra.H * 2 : nullptr;
   uint64_t *pbar = BULK ? reinterpret_cast<uint64_t *>(stage_base + size_t(kRelayWarps / 2) *
