@@ -318,6 +318,7 @@ def run_mode(d: Dist, mdir: Path, mode: str, S: int, tiles: int, K: int, W: int,
             raise RuntimeError(f"{mode}: device status {st}")
         info = eng.info()
         res["launches_per_run"] = info["launches_per_run"]
+        res["relay"] = info.get("relay")
         if d.rank == 0:
             logits = eng.last_logits()
             res["argmax"] = int(np.argmax(logits))
@@ -488,6 +489,7 @@ def run_ours(args, d: Dist):
                    "model": MODEL_NAMES.get(args.config, args.config),
                    "global_batch": 1, "seq_len": S, "parallelism": f"tp{N} MLP (attention replicated)",
                    "mode": split["mode"], "tiles": args.tiles, "graph": True,
+                   "relay_form": split.get("relay"),
                    "lm_head_rows": S,
                    "l2": "no flush needed: every step streams all weights (>=15 GB at tp1, >=4.5 GB per GPU at tp8) through the 126 MB L2"},
         "tp_baseline": None if base is None else {
