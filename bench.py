@@ -373,6 +373,10 @@ def roofline_block(cfg, S, k, rank, split_res, pk, nvlink_gbs=NVLINK_FALLBACK_GB
             ach = amount / (us * 1e-6) / 1e9
             stages[name] = {"us": round(us, 1), "achieved": round(ach, 1), "peak": pk["hbm_gbs"],
                             "unit": "GB/s", "frac": round(ach / pk["hbm_gbs"], 3)}
+    if "o" in stages and st.get("addnorm", 0.0) <= 0:
+        # the tp modes run o_proj, the residual add and ln2 as one kernel: its time (and
+        # the fraction, against the GEMM's flops alone) includes the Add+RMSNorm
+        stages["o"]["includes"] = "residual add + ln2 RMSNorm (one kernel)"
     relay_us = st.get("relay", 0.0)
     if relay_us > 0:
         roof_s, gemm_s, comm_s = relay_roofline_s(cfg, S, k, pk, nvlink_gbs)

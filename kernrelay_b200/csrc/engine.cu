@@ -198,6 +198,13 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
   const int half = bn_gu_ / 2;
   gu_rows_ = ((Iloc_ + half - 1) / half) * bn_gu_;
   bn_down_ = pick_bn_store(opts_.seq, c.H, sms);
+  // o_proj + residual + ln2 fused (tp modes, split and NCCL alike, so the two arms keep
+  // the same attention block): 4 row tiles when they are whole CTA-pair blocks, else 1
+  if (mode_.tp && mode_.fused && !opts_.microdag &&
+      !(std::getenv("KRB_FUSE_OPROJ") && std::getenv("KRB_FUSE_OPROJ")[0] == '0')) {
+    o_tiles_ = (opts_.seq % (4 * 256) == 0) ? 4 : 1;
+    if ((opts_.seq / o_tiles_) % 128 == 0) fuse_oproj_ = true;
+  }
   lm_rows_ = opts_.lm_rows > 0 ? std::min(opts_.lm_rows, opts_.seq) : opts_.seq;
   if (const char *e = std::getenv("KRB_LM_ROWS")) {
     const int r = std::atoi(e);
@@ -210,6 +217,11 @@ Engine::Engine(const EngineOpts &o) : opts_(o) {
   } else {
     load_weights();
     alloc_activations();
+  }
+  if (fuse_oproj_) {
+    oflags_layout_ = SymLayout::flags_only(o_tiles_);
+    KRB_CUDA(cudaMalloc(&oflags_, oflags_layout_.bytes));
+    KRB_CUDA(cudaMemset(oflags_, 0, oflags_layout_.bytes));
   }
   if (mode_.split) {
     const int S = opts_.seq, T = opts_.tiles, k = opts_.world;
@@ -256,6 +268,7 @@ Engine::~Engine() {
   if (graph_) cudaGraphExecDestroy(graph_);
   for (void *p : allocs_) cudaFree(p);
   if (sym_) cudaFree(sym_);
+  if (oflags_) cudaFree(oflags_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -502,6 +515,11 @@ void Engine::prologue(StageTimes *st) {
     bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(sym_) + sym_layout_.epoch()), stream_);
     ++launches_;
   }
+  if (fuse_oproj_) {
+    bump_epoch(reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(oflags_) + oflags_layout_.epoch()),
+               stream_);
+    ++launches_;
+  }
   rec.begin(st ? &st->embed : nullptr);
   embed_f32(ids_, embed_, h0_, opts_.seq, c.H, c.V, status_, stream_);
   add_rmsnorm_res_f32(h0_, static_cast<const float *>(nullptr), lw_[0].ln1, x_, nullptr, opts_.seq,
@@ -559,7 +577,39 @@ void Engine::layer(int l, StageTimes *st) {
   attention_tc<__half>(qkv_, vt_, ldvt_, attn_, S, c.HQ, c.HKV, D,
                        float(1.0 / std::sqrt(double(D))), status_, stream_);
   rec.end();
-  if (mode_.fused) {
+  if (fuse_oproj_) {
+    // o_proj, residual add and ln2 in one kernel: the relay kernel at k = 1 (the fp32
+    // o_proj rows land in h1, its relay warps add the residual and normalise each row tile
+    // as soon as its GEMM tiles are done, while the GEMM continues on the next tiles)
+    RelayArgs ra{};
+    ra.S = S;
+    ra.H = H;
+    ra.K = c.HQ * D;
+    ra.T = o_tiles_;
+    ra.k = 1;
+    ra.rank = 0;
+    ra.R = S / o_tiles_;
+    ra.Rk = ra.R;
+    ra.nseg = (H + 255) / 256;
+    ra.peer_base[0] = static_cast<uint8_t *>(oflags_);
+    ra.local_base = static_cast<uint8_t *>(oflags_);
+    ra.flag_off = oflags_layout_.flag_off;
+    ra.epoch = reinterpret_cast<const uint32_t *>(static_cast<uint8_t *>(oflags_) +
+                                                  oflags_layout_.epoch());
+    ra.layer = l;
+    ra.L = c.L;
+    ra.resid = h0_;
+    ra.gamma = w.ln2;
+    ra.sum_out = h1_;
+    ra.x_out = reinterpret_cast<__nv_bfloat16 *>(x_);  // holds fp16 (the relay's T)
+    ra.eps = eps;
+    ra.do_norm = 1;
+    ra.timeout_ns = flag_timeout_ns_;
+    ra.status = status_;
+    rec.begin(st ? &st->o : nullptr);
+    relay_down_layer(attn_, c.HQ * D, w.wo, c.HQ * D, bn_down_, ra, stream_);  // counted above
+    rec.end();
+  } else if (mode_.fused) {
     // o_proj output kept in fp32 (no bf16 rounding of o); residual add fused into the norm
     rec.begin(st ? &st->o : nullptr);
     gemm_f32out(attn_, c.HQ * D, w.wo, c.HQ * D, delta_, H, S, H, c.HQ * D, 0, status_, stream_);

@@ -187,6 +187,13 @@ class Engine {
   Mode mode_;
   int layer_begin_ = 0, layer_end_ = 0;
   bool fuse_rope_ = false;  // QK-norm + RoPE in the QKV GEMM epilogue
+  // tp modes: o_proj, the residual add and ln2 in one relay kernel at k = 1 (its own
+  // counters and run epoch in oflags_, o_tiles_ row tiles); KRB_FUSE_OPROJ=0 keeps the
+  // o_proj GEMM + Add+RMSNorm pair
+  bool fuse_oproj_ = false;
+  int o_tiles_ = 0;
+  SymLayout oflags_layout_{};
+  void *oflags_ = nullptr;
   int Iloc_ = 0, nqkv_ = 0, bn_gu_ = 256, bn_down_ = 256, gu_rows_ = 0;
   int lm_rows_ = 0;
   int launches_ = 0;
