@@ -86,12 +86,12 @@ class Dist:
     def init(self, backend: str | None = None, timeout_s: float | None = None):
         """One process group per job: NCCL on GPUs (the driver's contract); gloo is
         accepted for the CPU tests of the host-side exchange logic.  A collective that a
-        peer never joins fails after timeout_s (KRB_DIST_TIMEOUT_S, default 600 s)."""
+        peer never joins fails after timeout_s (KRB_DIST_TIMEOUT_S, default 300 s)."""
         import torch
         import torch.distributed as dist
         self.backend = backend or os.environ.get("KRB_DIST_BACKEND", "nccl")
         if timeout_s is None:
-            timeout_s = float(os.environ.get("KRB_DIST_TIMEOUT_S", "600"))
+            timeout_s = float(os.environ.get("KRB_DIST_TIMEOUT_S", "300"))
         if self.backend == "nccl":
             torch.cuda.set_device(self.local)
         if self.world > 1:
