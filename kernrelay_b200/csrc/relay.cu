@@ -240,7 +240,10 @@ __device__ __forceinline__ int wait_all_sources(const RelayArgs &ra, size_t cnt_
       ok = wait_counter_geq(flag_ptr(ra.local_base, cnt_base + (size_t(t) * ra.k + src) * 128),
                             target, timeout_ns);
     ok = __all_sync(0xffffffffu, ok);
-    const bool done = gemm_done && *gemm_done;
+    // one read, broadcast from lane 0: the epilogue may set the flag while the lanes read
+    // it, and every lane must take the same branch into sources_ready's __all_sync
+    const bool done =
+        __shfl_sync(0xffffffffu, (gemm_done && *gemm_done) ? 1 : 0, 0) != 0;
     int e = t + 1;
     if (ok && done)
       while (e < extend_limit && sources_ready(ra, cnt_base, e, target)) ++e;
@@ -832,8 +835,9 @@ __device__ __forceinline__ void relay_consumer(const RelayArgs &ra, const TileSc
       while (choice == 0) {
         if ((threadIdx.x >> 5) == kRelayWarp0) {
           // runs only once the GEMM is done here: before that a pair has one slot and a
-          // run would only delay the first tile's all-gather
-          const bool done = *gemm_done != 0;
+          // run would only delay the first tile's all-gather (one read, broadcast from lane
+          // 0, so every lane takes the same branch into sources_ready's __all_sync)
+          const bool done = __shfl_sync(0xffffffffu, *gemm_done != 0 ? 1 : 0, 0) != 0;
           int c = 0, e = 0;
           if (next_rs < ra.T && sources_ready(ra, rs_cnt_base, next_rs, rs_target)) {
             c = 1;
