@@ -6,27 +6,30 @@
 //   red_t = AllReduce_sum(down_t)        (HcclAllReduce on the comm stream)
 //   h0_t, x_t = AddRmsNorm(h1_t, red_t)  (aclnnAddRmsNorm)
 //
-// B200 design: ONE persistent cooperative kernel per layer and rank, 14 warps:
-//   warps 0..5   tcgen05 GEMM (TMA producer, MMA issuer, 4 epilogue warps) over
-//                the output tiles in row-tile order.  The epilogue writes the
-//                bf16 partial tile into this rank's `part` buffer (local,
-//                coalesced) and, after a CTA barrier, one thread fences at system
-//                scope and releases rs_cnt[t][rank] on every rank whose owner
-//                slice the tile touches (the GM-flag publish).
-//   warps 6..13  relay, per row tile t, one of two variants:
+// B200 design: ONE persistent cooperative kernel per layer and rank, 15 warps:
+//   warps 0..5   tcgen05 GEMM (TMA producer, MMA issuer, 4 epilogue warps) over the
+//                output tiles in row-tile order (CTA pairs where the rows allow).  The
+//                epilogue writes the 2-byte partial tile into this rank's `part` buffer
+//                (local, coalesced; k = 1: the fp32 tile straight into sum_out) and,
+//                after a barrier of the epilogue warps, one thread adds 1 to the local
+//                completion counter of its row tile at GPU scope.
+//   warps 6..13  relay, per row tile t (or run of tiles), one of two forms:
 //                direct (default for k <= 2): acquire rs_cnt[t][*] (the bounded
 //                GM-flag wait), then h0 = h1 + sum_src part_src (the k partial rows
 //                pulled from every rank's `part`, local or over NVLink, summed in
 //                fp32), x = RMSNorm(h0) * gamma, two warps per row, the half row
 //                held in registers.  One synchronisation per tile.
-//                rsag (k >= 4, software-pipelined): acquire rs_cnt[t][*]; PULL the
-//                k partial slices of the rows this rank owns, sum in fp32, round
-//                once, store into the local `red` buffer and release
-//                ag_cnt[t][rank] on every rank; acquire ag_cnt[t][*] and apply the
+//                rsag (k >= 4; fixed order rs(t+1) before ag(t) by default): acquire
+//                rs_cnt[t][*]; PULL the k partial slices of the rows this rank owns,
+//                sum in fp32, round once, store into the local `red` buffer and add
+//                to the local ag_done[t]; acquire ag_cnt[t][*] and apply the
 //                Add+RMSNorm with the reduced rows pulled from each row's owner.
 //                NVLink bytes per rank and tile: direct (k-1)/k * k = k-1 tiles,
 //                rsag 2(k-1)/k tiles; equal at k = 2, where direct saves the second
 //                system-scope synchronisation (~17 us per tile measured).
+//   warp 14      signal: one thread per (row tile, counter) and GPU waits for the local
+//                completion counter, fences at system scope and forwards the tile to
+//                rs_cnt / ag_cnt on every rank (the GM-flag publish).
 // Every region is written only by its own rank, so every system-scope fence
 // covers local stores only; all NVLink traffic is loads.  Releases are two-level:
 // GPU-scope adds into local completion counters (~1 us), and one signal thread
