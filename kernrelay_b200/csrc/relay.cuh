@@ -18,8 +18,7 @@ constexpr int kMaxRanks = 8;
 
 // Row ownership of the tp_split relay: global row g of the S rows lies in row
 // tile rt = g / R; within the tile the rows are cut into k contiguous owner
-// slices of Rk = R / k rows.  Used by the device epilogue (which owners a tile's
-// release goes to) and by the host (expected counter increments).
+// slices of Rk = R / k rows.  Used by the host (the relay plan's per-block owners).
 struct RowRoute {
   int tile, owner, local;
 };
@@ -35,8 +34,9 @@ KRB_RELAY_HD RowRoute relay_route(int g, int R, int Rk) {
 // Per-rank symmetric region (one allocation, mapped by every peer).  All writes
 // into a region are made by its own rank; peers only READ it (pull protocol), so
 // every system-scope release covers local stores only.
-//   part   [S][H] bf16   this rank's partial down_proj output (GEMM epilogue)
-//   red    [S][H] bf16   reduced rows (sum over ranks) of the rows this rank owns
+//   part   [S][H] 2-byte this rank's partial down_proj output (GEMM epilogue; fp16 in
+//                        the engine)
+//   red    [S][H] 2-byte reduced rows (sum over ranks) of the rows this rank owns
 //   flags  rs_cnt[T][k]: "source src released tile t" (incremented by the sources),
 //          ag_cnt[T][k]: "owner j released its reduced rows of tile t" (incremented
 //          by the owners), the local run epoch (+1 spare line), then the local
