@@ -50,3 +50,27 @@ def test_reference_arm_other_ranks_exit_quietly():
 def test_our_arm_checks_world_size():
     p = _bench(["--gpus", "2"], {"RANK": "0", "WORLD_SIZE": "1"})
     assert p.returncode != 0 and "WORLD_SIZE=1" in (p.stderr + p.stdout)
+
+
+def test_roofline_block_from_stage_times():
+    """The bench's per-stage rooflines from fabricated stage times (no GPU): the dominant
+    stage's DRAM traffic comes from the committed ncu summary for that model and length
+    only, and a fused o_proj stage (no separate Add+RMSNorm) says what it includes."""
+    sys.path.insert(0, str(REPO))
+    import bench
+    from kernrelay_b200 import model_gen
+    cfg = model_gen.CONFIGS["qwen2.5-7b"]
+    pk = {"tflops_sustained": 1400.0, "hbm_gbs": 6500.0, "source": "test"}
+    st = {"qkv": 2400.0, "attention": 1900.0, "o": 2500.0, "gateup": 12200.0, "addnorm": 0.0,
+          "embed": 30.0, "lm_head": 1700.0, "relay": 8100.0}
+    roof, stages = bench.roofline_block(cfg, 2048, 1, 0, {"stage_us": st}, pk, 770.0,
+                                        "qwen2.5-7b")
+    assert roof["kernel"] == "gateup" and roof["bound"] == "tensor"
+    assert roof["traffic"] == bench.traffic_for("qwen2.5-7b", 2048, "gateup", 1) > 0
+    assert 0.8 < roof["frac"] < 1.0
+    assert "includes" in stages["o"] and "addnorm" not in stages
+    roof8, _ = bench.roofline_block(cfg, 4096, 1, 0, {"stage_us": st}, pk, 770.0, "qwen3-vl-8b")
+    assert roof8["traffic"] is None   # no capture for that model and length
+    st2 = dict(st, addnorm=700.0)
+    _, stages2 = bench.roofline_block(cfg, 2048, 1, 0, {"stage_us": st2}, pk, 770.0)
+    assert "includes" not in stages2["o"] and stages2["addnorm"]["unit"] == "GB/s"
